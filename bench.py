@@ -1,0 +1,398 @@
+"""Benchmark of Depthformer chunk decoding on B200 (the north-star hot path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one 2 s chunk of BASELINE config 2: the benchmark architecture
+("hybrid": d_model 1024, 16 x 64 heads, d_ff 2816, layers 12/20/4, vocab
+16388) in bf16 with random-init N(0, 0.02) weights (seed 0), batch 1 with
+CFG (cond/uncond rows), guidance 4.0, top-k 40, temperature 1.1, Philox
+seed 1 + chunk index: the encoder over 1006 context tokens, 50 temporal steps
+and 16 depth steps + sampling per frame = 800 RVQ tokens.
+
+* value: RVQ tokens/s over K chunks with the inputs resident in HBM
+  (mrtdf_generate_tokens_dev), CUDA events on the engine's stream,
+  max over ranks.
+* e2e: the same metric through the reference-facing host API exactly as
+  System::generate_chunk drives it (system.cpp:177-333): host context ->
+  encoder ids -> mrtdf_generate_tokens (host->device ids, device->host
+  tokens) -> llm_to_rvq -> context roll, streaming K chunks.
+* roofline: the dominant kernel is the decode GEMV phase; its algorithmic
+  bytes per launch / its average launch duration, measured with CUDA events
+  by replaying exactly the chunk's GEMV launches (mrtdf_bench_gemv).
+* cpu_baseline: the CPU oracle (C++ restatement of the reference's eager
+  Depthformer, all host threads) on a bounded sample: the encoder pass and
+  two frames, extrapolated to a 50-frame chunk.
+
+Multi-GPU (torchrun, one process per GPU): independent replicas, one stream
+per GPU with seed offset by rank, no collective on the data path
+(scaling = weak); the barrier and the max-over-ranks reduction use
+torch.distributed.
+
+`--impl reference` times the reference's algorithm on the host cores: the
+reference (MLX) cannot be built here, so this runs the oracle port.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "magenta-realtime-mlx-cpp_b200")
+sys.path.insert(0, PKG)
+
+METRIC = "RVQ tokens/s (2 s chunk = 800 tokens, bf16, batch 1 + CFG)"
+UNIT = "tokens/s"
+TOKENS_PER_CHUNK = 800
+CHUNK_SECONDS = 2.0
+ENC_LEN = 1006
+
+
+def workload_config(n_gpus: int) -> dict:
+    return {
+        "workload": "BASELINE config 2: bf16 Depthformer chunk decode, CFG pair (batch 1), guidance 4.0, "
+                    "top-k 40, T 1.1, 1006-token context, 50 frames x 16 levels",
+        "model": "depthformer-hybrid (d1024 h16x64 ff2816 L12/20/4 V16388)",
+        "global_batch": n_gpus,
+        "seq_len": ENC_LEN,
+        "parallelism": f"replicas x{n_gpus} (no collective)",
+        "l2": "inputs larger than L2: 1.2 GB of weights and 165 MB of cross K/V streamed per chunk",
+    }
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle port of the reference's eager path)
+# ---------------------------------------------------------------------------
+def cpu_sample(frames: int = 2):
+    """Time the oracle on the encoder + `frames` frames of the same workload;
+    returns (tokens/s extrapolated to a 50-frame chunk, ms per chunk, threads)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import mrtdf
+    import oracle_py
+
+    cfg = mrtdf.preset("hybrid", mrtdf.DTYPE_BF16)
+    with tempfile.TemporaryDirectory() as td:
+        path = os.path.join(td, "w.safetensors")
+        mrtdf.write_random_safetensors(cfg, 0, path)
+        orc = oracle_py.Oracle(path, cfg.as_ints())
+    ids = _initial_ids(mrtdf, cfg, 0)
+    t0 = time.perf_counter()
+    orc.encode(ids)
+    t_enc = time.perf_counter() - t0
+    rng = np.random.default_rng(0)
+    t0 = time.perf_counter()
+    x = None
+    for f in range(frames):
+        tout = orc.temporal_step(x, f)
+        d = None
+        for l in range(cfg.rvq_depth):
+            orc.depth_step(d, l)
+            d = tout if l == 0 else d
+        x = rng.standard_normal(tout.shape).astype(np.float32) * 0.1
+    t_frame = (time.perf_counter() - t0) / frames
+    ms_chunk = 1e3 * (t_enc + 50 * t_frame)
+    return TOKENS_PER_CHUNK / (ms_chunk / 1e3), ms_chunk, oracle_py.num_threads(), t_enc, t_frame
+
+
+def _initial_ids(mrtdf, cfg, seed: int) -> np.ndarray:
+    """Chunk-0 encoder ids: empty context (all MASK) + 6 style ids drawn
+    uniformly from the codec range (stand-in for MusicCoCa tokens)."""
+    rng = np.random.default_rng(1000 + seed)
+    ctx = -np.ones((250, cfg.rvq_depth), np.int32)
+    style = rng.integers(cfg.codec_offset, cfg.codec_offset + cfg.rvq_depth * cfg.codebook_size, 6).astype(np.int32)
+    return mrtdf.build_encoder_inputs(ctx, style, 4, cfg.codebook_size, cfg.codec_offset)
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def init_dist(world: int, local: int, backend: str = "nccl"):
+    if world <= 1:
+        return None
+    import torch
+    import torch.distributed as dist
+
+    if backend == "nccl":
+        torch.cuda.set_device(local)
+    dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    return dist
+
+
+def max_over_ranks(dist, value: float, device=None) -> float:
+    if dist is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist, device=None):
+    if dist is not None:
+        if device is not None and device.type == "cuda":
+            dist.barrier(device_ids=[device.index])
+        else:
+            dist.barrier()
+
+
+# ---------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    rank, world, local = dist_env()
+    if rank != 0:
+        return 0
+    W, K = args.warmup, args.steps
+    # one step = one frame of CPU decode; the encoder pass is timed once and
+    # amortised over the chunk
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import mrtdf
+    import oracle_py
+
+    cfg = mrtdf.preset("hybrid", mrtdf.DTYPE_BF16)
+    with tempfile.TemporaryDirectory() as td:
+        path = os.path.join(td, "w.safetensors")
+        mrtdf.write_random_safetensors(cfg, 0, path)
+        orc = oracle_py.Oracle(path, cfg.as_ints())
+    ids = _initial_ids(mrtdf, cfg, 0)
+    t0 = time.perf_counter()
+    orc.encode(ids)
+    t_enc = time.perf_counter() - t0
+    rng = np.random.default_rng(0)
+    times = []
+    x = None
+    for s in range(W + K):
+        f = s % cfg.max_frames
+        if f == 0 and s:
+            orc.encode(ids)
+            x = None
+        t0 = time.perf_counter()
+        tout = orc.temporal_step(x, f)
+        d = None
+        for l in range(cfg.rvq_depth):
+            orc.depth_step(d, l)
+            d = tout
+        if s >= W:
+            times.append(time.perf_counter() - t0)
+        x = rng.standard_normal(tout.shape).astype(np.float32) * 0.1
+    t_frame = float(np.mean(times))
+    ms_chunk = 1e3 * (t_enc + 50 * t_frame)
+    value = TOKENS_PER_CHUNK / (ms_chunk / 1e3)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": ms_chunk, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (random-init weights N(0,0.02) seed 0; chunk-0 context)",
+        "config": workload_config(world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": oracle_py.num_threads(), "kind": "port",
+                         "sample": f"encoder pass once ({t_enc:.2f} s) + {K} timed frames "
+                                   f"({t_frame:.2f} s each), extrapolated to 50 frames; "
+                                   "the reference's MLX build is unavailable here (MLX not installable)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+
+    import mrtdf
+
+    rank, world, local = dist_env()
+    dist = init_dist(world, local)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    cfg = mrtdf.preset("hybrid", mrtdf.DTYPE_BF16)
+    eng = mrtdf.Engine(cfg, device=local).load_random(0)
+    st = mrtdf.Stream(eng, 1, True)
+    ext = torch.cuda.ExternalStream(st.cuda_stream(), device=device)
+    W, K = args.warmup, args.steps
+
+    ids = _initial_ids(mrtdf, cfg, rank)
+    ids_dev = torch.from_numpy(ids).to(device)
+    out_dev = torch.empty((1, 50, cfg.rvq_depth), dtype=torch.int32, device=device)
+
+    def chunk_dev(k):
+        o = mrtdf.gen_opts(cfg, 50, temperature=1.1, top_k=40, guidance_weight=4.0, seed=1 + k + 1000 * rank)
+        st.generate_tokens_dev(ids_dev.data_ptr(), ENC_LEN, o, out_dev.data_ptr())
+
+    for k in range(W):
+        chunk_dev(k)
+    st.sync()
+
+    # ---- value: device-resident inputs --------------------------------------
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier(dist, device)
+    torch.cuda.synchronize(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    for k in range(K):
+        chunk_dev(W + k)
+    e1.record(ext)
+    e1.synchronize()
+    st.sync()
+    torch.cuda.synchronize(device)
+    barrier(dist, device)
+    clk = clocks.stop()
+    ms_dev = e0.elapsed_time(e1) / K
+    ms_dev = max_over_ranks(dist, ms_dev, device)
+
+    # ---- e2e: reference-facing host streaming loop --------------------------
+    ctx = -np.ones((250, cfg.rvq_depth), np.int32)
+    style = ids[0, -6:].copy()
+    o = mrtdf.gen_opts(cfg, 50, seed=1)
+    st.generate_tokens(mrtdf.build_encoder_inputs(ctx, style, 4, cfg.codebook_size, cfg.codec_offset), o)
+    barrier(dist, device)
+    torch.cuda.synchronize(device)
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    e2.record(ext)
+    for k in range(K):
+        enc = mrtdf.build_encoder_inputs(ctx, style, 4, cfg.codebook_size, cfg.codec_offset)
+        o = mrtdf.gen_opts(cfg, 50, seed=1 + k + 1000 * rank)
+        toks = st.generate_tokens(enc, o)[0]
+        rvq = mrtdf.llm_to_rvq(toks, cfg.codebook_size, cfg.codec_offset)
+        ctx = mrtdf.context_roll(ctx, rvq)
+    e3.record(ext)
+    e3.synchronize()
+    ms_e2e = max_over_ranks(dist, e2.elapsed_time(e3) / K, device)
+    h2d = ENC_LEN * 2 * 4 + 8
+    d2h = TOKENS_PER_CHUNK * 4 + 4
+
+    # ---- roofline of the dominant kernel (decode GEMV phases) ---------------
+    o = mrtdf.gen_opts(cfg, 50, seed=1)
+    g_ms, g_launches, g_bytes = st.bench_gemv(o, 3)
+    per_launch_s = g_ms / 1e3 / g_launches
+    achieved = g_bytes / g_launches / per_launch_s / 1e9
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    peak = peaks.get("hbm_gbs", 6650.0)
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+
+    value = TOKENS_PER_CHUNK * world / (ms_dev / 1e3)
+    e2e_value = TOKENS_PER_CHUNK * world / (ms_e2e / 1e3)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms_dev, "rtf": CHUNK_SECONDS * 1e3 / ms_dev, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights N(0,0.02) seed 0, RMSNorm scales 1; chunk-0 context + random style)",
+        "config": workload_config(world),
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_chunk": ms_e2e, "rtf": CHUNK_SECONDS * 1e3 / ms_e2e},
+        "gpu_launches": None,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "kernel": "gemv_phase_kernel (decode GEMV phases)",
+                     "peak_source": peak_src, "launches_per_chunk": g_launches,
+                     "bytes_per_launch": g_bytes / g_launches, "us_per_launch": per_launch_s * 1e6,
+                     "gemv_ms_per_chunk": g_ms},
+        "clocks": clk,
+    }
+    launches = st_launch_count(cfg)
+    line["gpu_launches"] = launches * K
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tps, ms_cpu, cores, t_enc, t_frame = cpu_sample(2)
+        line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port",
+                                "sample": f"encoder pass ({t_enc:.2f} s) + 2 frames ({t_frame:.2f} s each) "
+                                          "of the same bf16 workload, extrapolated to a 50-frame chunk"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    st.close()
+    eng.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+def st_launch_count(cfg) -> int:
+    """Kernels of one chunk graph (our own): encoder + PAD embedding +
+    50 x (temporal layers + 16 x (depth layers + lm_head + sampler))."""
+    enc = 1 + cfg.num_encoder_layers * 7 + 2
+    temporal = cfg.num_temporal_layers * 8
+    depth = cfg.num_depth_layers * 5 + 1 + 1
+    return enc + 1 + 50 * (temporal + cfg.rvq_depth * depth)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,726 @@
+// Decode-step kernels for sm_100a: the GEMV phase kernel behind every
+// projection of temporal_step / depth_step, single-query attention (self
+// with relative-position bias, split-K cross attention), and the fused
+// CFG + vocab-mask + temperature + top-k + Gumbel-max sampler.
+//
+// Reference semantics (rhymeswithlion/magenta-realtime-mlx-cpp):
+//   RMSNorm            depthformer/modules.cpp:72-84 (eps 1e-6, 342-346)
+//   Linear             modules.cpp:98-100 (bias-free, W stored (out, in))
+//   MHA (scale 1.0)    modules.cpp:243-321 (SDPA with additive bias)
+//   KV append          modules.cpp:271-275, 428-429
+//   Gated FFN          modules.cpp:222-226 + gelu_approx nn_ops.h:66-84
+//   DecoderLayer       modules.cpp:384-408
+//   sampling           decode.cpp:71-148, 465-477, 484
+// In bf16 mode every op output is rounded to bf16 as MLX does; reductions
+// accumulate in fp32.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "decode_kernels.cuh"
+
+namespace mrtdf {
+
+// ---------------------------------------------------------------------------
+// GEMV phase kernel
+//
+// One CTA per SM. CTA c owns the contiguous unit range
+// [c * units / G, (c + 1) * units / G) of the weight matrix; its rows are one
+// contiguous byte range in HBM, streamed into shared memory by the TMA
+// engine (cp.async.bulk) through a ring of kGemvStages buffers. The first
+// stages are issued BEFORE griddepcontrol.wait, so under programmatic
+// dependent launch the weight fetch overlaps the previous kernel. The input
+// vector (B rows, optionally RMS-normalised) is read after the wait and kept
+// in shared memory as float. Each warp reduces whole rows with 16-byte
+// shared loads and a shuffle reduction; the epilogue is fused.
+// ---------------------------------------------------------------------------
+template <typename T, int BMAX, bool NORM, int MODE>
+__global__ void __launch_bounds__(kGemvThreads) gemv_phase_kernel(const GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int RPU = (MODE == kGemvGeglu) ? 2 : 1;
+  constexpr int EPC = Vec16<T>::N;
+  uint8_t* stage_buf = smem;
+  float* xs = reinterpret_cast<float*>(smem + kGemvStages * kGemvStageBytes);
+  uint64_t* bars =
+      reinterpret_cast<uint64_t*>(smem + kGemvStages * kGemvStageBytes + (((size_t)p.B * p.cols * 4 + 15) & ~15));
+  __shared__ float red[kGemvThreads / 32][BMAX];
+  __shared__ float rstd[BMAX];
+  __shared__ int ok_flag;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = gridDim.x, c = blockIdx.x;
+  const int u0 = (int)(((long long)c * p.units) / G);
+  const int u1 = (int)(((long long)(c + 1) * p.units) / G);
+  const int nunits = u1 - u0;
+  const int unit_bytes = RPU * p.cols * (int)sizeof(T);
+  const int ups = kGemvStageBytes / unit_bytes;  // host guarantees >= 1
+  const int nstages = (nunits + ups - 1) / ups;
+  const uint8_t* wbase = reinterpret_cast<const uint8_t*>(p.W) + (size_t)u0 * unit_bytes;
+
+  auto issue = [&](int s) {
+    const int first = s * ups;
+    const int n = min(ups, nunits - first);
+    const uint32_t bytes = (uint32_t)(n * unit_bytes);
+    uint64_t* bar = &bars[s % kGemvStages];
+    mbar_arrive_expect_tx(bar, bytes);
+    bulk_g2s(stage_buf + (size_t)(s % kGemvStages) * kGemvStageBytes, wbase + (size_t)first * unit_bytes, bytes, bar);
+  };
+
+  if (tid == 0) {
+    for (int i = 0; i < kGemvStages; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+    ok_flag = 1;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int s = 0; s < min(kGemvStages, nstages); ++s) issue(s);
+  }
+  pdl_launch_dependents();
+  pdl_wait();
+
+  // ---- input vector -> shared memory (optionally RMS-normalised) ----------
+  const T* x = reinterpret_cast<const T*>(p.x);
+  float ss[BMAX];
+#pragma unroll
+  for (int b = 0; b < BMAX; ++b) ss[b] = 0.f;
+#pragma unroll
+  for (int b = 0; b < BMAX; ++b) {
+    if (b < p.B) {
+      for (int i = tid; i < p.cols; i += kGemvThreads) {
+        const float v = to_f(x[(size_t)b * p.x_stride + i]);
+        xs[(size_t)b * p.cols + i] = v;
+        if (NORM) ss[b] += v * v;
+      }
+    }
+  }
+  if (NORM) {
+#pragma unroll
+    for (int b = 0; b < BMAX; ++b) {
+      const float v = warp_sum(ss[b]);
+      if (lane == 0) red[warp][b] = v;
+    }
+    __syncthreads();
+    if (tid < BMAX) {
+      float t = 0.f;
+      for (int w = 0; w < kGemvThreads / 32; ++w) t += red[w][tid];
+      rstd[tid] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)p.cols), 1e-6f)));
+    }
+    __syncthreads();
+    const T* nw = reinterpret_cast<const T*>(p.norm_w);
+#pragma unroll
+    for (int b = 0; b < BMAX; ++b) {
+      if (b < p.B) {
+        const float r = rstd[b];
+        for (int i = tid; i < p.cols; i += kGemvThreads) {
+          const float v = xs[(size_t)b * p.cols + i];
+          xs[(size_t)b * p.cols + i] = rnd<T>(__fmul_rn(to_f(nw[i]), rnd<T>(__fmul_rn(v, r))));
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  const int nchunk = p.cols / EPC;
+  for (int s = 0; s < nstages; ++s) {
+    if (tid == 0) ok_flag = mbar_wait_bounded(&bars[s % kGemvStages], (uint32_t)((s / kGemvStages) & 1), p.err);
+    __syncthreads();
+    if (!ok_flag) break;
+    const uint8_t* buf = stage_buf + (size_t)(s % kGemvStages) * kGemvStageBytes;
+    const int first = s * ups;
+    const int n_u = min(ups, nunits - first);
+    for (int uu = warp; uu < n_u; uu += kGemvThreads / 32) {
+      float acc[RPU][BMAX];
+#pragma unroll
+      for (int r = 0; r < RPU; ++r)
+#pragma unroll
+        for (int b = 0; b < BMAX; ++b) acc[r][b] = 0.f;
+      const uint8_t* urow = buf + (size_t)uu * unit_bytes;
+      for (int ch = lane; ch < nchunk; ch += 32) {
+        float wv[RPU][EPC];
+#pragma unroll
+        for (int r = 0; r < RPU; ++r) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(urow + (size_t)r * p.cols * sizeof(T) + (size_t)ch * 16);
+          Vec16<T>::unpack(raw, wv[r]);
+        }
+#pragma unroll
+        for (int b = 0; b < BMAX; ++b) {
+          if (b < p.B) {
+            const float* xv = xs + (size_t)b * p.cols + (size_t)ch * EPC;
+            float xr[EPC];
+#pragma unroll
+            for (int e = 0; e < EPC; e += 4) {
+              const float4 f4 = *reinterpret_cast<const float4*>(xv + e);
+              xr[e] = f4.x;
+              xr[e + 1] = f4.y;
+              xr[e + 2] = f4.z;
+              xr[e + 3] = f4.w;
+            }
+#pragma unroll
+            for (int r = 0; r < RPU; ++r)
+#pragma unroll
+              for (int e = 0; e < EPC; ++e) acc[r][b] = fmaf(wv[r][e], xr[e], acc[r][b]);
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < RPU; ++r)
+#pragma unroll
+        for (int b = 0; b < BMAX; ++b) acc[r][b] = warp_sum(acc[r][b]);
+
+      const int u = u0 + first + uu;
+#pragma unroll
+      for (int b = 0; b < BMAX; ++b) {
+        if (b < p.B && lane == b) {
+          if (MODE == kGemvStore) {
+            reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + p.out_offset + u] = from_f<T>(acc[0][b]);
+          } else if (MODE == kGemvLogits) {
+            reinterpret_cast<float*>(p.out)[(size_t)b * p.out_stride + p.out_offset + u] = rnd<T>(acc[0][b]);
+          } else if (MODE == kGemvResid) {
+            const float rv = to_f(reinterpret_cast<const T*>(p.resid)[(size_t)b * p.resid_stride + u]);
+            reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + u] = from_f<T>(__fadd_rn(rv, rnd<T>(acc[0][b])));
+          } else if (MODE == kGemvGeglu) {
+            const float a = rnd<T>(acc[0][b]);
+            const float g = rnd<T>(acc[1][b]);
+            reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + u] = from_f<T>(__fmul_rn(gelu_approx<T>(a), g));
+          } else {  // kGemvQKV
+            const int sect = u / p.inner, rr = u - sect * p.inner;
+            if (sect == 0) {
+              reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + rr] = from_f<T>(acc[0][b]);
+            } else {
+              const int h = rr >> 6, cc = rr & 63;
+              T* cache = reinterpret_cast<T*>(sect == 1 ? p.kc : p.vc);
+              cache[(((size_t)b * p.H + h) * p.cap + p.pos) * 64 + cc] = from_f<T>(acc[0][b]);
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();  // every warp is done with this buffer
+    if (tid == 0 && s + kGemvStages < nstages) issue(s + kGemvStages);
+  }
+  if (!ok_flag && tid == 0) {
+    // Give in-flight copies a bounded chance to land before the CTA exits.
+    for (int s = 0; s < nstages; ++s) mbar_wait_bounded(&bars[s % kGemvStages], (uint32_t)((s / kGemvStages) & 1), nullptr);
+  }
+}
+
+size_t gemv_smem_bytes(int B, int cols) {
+  return (size_t)kGemvStages * kGemvStageBytes + (((size_t)B * cols * 4 + 15) & ~(size_t)15) + kGemvStages * 8;
+}
+
+template <typename T, int BMAX, bool NORM, int MODE>
+static cudaError_t launch_gemv_t(const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = gemv_smem_bytes(p.B, p.cols);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemv_phase_kernel<T, BMAX, NORM, MODE>, p);
+}
+
+template <typename T, int BMAX>
+static cudaError_t dispatch_mode(int mode, bool norm, const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
+  switch (mode) {
+    case kGemvStore:
+      return norm ? launch_gemv_t<T, BMAX, true, kGemvStore>(p, grid, s, pdl)
+                  : launch_gemv_t<T, BMAX, false, kGemvStore>(p, grid, s, pdl);
+    case kGemvResid:
+      return norm ? launch_gemv_t<T, BMAX, true, kGemvResid>(p, grid, s, pdl)
+                  : launch_gemv_t<T, BMAX, false, kGemvResid>(p, grid, s, pdl);
+    case kGemvQKV:
+      return launch_gemv_t<T, BMAX, true, kGemvQKV>(p, grid, s, pdl);
+    case kGemvGeglu:
+      return launch_gemv_t<T, BMAX, true, kGemvGeglu>(p, grid, s, pdl);
+    case kGemvLogits:
+      return launch_gemv_t<T, BMAX, true, kGemvLogits>(p, grid, s, pdl);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <typename T>
+static cudaError_t dispatch_b(int mode, bool norm, const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
+  if (p.B <= 1) return dispatch_mode<T, 1>(mode, norm, p, grid, s, pdl);
+  if (p.B <= 2) return dispatch_mode<T, 2>(mode, norm, p, grid, s, pdl);
+  if (p.B <= 4) return dispatch_mode<T, 4>(mode, norm, p, grid, s, pdl);
+  if (p.B <= 8) return dispatch_mode<T, 8>(mode, norm, p, grid, s, pdl);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemv(int dtype, int mode, bool norm, const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
+  const int ebytes = dtype == 1 ? 2 : 4;
+  const int rpu = mode == kGemvGeglu ? 2 : 1;
+  if (p.cols % (16 / ebytes) != 0 || rpu * p.cols * ebytes > kGemvStageBytes) return cudaErrorInvalidValue;
+  if (grid <= 0) return cudaSuccess;
+  return dtype == 1 ? dispatch_b<__nv_bfloat16>(mode, norm, p, grid, s, pdl) : dispatch_b<float>(mode, norm, p, grid, s, pdl);
+}
+
+template <typename T, int BMAX>
+static cudaError_t set_limits_b() {
+  const int mx = (int)gemv_smem_bytes(BMAX, 4096);
+  cudaError_t e = cudaSuccess;
+  auto set = [&](const void* f) {
+    cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    if (r != cudaSuccess) e = r;
+  };
+  set((const void*)gemv_phase_kernel<T, BMAX, true, kGemvStore>);
+  set((const void*)gemv_phase_kernel<T, BMAX, false, kGemvStore>);
+  set((const void*)gemv_phase_kernel<T, BMAX, true, kGemvResid>);
+  set((const void*)gemv_phase_kernel<T, BMAX, false, kGemvResid>);
+  set((const void*)gemv_phase_kernel<T, BMAX, true, kGemvQKV>);
+  set((const void*)gemv_phase_kernel<T, BMAX, true, kGemvGeglu>);
+  set((const void*)gemv_phase_kernel<T, BMAX, true, kGemvLogits>);
+  return e;
+}
+
+template <typename T>
+static cudaError_t set_limits_t() {
+  cudaError_t e;
+  if ((e = set_limits_b<T, 1>()) != cudaSuccess) return e;
+  if ((e = set_limits_b<T, 2>()) != cudaSuccess) return e;
+  if ((e = set_limits_b<T, 4>()) != cudaSuccess) return e;
+  return set_limits_b<T, 8>();
+}
+
+cudaError_t gemv_set_smem_limits() {
+  cudaError_t e = set_limits_t<__nv_bfloat16>();
+  if (e != cudaSuccess) return e;
+  return set_limits_t<float>();
+}
+
+// ---------------------------------------------------------------------------
+// Self-attention for one new query (decode), one warp per (row, head):
+// lane j scores key j of each 32-key chunk, online softmax over chunks,
+// lane l accumulates output dims 2l, 2l+1. Scale 1.0, additive bias
+// (relative-position bias of this query position, already in the compute
+// dtype's values).
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(128) attn_self_kernel(const AttnParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ float qs[4][64];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gw = blockIdx.x * 4 + warp;
+  if (gw >= p.B * p.H) return;
+  const int b = gw / p.H, h = gw - b * p.H;
+  const T* q = reinterpret_cast<const T*>(p.q) + (size_t)b * p.inner + h * 64;
+  qs[warp][2 * lane] = to_f(q[2 * lane]);
+  qs[warp][2 * lane + 1] = to_f(q[2 * lane + 1]);
+  __syncwarp();
+  const size_t base = ((size_t)b * p.H + h) * p.cap * 64;
+  const T* K = reinterpret_cast<const T*>(p.K) + base;
+  const T* V = reinterpret_cast<const T*>(p.V) + base;
+  const float* bias = p.bias ? p.bias + (size_t)h * p.bias_stride : nullptr;
+  float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
+  for (int j0 = 0; j0 < p.T; j0 += 32) {
+    const int j = j0 + lane;
+    float sc = -INFINITY;
+    if (j < p.T) {
+      const T* kr = K + (size_t)j * 64;
+      float acc = 0.f;
+#pragma unroll 16
+      for (int cc = 0; cc < 64; ++cc) acc = fmaf(qs[warp][cc], to_f(kr[cc]), acc);
+      if (bias) acc += bias[j];
+      sc = acc;
+    }
+    const float cm = warp_max(sc);
+    const float nm = fmaxf(m, cm);
+    const float scale = (m == -INFINITY) ? 0.f : expf(m - nm);
+    const float pj = (j < p.T) ? expf(sc - nm) : 0.f;
+    l = l * scale + warp_sum(pj);
+    o0 *= scale;
+    o1 *= scale;
+    const int nj = min(32, p.T - j0);
+    for (int jj = 0; jj < nj; ++jj) {
+      const float pw = __shfl_sync(0xffffffffu, pj, jj);
+      const T* vr = V + (size_t)(j0 + jj) * 64;
+      o0 = fmaf(pw, to_f(vr[2 * lane]), o0);
+      o1 = fmaf(pw, to_f(vr[2 * lane + 1]), o1);
+    }
+    m = nm;
+  }
+  T* out = reinterpret_cast<T*>(p.out) + (size_t)b * p.inner + h * 64;
+  out[2 * lane] = from_f<T>(o0 / l);
+  out[2 * lane + 1] = from_f<T>(o1 / l);
+}
+
+// ---------------------------------------------------------------------------
+// Cross-attention for one new query over the cached encoder K/V: grid
+// (B*H, nsplit), 4 warps per CTA. Each CTA reduces its key slice to a
+// partial (max, sum, o[64]) in global scratch; the last CTA of a (row, head)
+// to arrive (atomic ticket) combines all slices and resets the ticket.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(128) attn_cross_kernel(const AttnParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ float qs[64];
+  __shared__ float wm[4], wl[4], wo[4][64];
+  __shared__ int is_last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int bh = blockIdx.x, sp = blockIdx.y;
+  const int b = bh / p.H, h = bh - b * p.H;
+  if (threadIdx.x < 64) qs[threadIdx.x] = to_f(reinterpret_cast<const T*>(p.q)[(size_t)b * p.inner + h * 64 + threadIdx.x]);
+  __syncthreads();
+  const size_t base = ((size_t)b * p.H + h) * p.cap * 64;
+  const T* K = reinterpret_cast<const T*>(p.K) + base;
+  const T* V = reinterpret_cast<const T*>(p.V) + base;
+  const int k0 = (int)(((long long)sp * p.T) / p.nsplit), k1 = (int)(((long long)(sp + 1) * p.T) / p.nsplit);
+  float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
+  for (int j0 = k0 + warp * 32; j0 < k1; j0 += 128) {
+    const int j = j0 + lane;
+    float sc = -INFINITY;
+    if (j < k1) {
+      const uint4* kr = reinterpret_cast<const uint4*>(K + (size_t)j * 64);
+      float acc = 0.f;
+      constexpr int EPC = Vec16<T>::N;
+#pragma unroll
+      for (int ch = 0; ch < 64 / EPC; ++ch) {
+        float kv[EPC];
+        Vec16<T>::unpack(kr[ch], kv);
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) acc = fmaf(qs[ch * EPC + e], kv[e], acc);
+      }
+      sc = acc;
+    }
+    const float cm = warp_max(sc);
+    const float nm = fmaxf(m, cm);
+    const float scale = (m == -INFINITY) ? 0.f : expf(m - nm);
+    const float pj = (j < k1) ? expf(sc - nm) : 0.f;
+    l = l * scale + warp_sum(pj);
+    o0 *= scale;
+    o1 *= scale;
+    const int nj = min(32, k1 - j0);
+    for (int jj = 0; jj < nj; ++jj) {
+      const float pw = __shfl_sync(0xffffffffu, pj, jj);
+      const T* vr = V + (size_t)(j0 + jj) * 64;
+      o0 = fmaf(pw, to_f(vr[2 * lane]), o0);
+      o1 = fmaf(pw, to_f(vr[2 * lane + 1]), o1);
+    }
+    m = nm;
+  }
+  if (lane == 0) {
+    wm[warp] = m;
+    wl[warp] = l;
+  }
+  wo[warp][2 * lane] = o0;
+  wo[warp][2 * lane + 1] = o1;
+  __syncthreads();
+  float* part = p.part + ((size_t)bh * p.nsplit + sp) * 66;
+  if (threadIdx.x < 64) {
+    float M = -INFINITY;
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w]);
+    float L = 0.f, O = 0.f;
+    for (int w = 0; w < 4; ++w) {
+      if (wm[w] == -INFINITY) continue;
+      const float f = expf(wm[w] - M);
+      L += wl[w] * f;
+      O += wo[w][threadIdx.x] * f;
+    }
+    part[2 + threadIdx.x] = O;
+    if (threadIdx.x == 0) {
+      part[0] = M;
+      part[1] = L;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = (atomicAdd(&p.counters[bh], 1) == p.nsplit - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  if (threadIdx.x < 64) {
+    const float* pb = p.part + (size_t)bh * p.nsplit * 66;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < p.nsplit; ++s2) M = fmaxf(M, __ldcg(pb + (size_t)s2 * 66));
+    float L = 0.f, O = 0.f;
+    for (int s2 = 0; s2 < p.nsplit; ++s2) {
+      const float ms = __ldcg(pb + (size_t)s2 * 66);
+      if (ms == -INFINITY) continue;
+      const float f = expf(ms - M);
+      L += __ldcg(pb + (size_t)s2 * 66 + 1) * f;
+      O += __ldcg(pb + (size_t)s2 * 66 + 2 + threadIdx.x) * f;
+    }
+    reinterpret_cast<T*>(p.out)[(size_t)b * p.inner + h * 64 + threadIdx.x] = from_f<T>(O / L);
+  }
+  if (threadIdx.x == 0) p.counters[bh] = 0;
+}
+
+template <typename P>
+static cudaError_t launch_k(void (*kern)(const P), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                            const P& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+cudaError_t launch_attn_self(int dtype, const AttnParams& p, cudaStream_t s, bool pdl) {
+  const dim3 grid((p.B * p.H + 3) / 4);
+  return dtype == 1 ? launch_k(attn_self_kernel<__nv_bfloat16>, grid, dim3(128), 0, s, pdl, p)
+                    : launch_k(attn_self_kernel<float>, grid, dim3(128), 0, s, pdl, p);
+}
+
+cudaError_t launch_attn_cross(int dtype, const AttnParams& p, cudaStream_t s, bool pdl) {
+  const dim3 grid(p.B * p.H, p.nsplit);
+  return dtype == 1 ? launch_k(attn_cross_kernel<__nv_bfloat16>, grid, dim3(128), 0, s, pdl, p)
+                    : launch_k(attn_cross_kernel<float>, grid, dim3(128), 0, s, pdl, p);
+}
+
+// ---------------------------------------------------------------------------
+// Sampler: one CTA of 1024 threads per sequence.
+//   guided = CFG mix of the sequence's two rows (fp32), restricted to the
+//   candidate range [lo, hi) (the level's vocab mask); temperature 0 ->
+//   argmax (first index on ties); else scaled = guided / T, threshold = the
+//   top_k-th largest scaled value (radix select on order-preserving keys;
+//   ties at the threshold survive), token = argmax(scaled + Gumbel(u)) over
+//   the survivors. Then the embedding of the token becomes the next depth
+//   input of every row of the sequence and is added into the frame sum;
+//   on the last level the next temporal input R(sum / depth) is written.
+// ---------------------------------------------------------------------------
+constexpr int kSampleThreads = 1024;
+
+__device__ __forceinline__ void argmax_combine(float& v, int& i, float v2, int i2) {
+  if (v2 > v || (v2 == v && i2 < i)) {
+    v = v2;
+    i = i2;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  extern __shared__ __align__(16) float vals[];
+  __shared__ unsigned hist[256];
+  __shared__ unsigned sel_prefix, sel_k;
+  __shared__ float rv[32];
+  __shared__ int ri[32];
+  __shared__ int tok_s;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int seq = blockIdx.x;
+  const int n = p.hi - p.lo;
+  const int r0 = seq * p.rows_per_seq;
+
+  int token;
+  if (p.forced) {
+    token = p.forced[seq];
+  } else {
+    const float* l0 = p.logits + (size_t)r0 * p.logits_stride + (p.lo - p.col_offset);
+    const float* l1 = l0 + p.logits_stride;
+    for (int i = tid; i < n; i += kSampleThreads) {
+      float g = (p.rows_per_seq == 2) ? cfg_mix(l0[i], l1[i], p.w) : l0[i];
+      if (p.temperature != 0.0f) g = __fdiv_rn(g, p.temperature);
+      vals[i] = g;
+    }
+    __syncthreads();
+    float thr = -INFINITY;
+    if (p.temperature != 0.0f && p.top_k > 0 && p.top_k < n) {
+      if (tid == 0) {
+        sel_prefix = 0u;
+        sel_k = (unsigned)p.top_k;
+      }
+      unsigned mask = 0u;
+      for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        if (tid < 256) hist[tid] = 0u;
+        __syncthreads();
+        const unsigned prefix = sel_prefix;
+        for (int i = tid; i < n; i += kSampleThreads) {
+          const unsigned key = float_order_key(vals[i]);
+          if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (warp == 0) {
+          // lane L owns digits 255-8L ... 248-8L (descending)
+          unsigned cnt[8], tot = 0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            cnt[q] = hist[255 - 8 * lane - q];
+            tot += cnt[q];
+          }
+          unsigned incl = tot;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const unsigned t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+          }
+          const unsigned excl = incl - tot;
+          const unsigned kk = sel_k;
+          const bool mine = excl < kk && incl >= kk;
+          const unsigned ballot = __ballot_sync(0xffffffffu, mine);
+          if (mine) {
+            unsigned cum = excl;
+            int dg = 255 - 8 * lane;
+            for (int q = 0; q < 8; ++q) {
+              if (cum + cnt[q] >= kk) {
+                dg = 255 - 8 * lane - q;
+                break;
+              }
+              cum += cnt[q];
+            }
+            sel_prefix = prefix | ((unsigned)dg << shift);
+            sel_k = kk - cum;
+          }
+          (void)ballot;
+        }
+        mask |= 255u << shift;
+        __syncthreads();
+      }
+      thr = float_from_order_key(sel_prefix);
+    }
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    const float* uni = p.uniforms ? p.uniforms + (size_t)seq * p.uni_seq_stride : nullptr;
+    const uint64_t seed = p.seeds[seq];
+    for (int i = tid; i < n; i += kSampleThreads) {
+      float v = vals[i];
+      if (p.temperature != 0.0f) {
+        if (v < thr || v == -INFINITY) {
+          v = -INFINITY;
+        } else {
+          const int vid = p.lo + i;
+          const float u = uni ? uni[vid] : philox_uniform(seed, p.step, (uint32_t)vid);
+          v = __fadd_rn(v, gumbel_from_uniform(u));
+        }
+      }
+      argmax_combine(best, bi, v, i);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
+      const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+      argmax_combine(best, bi, v2, i2);
+    }
+    if (lane == 0) {
+      rv[warp] = best;
+      ri[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      best = rv[lane];
+      bi = ri[lane];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+        argmax_combine(best, bi, v2, i2);
+      }
+      if (lane == 0) tok_s = p.lo + (bi == 0x7fffffff ? 0 : bi);
+    }
+    __syncthreads();
+    token = tok_s;
+  }
+  if (token < 0 || token >= p.V) {
+    if (tid == 0) atomicOr(p.err, kErrBadToken);
+    token = 0;
+  }
+  if (tid == 0 && p.tokens) p.tokens[(size_t)seq * p.tok_stride + p.tok_index] = token;
+
+  const T* e = reinterpret_cast<const T*>(p.emb) + (size_t)token * p.d;
+  T* din = reinterpret_cast<T*>(p.din);
+  T* fs = reinterpret_cast<T*>(p.fsum);
+  T* tin = reinterpret_cast<T*>(p.tin);
+  for (int r = 0; r < p.rows_per_seq; ++r) {
+    const size_t row = (size_t)(r0 + r) * p.d;
+    for (int i = tid; i < p.d; i += kSampleThreads) {
+      const T ev = e[i];
+      din[row + i] = ev;
+      const float s = p.is_first ? to_f(ev) : rnd<T>(__fadd_rn(to_f(fs[row + i]), to_f(ev)));
+      fs[row + i] = from_f<T>(s);
+      if (p.is_last) tin[row + i] = from_f<T>(__fdiv_rn(s, (float)p.depth));
+    }
+  }
+}
+
+size_t sample_smem_bytes(int n_candidates) { return (size_t)n_candidates * 4; }
+
+cudaError_t sample_set_smem_limits() {
+  cudaError_t e = cudaFuncSetAttribute(sample_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kSampleMaxSmem);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(sample_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSampleMaxSmem);
+}
+
+cudaError_t launch_sample(int dtype, const SampleParams& p, int num_seq, cudaStream_t s, bool pdl) {
+  const size_t smem = sample_smem_bytes(p.hi - p.lo);
+  if (smem > (size_t)kSampleMaxSmem) return cudaErrorInvalidValue;
+  return dtype == 1 ? launch_k(sample_kernel<__nv_bfloat16>, dim3(num_seq), dim3(kSampleThreads), smem, s, pdl, p)
+                    : launch_k(sample_kernel<float>, dim3(num_seq), dim3(kSampleThreads), smem, s, pdl, p);
+}
+
+// ---------------------------------------------------------------------------
+// Small helpers
+// ---------------------------------------------------------------------------
+struct EmbedParams {
+  const void* emb;
+  const int32_t* ids;
+  int rows, d;
+  void* out;
+};
+
+template <typename T>
+__global__ void embed_rows_kernel(const EmbedParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int r = blockIdx.x;
+  const int id = p.ids ? p.ids[r] : 0;
+  const T* e = reinterpret_cast<const T*>(p.emb) + (size_t)id * p.d;
+  T* o = reinterpret_cast<T*>(p.out) + (size_t)r * p.d;
+  for (int i = threadIdx.x; i < p.d; i += blockDim.x) o[i] = e[i];
+}
+
+cudaError_t launch_embed_rows(int dtype, const void* emb, const int32_t* ids, int rows, int d, void* out,
+                              cudaStream_t s, bool pdl) {
+  EmbedParams p{emb, ids, rows, d, out};
+  return dtype == 1 ? launch_k(embed_rows_kernel<__nv_bfloat16>, dim3(rows), dim3(256), 0, s, pdl, p)
+                    : launch_k(embed_rows_kernel<float>, dim3(rows), dim3(256), 0, s, pdl, p);
+}
+
+struct ConvParams {
+  const void* src;
+  size_t n;
+  void* dst;
+};
+
+template <typename T>
+__global__ void f32_to_act_kernel(const ConvParams p) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < p.n; i += (size_t)gridDim.x * blockDim.x)
+    reinterpret_cast<T*>(p.dst)[i] = from_f<T>(reinterpret_cast<const float*>(p.src)[i]);
+}
+template <typename T>
+__global__ void act_to_f32_kernel(const ConvParams p) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < p.n; i += (size_t)gridDim.x * blockDim.x)
+    reinterpret_cast<float*>(p.dst)[i] = to_f(reinterpret_cast<const T*>(p.src)[i]);
+}
+
+cudaError_t launch_f32_to_act(int dtype, const float* src, size_t n, void* out, cudaStream_t s) {
+  ConvParams p{src, n, out};
+  const int grid = (int)std::min<size_t>((n + 255) / 256, 4096);
+  if (grid == 0) return cudaSuccess;
+  if (dtype == 1) f32_to_act_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(p);
+  else f32_to_act_kernel<float><<<grid, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_act_to_f32(int dtype, const void* src, size_t n, float* out, cudaStream_t s) {
+  ConvParams p{src, n, out};
+  const int grid = (int)std::min<size_t>((n + 255) / 256, 4096);
+  if (grid == 0) return cudaSuccess;
+  if (dtype == 1) act_to_f32_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(p);
+  else act_to_f32_kernel<float><<<grid, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace mrtdf

@@ -1,0 +1,102 @@
+// Parameter blocks and launch entry points of the decode-step kernels
+// (temporal_step / depth_step / sampler). Host code fills these structs;
+// every pointer is device memory.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mrtdf {
+
+// Epilogues of the GEMV phase kernel.
+enum GemvMode : int {
+  kGemvStore = 0,   // out[b, off + u] = R(acc)
+  kGemvResid = 1,   // out[b, u] = R(resid[b, u] + R(acc))      (residual add)
+  kGemvQKV = 2,     // fused q/k/v: q -> out, k/v -> cache at `pos`
+  kGemvGeglu = 3,   // unit = (wi_0 row, wi_1 row): out[b, u] = R(gelu(R(a)) * R(b))
+  kGemvLogits = 4,  // float out[b, off + u] = R(acc)
+};
+
+struct GemvParams {
+  const void* W;       // weight rows, (units * rows_per_unit, cols), row-major
+  const void* x;       // input activations (B, x_stride)
+  const void* norm_w;  // RMSNorm scale (cols), or null for a plain input
+  void* out;
+  const void* resid;
+  void* kc;
+  void* vc;
+  int* err;
+  int units;
+  int cols;
+  int B;
+  int x_stride, out_stride, resid_stride;
+  int out_offset;
+  int inner, H, cap, pos;  // kGemvQKV
+};
+
+// Bytes of one TMA stage of the GEMV kernel and the number of stages.
+constexpr int kGemvStageBytes = 24576;
+constexpr int kGemvStages = 3;
+constexpr int kGemvThreads = 256;
+constexpr int kGemvMaxB = 8;
+
+size_t gemv_smem_bytes(int B, int cols);
+// Launch the GEMV phase over `grid` CTAs. dtype: 0 fp32, 1 bf16.
+cudaError_t launch_gemv(int dtype, int mode, bool norm, const GemvParams& p, int grid, cudaStream_t s, bool pdl);
+cudaError_t gemv_set_smem_limits();
+
+struct AttnParams {
+  const void* q;    // (B, inner)
+  const void* K;    // (B, H, cap, 64)
+  const void* V;
+  const float* bias;  // (H, bias_stride) for this query position, or null
+  int bias_stride;
+  void* out;        // (B, inner)
+  float* part;      // split-K partials (B*H, nsplit, 66), cross attention only
+  int* counters;    // (B*H), zero between launches
+  int* err;
+  int B, H, cap, T;  // T = number of valid keys
+  int inner;
+  int nsplit;
+};
+cudaError_t launch_attn_self(int dtype, const AttnParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_attn_cross(int dtype, const AttnParams& p, cudaStream_t s, bool pdl);
+constexpr int kCrossSplit = 8;
+
+struct SampleParams {
+  const float* logits;  // (B, logits_stride); column c holds vocab id col_offset + c
+  int logits_stride;
+  int col_offset;
+  int lo, hi;            // candidate vocab range
+  int rows_per_seq;      // 2 with CFG, else 1
+  float w, temperature;
+  int top_k;
+  const uint64_t* seeds;  // per sequence
+  uint32_t step;          // frame * rvq_depth + level
+  const float* uniforms;  // optional draws: this step's row of V for sequence 0
+  long long uni_seq_stride;  // floats between the rows of consecutive sequences
+  const int32_t* forced;  // optional forced token per sequence (teacher forcing)
+  int32_t* tokens;        // tokens[seq * tok_stride + tok_index]
+  int tok_stride, tok_index;
+  const void* emb;        // (V, d)
+  int d, V;
+  void* din;              // (B, d) next depth input
+  void* fsum;             // (B, d) running embedding sum of the frame
+  void* tin;              // (B, d) next temporal input (written on the last level)
+  int depth;
+  int is_first, is_last;
+  int* err;
+};
+cudaError_t launch_sample(int dtype, const SampleParams& p, int num_seq, cudaStream_t s, bool pdl);
+size_t sample_smem_bytes(int n_candidates);
+cudaError_t sample_set_smem_limits();
+constexpr int kSampleMaxSmem = 160 * 1024;
+
+// out[r, :] = emb[ids[r], :] for r < rows (ids == null: id 0 = PAD).
+cudaError_t launch_embed_rows(int dtype, const void* emb, const int32_t* ids, int rows, int d, void* out,
+                              cudaStream_t s, bool pdl);
+// out[r, :] = from_f(src_f32[r, :]) (host-provided inputs already on device).
+cudaError_t launch_f32_to_act(int dtype, const float* src, size_t n, void* out, cudaStream_t s);
+cudaError_t launch_act_to_f32(int dtype, const void* src, size_t n, float* out, cudaStream_t s);
+
+}  // namespace mrtdf

@@ -1,0 +1,47 @@
+// Parameter blocks and launch entry points of the encoder kernels
+// (Depthformer::encode and the cross-attention K/V projection).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mrtdf {
+
+enum GemmEpi : int {
+  kEpiStore = 0,    // out[m, n] = R(acc)
+  kEpiResid = 1,    // out[m, n] = R(out[m, n] + R(acc))
+  kEpiGeglu = 2,    // columns (2j, 2j+1) = (wi_0, wi_1): out[m, j] = R(gelu(R(a)) * R(b))
+  kEpiCrossKV = 3,  // column n of the all-layer K/V projection -> cross cache
+};
+
+struct GemmParams {
+  const void* A;  // (M, K) row-major, lda
+  const void* W;  // (N, K) row-major (Linear weight layout (out, in))
+  void* out;      // (M, ldo)
+  int M, N, K;
+  int lda, ldo;
+  // kEpiCrossKV: ck / cv are (Lt, B, H, Smax, 64); row m = b * S + s
+  void* ck;
+  void* cv;
+  int S, B, H, Smax, inner;
+};
+
+cudaError_t launch_gemm(int dtype, int epi, const GemmParams& p, cudaStream_t s, bool pdl);
+cudaError_t gemm_set_smem_limits();
+
+struct EncAttnParams {
+  const void* qkv;  // (B*S, 3*inner): q | k | v
+  void* out;        // (B*S, inner)
+  int B, S, H, inner;
+};
+cudaError_t launch_enc_attention(int dtype, const EncAttnParams& p, cudaStream_t s, bool pdl);
+
+// x[b*S+s, :] = R(emb[ids[b*S+s], :] + pe[s, :]) with pe already rounded to the dtype.
+// An id outside [0, V) sets kErrBadToken in *err and reads row 0 instead.
+cudaError_t launch_embed_pe(int dtype, const void* emb, const float* pe, const int32_t* ids, int rows, int S, int d,
+                            int V, void* out, int* err, cudaStream_t s, bool pdl);
+// out[m, :] = RMSNorm(x[m, :]) * w (rounding as in the decode path).
+cudaError_t launch_rmsnorm_rows(int dtype, const void* x, const void* w, int rows, int d, void* out, cudaStream_t s,
+                                bool pdl);
+
+}  // namespace mrtdf

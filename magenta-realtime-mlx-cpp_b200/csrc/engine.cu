@@ -1,0 +1,1109 @@
+// Engine and C ABI (include/mrtdf.h): weight upload into fused device
+// layouts, per-stream KV arenas, the step sequences of encode /
+// temporal_step / depth_step / sample, and the whole-chunk CUDA graph of
+// generate_tokens.
+//
+// Reference call structure (rhymeswithlion/magenta-realtime-mlx-cpp):
+//   Depthformer ctor       depthformer/model.cpp:173-213
+//   encode                 model.cpp:226-241
+//   temporal_step (eager)  model.cpp:322-514 (493-513)
+//   depth_step (eager)     model.cpp:516-659 (638-659)
+//   bias precompute        model.cpp:302-320
+//   generate_tokens        depthformer/decode.cpp:239-573 (non-speculative)
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/mrtdf.h"
+#include "decode_kernels.cuh"
+#include "device_errors.h"
+#include "encoder_kernels.cuh"
+#include "host_util.h"
+
+using namespace mrtdf;
+
+namespace {
+
+#define CUDA_OK(expr)                                                                                    \
+  do {                                                                                                   \
+    cudaError_t e_ = (expr);                                                                             \
+    if (e_ != cudaSuccess)                                                                               \
+      throw Error{MRTDF_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)};                   \
+  } while (0)
+
+bool env_flag(const char* name, bool dflt) {
+  const char* v = std::getenv(name);
+  if (!v || !*v) return dflt;
+  return !(v[0] == '0' || v[0] == 'n' || v[0] == 'N' || v[0] == 'f' || v[0] == 'F');
+}
+
+// Sub-allocator over one cudaMalloc: 256-byte aligned slices.
+struct Arena {
+  uint8_t* base = nullptr;
+  size_t cap = 0, used = 0;
+  void reserve(size_t bytes) {
+    if (base) cudaFree(base);
+    base = nullptr;
+    cap = bytes;
+    used = 0;
+    if (bytes) CUDA_OK(cudaMalloc(&base, bytes));
+  }
+  void* take(size_t bytes) {
+    const size_t off = (used + 255) & ~(size_t)255;
+    if (off + bytes > cap) throw Error{MRTDF_ERR_CUDA, "arena overflow"};
+    used = off + bytes;
+    return base + off;
+  }
+  ~Arena() {
+    if (base) cudaFree(base);
+  }
+};
+
+struct EncLayerDev {
+  void *wqkv, *wo, *n_attn, *wi, *wout, *n_ffn;
+};
+struct DecLayerDev {
+  void *wqkv, *wo, *n_self, *wcq, *wco, *n_cross, *wi, *wout, *n_ffn;
+};
+
+}  // namespace
+
+struct mrtdf_engine {
+  mrtdf_config c{};
+  int device = 0;
+  int num_sms = 148;
+  int esize = 2;  // bytes per element of the compute dtype
+  bool loaded = false;
+  bool pdl = true;
+  Arena weights;
+  void* emb = nullptr;
+  void* enc_norm = nullptr;
+  void* dec_norm = nullptr;
+  void* lm_head = nullptr;
+  void* wckv = nullptr;  // (Lt * 2 * inner, d)
+  std::vector<EncLayerDev> enc;
+  std::vector<DecLayerDev> tl, dl;
+  float* tbias = nullptr;  // (Tmax, H, Tmax)
+  float* dbias = nullptr;  // (depth, H, depth)
+  float* pe = nullptr;     // (Smax, d)
+  int inner() const { return c.num_heads * c.d_kv; }
+};
+
+struct GraphKey {
+  int frames, depth, top_k, masked, has_uniforms, seq_len;
+  float temperature, w;
+  bool operator<(const GraphKey& o) const {
+    return std::memcmp(this, &o, sizeof(GraphKey)) < 0;
+  }
+};
+
+struct mrtdf_stream {
+  mrtdf_engine* eng = nullptr;
+  int nseq = 1, rps = 2, B = 2;
+  cudaStream_t s = nullptr;
+  Arena mem;
+  // activations (compute dtype unless noted)
+  void *tx, *dx, *tin, *din, *fsum, *qb, *ao, *hb;
+  float* logits;  // (B, V)
+  float* stage_f32;  // host<->device float staging, (B, max(d, V))
+  // caches
+  void *tk, *tv, *ck, *cv, *dk, *dv;
+  // encoder scratch
+  void *ex, *en, *eqkv, *eo, *eh;
+  int32_t* ids;
+  int32_t* tokens;  // (nseq, Tmax, depth)
+  uint64_t* seeds;  // (nseq)
+  int32_t* forced;  // (nseq)
+  float* part;
+  int* counters;
+  int* err;
+  float* uniforms = nullptr;
+  size_t uniforms_cap = 0;
+  // host state
+  bool encoded = false;
+  int S = 0;
+  int t_len = 0, d_len = 0;
+  bool have_temporal = false;
+  std::map<GraphKey, cudaGraphExec_t> graphs;
+  // measurement hook: when set, only the GEMV phases are enqueued and their
+  // launches / algorithmic bytes are counted
+  bool gemv_only = false;
+  long long gemv_launches = 0;
+  double gemv_bytes = 0.0;
+  ~mrtdf_stream() {
+    for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+    if (s) cudaStreamDestroy(s);
+  }
+};
+
+// ---------------------------------------------------------------------------
+// helpers
+// ---------------------------------------------------------------------------
+namespace {
+
+template <typename F>
+int guarded(F&& f) {
+  try {
+    f();
+    return MRTDF_OK;
+  } catch (const Error& e) {
+    set_error(e.code, e.msg);
+    return e.code;
+  } catch (const std::exception& e) {
+    set_error(MRTDF_ERR_INVALID, e.what());
+    return MRTDF_ERR_INVALID;
+  }
+}
+
+void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw Error{MRTDF_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e)};
+}
+
+// Convert host float32 data to the compute dtype's bytes.
+std::vector<uint8_t> to_dtype(const float* src, size_t n, int dtype) {
+  std::vector<uint8_t> out(n * (dtype == MRTDF_DTYPE_BF16 ? 2 : 4));
+  if (dtype == MRTDF_DTYPE_BF16) {
+    uint16_t* o = (uint16_t*)out.data();
+    parallel_for((int64_t)n, [&](int64_t a, int64_t b) {
+      for (int64_t i = a; i < b; ++i) o[i] = bf16_bits(src[i]);
+    });
+  } else {
+    std::memcpy(out.data(), src, n * 4);
+  }
+  return out;
+}
+
+// Weight source: key -> float32 host data.
+struct WeightSource {
+  std::function<const float*(const std::string&, int64_t)> get;
+};
+
+}  // namespace
+
+// Upload every weight into fused device tensors.
+static void upload_weights(mrtdf_engine* E, const WeightSource& src) {
+  const mrtdf_config& c = E->c;
+  const int64_t d = c.d_model, in = E->inner(), ff = c.d_ff, V = c.vocab_size;
+  const int es = E->esize;
+  // bytes: count everything first
+  size_t total = 0;
+  auto add = [&](int64_t n) { total += ((size_t)n * es + 255) & ~(size_t)255; };
+  add(V * d);
+  for (int i = 0; i < c.num_encoder_layers; ++i) {
+    add(3 * in * d); add(d * in); add(d); add(2 * ff * d); add(d * ff); add(d);
+  }
+  add(d);
+  for (int i = 0; i < c.num_temporal_layers; ++i) {
+    add(3 * in * d); add(d * in); add(d); add(in * d); add(d * in); add(d); add(2 * ff * d); add(d * ff); add(d);
+  }
+  add((int64_t)c.num_temporal_layers * 2 * in * d);
+  for (int i = 0; i < c.num_depth_layers; ++i) {
+    add(3 * in * d); add(d * in); add(d); add(2 * ff * d); add(d * ff); add(d);
+  }
+  add(d);
+  add(V * d);
+  const size_t tb = (size_t)c.max_frames * c.num_heads * c.max_frames * 4;
+  const size_t db = (size_t)c.rvq_depth * c.num_heads * c.rvq_depth * 4;
+  const size_t pb = (size_t)c.max_encoder_length * d * 4;
+  total += tb + db + pb + 3 * 256;
+  E->weights.reserve(total);
+
+  std::vector<float> tmp;
+  auto put = [&](void* dst, const float* host, int64_t n) {
+    std::vector<uint8_t> bytes = to_dtype(host, (size_t)n, c.dtype);
+    CUDA_OK(cudaMemcpy(dst, bytes.data(), bytes.size(), cudaMemcpyHostToDevice));
+  };
+  auto fetch = [&](const std::string& key, int64_t n) { return src.get(key, n); };
+  auto single = [&](const std::string& key, int64_t n) {
+    void* dst = E->weights.take((size_t)n * es);
+    put(dst, fetch(key, n), n);
+    return dst;
+  };
+  // concatenate rows of several (rows_i, d) matrices
+  auto concat = [&](const std::vector<std::pair<std::string, int64_t>>& parts, int64_t cols) {
+    int64_t rows = 0;
+    for (auto& p : parts) rows += p.second;
+    tmp.resize((size_t)(rows * cols));
+    int64_t r = 0;
+    for (auto& p : parts) {
+      const float* h = fetch(p.first, p.second * cols);
+      std::memcpy(&tmp[(size_t)(r * cols)], h, (size_t)(p.second * cols) * 4);
+      r += p.second;
+    }
+    void* dst = E->weights.take((size_t)(rows * cols) * es);
+    put(dst, tmp.data(), rows * cols);
+    return dst;
+  };
+  // interleave wi_0 / wi_1 rows: row 2j = wi_0[j], row 2j+1 = wi_1[j]
+  auto geglu = [&](const std::string& p) {
+    const float* a = fetch(p + "ffn.wi_0.weight", ff * d);
+    const float* b = fetch(p + "ffn.wi_1.weight", ff * d);
+    tmp.resize((size_t)(2 * ff * d));
+    for (int64_t j = 0; j < ff; ++j) {
+      std::memcpy(&tmp[(size_t)((2 * j) * d)], a + j * d, (size_t)d * 4);
+      std::memcpy(&tmp[(size_t)((2 * j + 1) * d)], b + j * d, (size_t)d * 4);
+    }
+    void* dst = E->weights.take((size_t)(2 * ff * d) * es);
+    put(dst, tmp.data(), 2 * ff * d);
+    return dst;
+  };
+
+  E->emb = single("token_embedding.weight", V * d);
+  E->enc.resize(c.num_encoder_layers);
+  for (int i = 0; i < c.num_encoder_layers; ++i) {
+    const std::string p = "encoder_layers." + std::to_string(i) + ".";
+    EncLayerDev& L = E->enc[i];
+    L.wqkv = concat({{p + "self_attn.q_proj.weight", in}, {p + "self_attn.k_proj.weight", in},
+                     {p + "self_attn.v_proj.weight", in}},
+                    d);
+    L.wo = single(p + "self_attn.o_proj.weight", d * in);
+    L.n_attn = single(p + "pre_attn_norm.weight", d);
+    L.wi = geglu(p);
+    L.wout = single(p + "ffn.wo.weight", d * ff);
+    L.n_ffn = single(p + "pre_ffn_norm.weight", d);
+  }
+  E->enc_norm = single("encoder_norm.weight", d);
+  E->tl.resize(c.num_temporal_layers);
+  for (int i = 0; i < c.num_temporal_layers; ++i) {
+    const std::string p = "temporal_layers." + std::to_string(i) + ".";
+    DecLayerDev& L = E->tl[i];
+    L.wqkv = concat({{p + "self_attn.q_proj.weight", in}, {p + "self_attn.k_proj.weight", in},
+                     {p + "self_attn.v_proj.weight", in}},
+                    d);
+    L.wo = single(p + "self_attn.o_proj.weight", d * in);
+    L.n_self = single(p + "pre_self_attn_norm.weight", d);
+    L.wcq = single(p + "cross_attn.q_proj.weight", in * d);
+    L.wco = single(p + "cross_attn.o_proj.weight", d * in);
+    L.n_cross = single(p + "pre_cross_attn_norm.weight", d);
+    L.wi = geglu(p);
+    L.wout = single(p + "ffn.wo.weight", d * ff);
+    L.n_ffn = single(p + "pre_ffn_norm.weight", d);
+  }
+  {
+    std::vector<std::pair<std::string, int64_t>> parts;
+    for (int i = 0; i < c.num_temporal_layers; ++i) {
+      const std::string p = "temporal_layers." + std::to_string(i) + ".";
+      parts.push_back({p + "cross_attn.k_proj.weight", in});
+      parts.push_back({p + "cross_attn.v_proj.weight", in});
+    }
+    E->wckv = concat(parts, d);
+  }
+  E->dl.resize(c.num_depth_layers);
+  for (int i = 0; i < c.num_depth_layers; ++i) {
+    const std::string p = "depth_layers." + std::to_string(i) + ".";
+    DecLayerDev& L = E->dl[i];
+    L.wqkv = concat({{p + "self_attn.q_proj.weight", in}, {p + "self_attn.k_proj.weight", in},
+                     {p + "self_attn.v_proj.weight", in}},
+                    d);
+    L.wo = single(p + "self_attn.o_proj.weight", d * in);
+    L.n_self = single(p + "pre_self_attn_norm.weight", d);
+    L.wcq = L.wco = L.n_cross = nullptr;
+    L.wi = geglu(p);
+    L.wout = single(p + "ffn.wo.weight", d * ff);
+    L.n_ffn = single(p + "pre_ffn_norm.weight", d);
+  }
+  E->dec_norm = single("decoder_norm.weight", d);
+  E->lm_head = single("lm_head.weight", V * d);
+
+  // Relative-position bias per query position (precompute_*_biases,
+  // model.cpp:302-320): bias[q][h][j] = table[bucket(j - q)][h], j <= q,
+  // table values in the compute dtype (load_param casts, modules.cpp:127-128).
+  auto bias_table = [&](const std::string& key, int nb, int maxd, int T) {
+    const float* tab = fetch(key, (int64_t)nb * c.num_heads);
+    std::vector<float> b((size_t)T * c.num_heads * T, 0.f);
+    for (int q = 0; q < T; ++q)
+      for (int j = 0; j <= q; ++j) {
+        const int bk = relative_bucket(j - q, nb, maxd);
+        for (int h = 0; h < c.num_heads; ++h) {
+          float v = tab[(size_t)bk * c.num_heads + h];
+          if (c.dtype == MRTDF_DTYPE_BF16) v = bf16_round_host(v);
+          b[((size_t)q * c.num_heads + h) * T + j] = v;
+        }
+      }
+    float* dst = (float*)E->weights.take(b.size() * 4);
+    CUDA_OK(cudaMemcpy(dst, b.data(), b.size() * 4, cudaMemcpyHostToDevice));
+    return dst;
+  };
+  E->tbias = bias_table("temporal_rel_pos.relative_attention_bias.weight", c.temporal_num_buckets,
+                        c.temporal_max_distance, c.max_frames);
+  E->dbias = bias_table("depth_rel_pos.relative_attention_bias.weight", c.depth_num_buckets, c.depth_max_distance,
+                        c.rvq_depth);
+  // Sinusoid table, cast to the compute dtype (model.cpp:232-235).
+  std::vector<float> pe = sinusoid_table(c.max_encoder_length, (int)d);
+  if (c.dtype == MRTDF_DTYPE_BF16)
+    for (auto& v : pe) v = bf16_round_host(v);
+  E->pe = (float*)E->weights.take(pe.size() * 4);
+  CUDA_OK(cudaMemcpy(E->pe, pe.data(), pe.size() * 4, cudaMemcpyHostToDevice));
+  E->loaded = true;
+}
+
+// ---------------------------------------------------------------------------
+// Step sequences
+// ---------------------------------------------------------------------------
+namespace {
+
+int gemv_grid(const mrtdf_engine* E, int units) { return std::min(units, E->num_sms); }
+
+void gemv(mrtdf_stream* st, int mode, bool norm, GemvParams p) {
+  mrtdf_engine* E = st->eng;
+  p.err = st->err;
+  p.B = st->B;
+  // algorithmic bytes: weight rows + input rows + output rows (+ residual)
+  const double es = E->esize;
+  const int rpu = mode == kGemvGeglu ? 2 : 1;
+  double bytes = (double)p.units * rpu * p.cols * es + (double)p.B * p.cols * es;
+  bytes += (double)p.B * p.units * (mode == kGemvLogits ? 4.0 : es) * (mode == kGemvResid ? 2.0 : 1.0);
+  if (norm) bytes += (double)p.cols * es;
+  st->gemv_launches += 1;
+  st->gemv_bytes += bytes;
+  check_cuda(launch_gemv(E->c.dtype, mode, norm, p, gemv_grid(E, p.units), st->s, E->pdl), "gemv launch");
+}
+
+size_t act_bytes(const mrtdf_engine* E, size_t n) { return n * E->esize; }
+
+// One DecoderLayer::forward for the stream's B rows at cache position
+// `pos` (modules.cpp:384-408). x_in is read, the layer output lands in xr.
+void enqueue_decoder_layer(mrtdf_stream* st, const DecLayerDev& L, const void* x_in, void* xr, void* kc, void* vc,
+                           int cap, int pos, const float* bias, int bias_stride, const void* ck, const void* cv) {
+  mrtdf_engine* E = st->eng;
+  const mrtdf_config& c = E->c;
+  const int d = c.d_model, in = E->inner(), ff = c.d_ff;
+  GemvParams p{};
+  // 1. pre-norm + fused q/k/v, k/v appended to the cache at `pos`
+  p.W = L.wqkv; p.x = x_in; p.norm_w = L.n_self; p.out = st->qb; p.kc = kc; p.vc = vc;
+  p.units = 3 * in; p.cols = d; p.x_stride = d; p.out_stride = in; p.inner = in; p.H = c.num_heads;
+  p.cap = cap; p.pos = pos;
+  gemv(st, kGemvQKV, true, p);
+  // 2. self attention with relative-position bias (scale 1.0)
+  AttnParams a{};
+  a.q = st->qb; a.K = kc; a.V = vc; a.bias = bias; a.bias_stride = bias_stride; a.out = st->ao; a.err = st->err;
+  a.B = st->B; a.H = c.num_heads; a.cap = cap; a.T = pos + 1; a.inner = in; a.nsplit = 1;
+  if (!st->gemv_only) check_cuda(launch_attn_self(c.dtype, a, st->s, E->pdl), "attn_self launch");
+  // 3. o_proj + residual
+  p = GemvParams{};
+  p.W = L.wo; p.x = st->ao; p.out = xr; p.resid = x_in; p.units = d; p.cols = in; p.x_stride = in;
+  p.out_stride = d; p.resid_stride = d;
+  gemv(st, kGemvResid, false, p);
+  if (ck) {
+    // 4. pre-norm + cross q
+    p = GemvParams{};
+    p.W = L.wcq; p.x = xr; p.norm_w = L.n_cross; p.out = st->qb; p.units = in; p.cols = d; p.x_stride = d;
+    p.out_stride = in;
+    gemv(st, kGemvStore, true, p);
+    // 5. cross attention over the cached encoder K/V
+    AttnParams ca{};
+    ca.q = st->qb; ca.K = ck; ca.V = cv; ca.bias = nullptr; ca.out = st->ao; ca.part = st->part;
+    ca.counters = st->counters; ca.err = st->err; ca.B = st->B; ca.H = c.num_heads; ca.cap = c.max_encoder_length;
+    ca.T = st->S; ca.inner = in; ca.nsplit = kCrossSplit;
+    if (!st->gemv_only) check_cuda(launch_attn_cross(c.dtype, ca, st->s, E->pdl), "attn_cross launch");
+    // 6. cross o_proj + residual
+    p = GemvParams{};
+    p.W = L.wco; p.x = st->ao; p.out = xr; p.resid = xr; p.units = d; p.cols = in; p.x_stride = in;
+    p.out_stride = d; p.resid_stride = d;
+    gemv(st, kGemvResid, false, p);
+  }
+  // 7. pre-norm + wi_0 / wi_1 + gelu * gate
+  p = GemvParams{};
+  p.W = L.wi; p.x = xr; p.norm_w = L.n_ffn; p.out = st->hb; p.units = ff; p.cols = d; p.x_stride = d;
+  p.out_stride = ff;
+  gemv(st, kGemvGeglu, true, p);
+  // 8. wo + residual
+  p = GemvParams{};
+  p.W = L.wout; p.x = st->hb; p.out = xr; p.resid = xr; p.units = d; p.cols = ff; p.x_stride = ff;
+  p.out_stride = d; p.resid_stride = d;
+  gemv(st, kGemvResid, false, p);
+}
+
+size_t layer_cache_elems(const mrtdf_stream* st, int cap) {
+  return (size_t)st->B * st->eng->c.num_heads * cap * 64;
+}
+
+// temporal_step: 20 decoder layers over tin -> tx (model.cpp:493-513).
+void enqueue_temporal(mrtdf_stream* st, int f) {
+  mrtdf_engine* E = st->eng;
+  const mrtdf_config& c = E->c;
+  const size_t tcs = layer_cache_elems(st, c.max_frames);
+  const size_t ccs = layer_cache_elems(st, c.max_encoder_length);
+  for (int l = 0; l < c.num_temporal_layers; ++l) {
+    uint8_t* tk = (uint8_t*)st->tk + act_bytes(E, tcs * l);
+    uint8_t* tv = (uint8_t*)st->tv + act_bytes(E, tcs * l);
+    const uint8_t* ck = (const uint8_t*)st->ck + act_bytes(E, ccs * l);
+    const uint8_t* cv = (const uint8_t*)st->cv + act_bytes(E, ccs * l);
+    enqueue_decoder_layer(st, E->tl[l], l == 0 ? st->tin : st->tx, st->tx, tk, tv, c.max_frames, f,
+                          E->tbias + (size_t)f * c.num_heads * c.max_frames, c.max_frames, ck, cv);
+  }
+}
+
+// depth_step: 4 decoder layers + decoder_norm + lm_head rows [lo, hi).
+void enqueue_depth(mrtdf_stream* st, int level, const void* x_in, int lo, int hi) {
+  mrtdf_engine* E = st->eng;
+  const mrtdf_config& c = E->c;
+  const size_t dcs = layer_cache_elems(st, c.rvq_depth);
+  for (int l = 0; l < c.num_depth_layers; ++l) {
+    uint8_t* dk = (uint8_t*)st->dk + act_bytes(E, dcs * l);
+    uint8_t* dv = (uint8_t*)st->dv + act_bytes(E, dcs * l);
+    enqueue_decoder_layer(st, E->dl[l], l == 0 ? x_in : st->dx, st->dx, dk, dv, c.rvq_depth, level,
+                          E->dbias + (size_t)level * c.num_heads * c.rvq_depth, c.rvq_depth, nullptr, nullptr);
+  }
+  GemvParams p{};
+  p.W = (const uint8_t*)E->lm_head + act_bytes(E, (size_t)lo * c.d_model);
+  p.x = st->dx; p.norm_w = E->dec_norm; p.out = st->logits; p.units = hi - lo; p.cols = c.d_model;
+  p.x_stride = c.d_model; p.out_stride = c.vocab_size; p.out_offset = lo;
+  gemv(st, kGemvLogits, true, p);
+}
+
+// encode: embed + PE, encoder layers, encoder_norm, cross K/V of every
+// temporal layer (model.cpp:226-241, modules.cpp:323-333).
+void enqueue_encode(mrtdf_stream* st, int S) {
+  mrtdf_engine* E = st->eng;
+  const mrtdf_config& c = E->c;
+  const int d = c.d_model, in = E->inner(), ff = c.d_ff;
+  const int M = st->B * S;
+  const int dt = c.dtype;
+  const bool pdl = E->pdl;
+  check_cuda(launch_embed_pe(dt, E->emb, E->pe, st->ids, M, S, d, c.vocab_size, st->ex, st->err, st->s, pdl),
+             "embed_pe");
+  for (int l = 0; l < c.num_encoder_layers; ++l) {
+    const EncLayerDev& L = E->enc[l];
+    check_cuda(launch_rmsnorm_rows(dt, st->ex, L.n_attn, M, d, st->en, st->s, pdl), "rmsnorm");
+    GemmParams g{};
+    g.A = st->en; g.W = L.wqkv; g.out = st->eqkv; g.M = M; g.N = 3 * in; g.K = d; g.lda = d; g.ldo = 3 * in;
+    check_cuda(launch_gemm(dt, kEpiStore, g, st->s, pdl), "gemm qkv");
+    EncAttnParams a{st->eqkv, st->eo, st->B, S, c.num_heads, in};
+    check_cuda(launch_enc_attention(dt, a, st->s, pdl), "enc attention");
+    g = GemmParams{};
+    g.A = st->eo; g.W = L.wo; g.out = st->ex; g.M = M; g.N = d; g.K = in; g.lda = in; g.ldo = d;
+    check_cuda(launch_gemm(dt, kEpiResid, g, st->s, pdl), "gemm o");
+    check_cuda(launch_rmsnorm_rows(dt, st->ex, L.n_ffn, M, d, st->en, st->s, pdl), "rmsnorm");
+    g = GemmParams{};
+    g.A = st->en; g.W = L.wi; g.out = st->eh; g.M = M; g.N = 2 * ff; g.K = d; g.lda = d; g.ldo = ff;
+    check_cuda(launch_gemm(dt, kEpiGeglu, g, st->s, pdl), "gemm wi");
+    g = GemmParams{};
+    g.A = st->eh; g.W = L.wout; g.out = st->ex; g.M = M; g.N = d; g.K = ff; g.lda = ff; g.ldo = d;
+    check_cuda(launch_gemm(dt, kEpiResid, g, st->s, pdl), "gemm wo");
+  }
+  check_cuda(launch_rmsnorm_rows(dt, st->ex, E->enc_norm, M, d, st->en, st->s, pdl), "encoder_norm");
+  GemmParams g{};
+  g.A = st->en; g.W = E->wckv; g.out = nullptr; g.M = M; g.N = c.num_temporal_layers * 2 * in; g.K = d; g.lda = d;
+  g.ck = st->ck; g.cv = st->cv; g.S = S; g.B = st->B; g.H = c.num_heads; g.Smax = c.max_encoder_length; g.inner = in;
+  check_cuda(launch_gemm(dt, kEpiCrossKV, g, st->s, pdl), "gemm cross kv");
+}
+
+void enqueue_sample(mrtdf_stream* st, int f, int level, const mrtdf_gen_opts& o, bool masked, int lo, int hi,
+                    bool forced) {
+  mrtdf_engine* E = st->eng;
+  const mrtdf_config& c = E->c;
+  SampleParams sp{};
+  sp.logits = st->logits; sp.logits_stride = c.vocab_size; sp.col_offset = 0; sp.lo = lo; sp.hi = hi;
+  sp.rows_per_seq = st->rps; sp.w = o.guidance_weight; sp.temperature = o.temperature; sp.top_k = o.top_k;
+  sp.seeds = st->seeds; sp.step = (uint32_t)(f * c.rvq_depth + level);
+  sp.uniforms = o.uniforms ? st->uniforms + (size_t)sp.step * c.vocab_size : nullptr;
+  sp.uni_seq_stride = (long long)o.num_frames * c.rvq_depth * c.vocab_size;
+  sp.forced = forced ? st->forced : nullptr;
+  sp.tokens = st->tokens; sp.tok_stride = c.max_frames * c.rvq_depth; sp.tok_index = f * c.rvq_depth + level;
+  sp.emb = E->emb; sp.d = c.d_model; sp.V = c.vocab_size; sp.din = st->din; sp.fsum = st->fsum; sp.tin = st->tin;
+  sp.depth = c.rvq_depth; sp.is_first = level == 0; sp.is_last = level == c.rvq_depth - 1; sp.err = st->err;
+  (void)masked;
+  check_cuda(launch_sample(c.dtype, sp, st->nseq, st->s, E->pdl), "sample launch");
+}
+
+void level_range(const mrtdf_config& c, bool masked, int level, int& lo, int& hi) {
+  if (masked) {
+    lo = c.codec_offset + level * c.codebook_size;
+    hi = lo + c.codebook_size;
+  } else {
+    lo = 0;
+    hi = c.vocab_size;
+  }
+}
+
+// The whole generate_tokens chunk (decode.cpp:364-513): PAD embedding for
+// frame 0, temporal step, rvq_depth x (depth step + sampler).
+void enqueue_chunk(mrtdf_stream* st, int S, const mrtdf_gen_opts& o) {
+  mrtdf_engine* E = st->eng;
+  const mrtdf_config& c = E->c;
+  if (!st->gemv_only) {
+    enqueue_encode(st, S);
+    check_cuda(launch_embed_rows(c.dtype, E->emb, nullptr, st->B, c.d_model, st->tin, st->s, E->pdl), "embed pad");
+  }
+  const bool masked = o.use_vocab_masks != 0;
+  for (int f = 0; f < o.num_frames; ++f) {
+    enqueue_temporal(st, f);
+    for (int l = 0; l < c.rvq_depth; ++l) {
+      int lo, hi;
+      level_range(c, masked, l, lo, hi);
+      enqueue_depth(st, l, l == 0 ? st->tx : st->din, lo, hi);
+      if (!st->gemv_only) enqueue_sample(st, f, l, o, masked, lo, hi, false);
+    }
+  }
+}
+
+void validate_opts(const mrtdf_stream* st, const mrtdf_gen_opts* o, int seq_len) {
+  const mrtdf_config& c = st->eng->c;
+  if (!o) throw Error{MRTDF_ERR_INVALID, "opts is NULL"};
+  if (o->num_frames <= 0 || o->num_frames > c.max_frames)
+    throw Error{MRTDF_ERR_RANGE, "num_frames must be in [1, max_frames]"};
+  if (o->rvq_depth != c.rvq_depth) throw Error{MRTDF_ERR_INVALID, "rvq_depth must equal the model's rvq_depth"};
+  if (o->temperature < 0.f) throw Error{MRTDF_ERR_INVALID, "temperature must be >= 0"};
+  if (seq_len <= 0 || seq_len > c.max_encoder_length)
+    throw Error{MRTDF_ERR_RANGE, "seq_len exceeds max_encoder_length"};
+  if (!o->use_vocab_masks && (size_t)c.vocab_size * 4 > 160 * 1024)
+    throw Error{MRTDF_ERR_INVALID, "unmasked sampling supports vocab_size <= 40960"};
+}
+
+void upload_ids(mrtdf_stream* st, const int32_t* ids, int S) {
+  const mrtdf_config& c = st->eng->c;
+  for (size_t i = 0; i < (size_t)st->B * S; ++i)
+    if (ids[i] < 0 || ids[i] >= c.vocab_size) throw Error{MRTDF_ERR_INVALID, "token id out of range"};
+  CUDA_OK(cudaMemcpyAsync(st->ids, ids, (size_t)st->B * S * 4, cudaMemcpyHostToDevice, st->s));
+}
+
+void upload_seeds(mrtdf_stream* st, const mrtdf_gen_opts* o, const uint64_t* seeds) {
+  std::vector<uint64_t> h(st->nseq);
+  for (int i = 0; i < st->nseq; ++i) h[i] = seeds ? seeds[i] : o->seed + (uint64_t)i;
+  CUDA_OK(cudaMemcpyAsync(st->seeds, h.data(), h.size() * 8, cudaMemcpyHostToDevice, st->s));
+  CUDA_OK(cudaStreamSynchronize(st->s));  // h is a local
+}
+
+void upload_uniforms(mrtdf_stream* st, const mrtdf_gen_opts* o) {
+  if (!o->uniforms) return;
+  const mrtdf_config& c = st->eng->c;
+  const size_t n = (size_t)st->nseq * o->num_frames * c.rvq_depth * c.vocab_size;
+  if (n > st->uniforms_cap) {
+    if (st->uniforms) cudaFree(st->uniforms);
+    st->uniforms = nullptr;
+    CUDA_OK(cudaMalloc(&st->uniforms, n * 4));
+    st->uniforms_cap = n;
+    for (auto& kv : st->graphs) cudaGraphExecDestroy(kv.second);
+    st->graphs.clear();
+  }
+  CUDA_OK(cudaMemcpyAsync(st->uniforms, o->uniforms, n * 4, cudaMemcpyHostToDevice, st->s));
+}
+
+int read_err(mrtdf_stream* st) {
+  int h = 0;
+  CUDA_OK(cudaMemcpyAsync(&h, st->err, 4, cudaMemcpyDeviceToHost, st->s));
+  CUDA_OK(cudaStreamSynchronize(st->s));
+  if (h) {
+    CUDA_OK(cudaMemsetAsync(st->err, 0, 4, st->s));
+    CUDA_OK(cudaStreamSynchronize(st->s));
+  }
+  return h;
+}
+
+void check_device_err(mrtdf_stream* st) {
+  const int h = read_err(st);
+  if (h & (kErrMbarTimeout | kErrCounterTimeout))
+    throw Error{MRTDF_ERR_TIMEOUT, "a device-side bounded wait gave up (error word " + std::to_string(h) + ")"};
+  if (h & kErrBadToken) throw Error{MRTDF_ERR_INVALID, "a token id outside the vocabulary reached the sampler"};
+}
+
+void run_chunk(mrtdf_stream* st, int S, const mrtdf_gen_opts& o) {
+  GraphKey key{o.num_frames, o.rvq_depth, o.top_k, o.use_vocab_masks, o.uniforms != nullptr, S, o.temperature,
+               o.guidance_weight};
+  const bool use_graph = env_flag("MRTDF_GRAPH", true);
+  if (!use_graph) {
+    enqueue_chunk(st, S, o);
+    return;
+  }
+  auto it = st->graphs.find(key);
+  if (it == st->graphs.end()) {
+    cudaGraph_t g = nullptr;
+    CUDA_OK(cudaStreamBeginCapture(st->s, cudaStreamCaptureModeThreadLocal));
+    try {
+      enqueue_chunk(st, S, o);
+    } catch (...) {
+      cudaStreamEndCapture(st->s, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    CUDA_OK(cudaStreamEndCapture(st->s, &g));
+    cudaGraphExec_t ex = nullptr;
+    const cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    check_cuda(e, "cudaGraphInstantiate");
+    it = st->graphs.emplace(key, ex).first;
+  }
+  CUDA_OK(cudaGraphLaunch(it->second, st->s));
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" {
+
+const char* mrtdf_last_error(void) { return last_error(); }
+
+const char* mrtdf_version(void) { return "mrtdf 0.1.0 sm_100a"; }
+
+int mrtdf_config_preset(const char* name, mrtdf_config* out) {
+  return guarded([&] {
+    if (!name || !out) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    if (!config_preset(name, out)) throw Error{MRTDF_ERR_INVALID, std::string("unknown preset: ") + name};
+  });
+}
+
+int mrtdf_write_random_safetensors(const mrtdf_config* cfg, uint64_t seed, float stddev, int norm_ones,
+                                   const char* path) {
+  return guarded([&] {
+    if (!cfg || !path) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    const std::string why = config_check(*cfg);
+    if (!why.empty()) throw Error{MRTDF_ERR_INVALID, why};
+    auto hw = random_host_weights(*cfg, seed, stddev, norm_ones != 0);
+    std::vector<OutTensor> ts;
+    for (const auto& spec : weight_specs(*cfg)) ts.push_back({spec.key, spec.shape, hw->ptr.at(spec.key)});
+    write_safetensors(path, ts);
+  });
+}
+
+int mrtdf_create(const mrtdf_config* cfg, int device, mrtdf_engine** out) {
+  return guarded([&] {
+    if (!cfg || !out) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    const std::string why = config_check(*cfg);
+    if (!why.empty()) throw Error{MRTDF_ERR_INVALID, why};
+    int n = 0;
+    CUDA_OK(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) throw Error{MRTDF_ERR_INVALID, "no such CUDA device"};
+    CUDA_OK(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    CUDA_OK(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10) throw Error{MRTDF_ERR_CUDA, std::string("built for sm_100a; device is ") + prop.name};
+    auto E = std::make_unique<mrtdf_engine>();
+    E->c = *cfg;
+    E->device = device;
+    E->num_sms = prop.multiProcessorCount;
+    E->esize = cfg->dtype == MRTDF_DTYPE_BF16 ? 2 : 4;
+    E->pdl = env_flag("MRTDF_PDL", true);
+    CUDA_OK(gemv_set_smem_limits());
+    CUDA_OK(gemm_set_smem_limits());
+    CUDA_OK(sample_set_smem_limits());
+    *out = E.release();
+  });
+}
+
+int mrtdf_destroy(mrtdf_engine* eng) {
+  return guarded([&] {
+    if (!eng) return;
+    cudaSetDevice(eng->device);
+    delete eng;
+  });
+}
+
+int mrtdf_load_safetensors(mrtdf_engine* E, const char* path) {
+  return guarded([&] {
+    if (!E || !path) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    CUDA_OK(cudaSetDevice(E->device));
+    SafetensorsFile f(path);
+    std::map<std::string, std::vector<float>> conv;
+    WeightSource src;
+    src.get = [&](const std::string& key, int64_t n) -> const float* {
+      const TensorRef* t = f.find(key);
+      if (!t) throw Error{MRTDF_ERR_KEY, "WeightBundle " + std::string(path) + ": missing key \"" + key + "\""};
+      if (t->numel() != n) throw Error{MRTDF_ERR_INVALID, "shape mismatch for " + key};
+      if (t->dtype == "F32") return reinterpret_cast<const float*>(t->data);
+      auto& v = conv[key];
+      v.resize((size_t)n);
+      const uint16_t* s = reinterpret_cast<const uint16_t*>(t->data);
+      for (int64_t i = 0; i < n; ++i) {
+        const uint32_t u = (uint32_t)s[i] << 16;
+        std::memcpy(&v[(size_t)i], &u, 4);
+      }
+      return v.data();
+    };
+    upload_weights(E, src);
+  });
+}
+
+int mrtdf_load_random(mrtdf_engine* E, uint64_t seed, float stddev, int norm_ones) {
+  return guarded([&] {
+    if (!E) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    CUDA_OK(cudaSetDevice(E->device));
+    auto hw = random_host_weights(E->c, seed, stddev, norm_ones != 0);
+    WeightSource src;
+    src.get = [&](const std::string& key, int64_t n) -> const float* {
+      auto it = hw->ptr.find(key);
+      if (it == hw->ptr.end()) throw Error{MRTDF_ERR_KEY, "missing key \"" + key + "\""};
+      (void)n;
+      return it->second;
+    };
+    upload_weights(E, src);
+  });
+}
+
+int mrtdf_stream_create(mrtdf_engine* E, int num_sequences, int cfg, mrtdf_stream** out) {
+  return guarded([&] {
+    if (!E || !out) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    if (!E->loaded) throw Error{MRTDF_ERR_STATE, "load weights before creating a stream"};
+    if (num_sequences <= 0) throw Error{MRTDF_ERR_INVALID, "num_sequences must be positive"};
+    const int rps = cfg ? 2 : 1;
+    if (num_sequences * rps > kGemvMaxB)
+      throw Error{MRTDF_ERR_INVALID, "rows per step (num_sequences * (cfg ? 2 : 1)) must be <= 8"};
+    CUDA_OK(cudaSetDevice(E->device));
+    const mrtdf_config& c = E->c;
+    auto st = std::make_unique<mrtdf_stream>();
+    st->eng = E;
+    st->nseq = num_sequences;
+    st->rps = rps;
+    st->B = num_sequences * rps;
+    CUDA_OK(cudaStreamCreateWithFlags(&st->s, cudaStreamNonBlocking));
+    const size_t B = st->B, d = c.d_model, in = E->inner(), ff = c.d_ff, V = c.vocab_size, H = c.num_heads;
+    const size_t es = E->esize;
+    const size_t Mx = B * c.max_encoder_length;
+    std::vector<std::pair<void**, size_t>> plan = {
+        {&st->tx, B * d * es}, {&st->dx, B * d * es}, {&st->tin, B * d * es}, {&st->din, B * d * es},
+        {&st->fsum, B * d * es}, {&st->qb, B * in * es}, {&st->ao, B * in * es}, {&st->hb, B * ff * es},
+        {(void**)&st->logits, B * V * 4}, {(void**)&st->stage_f32, B * std::max(d, V) * 4},
+        {&st->tk, c.num_temporal_layers * B * H * c.max_frames * 64 * es},
+        {&st->tv, c.num_temporal_layers * B * H * c.max_frames * 64 * es},
+        {&st->ck, c.num_temporal_layers * B * H * c.max_encoder_length * 64 * es},
+        {&st->cv, c.num_temporal_layers * B * H * c.max_encoder_length * 64 * es},
+        {&st->dk, c.num_depth_layers * B * H * c.rvq_depth * 64 * es},
+        {&st->dv, c.num_depth_layers * B * H * c.rvq_depth * 64 * es},
+        {&st->ex, Mx * d * es}, {&st->en, Mx * d * es}, {&st->eqkv, Mx * 3 * in * es}, {&st->eo, Mx * in * es},
+        {&st->eh, Mx * ff * es}, {(void**)&st->ids, Mx * 4},
+        {(void**)&st->tokens, (size_t)num_sequences * c.max_frames * c.rvq_depth * 4},
+        {(void**)&st->seeds, (size_t)num_sequences * 8}, {(void**)&st->forced, (size_t)num_sequences * 4},
+        {(void**)&st->part, B * H * kCrossSplit * 66 * 4}, {(void**)&st->counters, B * H * 4},
+        {(void**)&st->err, 64}};
+    size_t total = 0;
+    for (auto& p : plan) total += (p.second + 255) & ~(size_t)255;
+    st->mem.reserve(total);
+    for (auto& p : plan) *p.first = st->mem.take(p.second);
+    CUDA_OK(cudaMemsetAsync(st->mem.base, 0, st->mem.cap, st->s));
+    CUDA_OK(cudaStreamSynchronize(st->s));
+    *out = st.release();
+  });
+}
+
+int mrtdf_stream_destroy(mrtdf_stream* st) {
+  return guarded([&] {
+    if (!st) return;
+    cudaSetDevice(st->eng->device);
+    cudaStreamSynchronize(st->s);
+    if (st->uniforms) cudaFree(st->uniforms);
+    delete st;
+  });
+}
+
+int mrtdf_stream_rows(const mrtdf_stream* st) { return st ? st->B : 0; }
+
+void* mrtdf_stream_cuda(mrtdf_stream* st) { return st ? (void*)st->s : nullptr; }
+
+int mrtdf_stream_sync(mrtdf_stream* st) {
+  return guarded([&] {
+    if (!st) throw Error{MRTDF_ERR_INVALID, "NULL stream"};
+    CUDA_OK(cudaSetDevice(st->eng->device));
+    CUDA_OK(cudaStreamSynchronize(st->s));
+    check_device_err(st);
+  });
+}
+
+int mrtdf_encode(mrtdf_stream* st, const int32_t* ids, int seq_len, float* enc_out) {
+  return guarded([&] {
+    if (!st || !ids) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    mrtdf_engine* E = st->eng;
+    if (seq_len <= 0 || seq_len > E->c.max_encoder_length)
+      throw Error{MRTDF_ERR_RANGE, "seq_len exceeds max_encoder_length"};
+    CUDA_OK(cudaSetDevice(E->device));
+    upload_ids(st, ids, seq_len);
+    enqueue_encode(st, seq_len);
+    st->S = seq_len;
+    st->encoded = true;
+    st->t_len = 0;
+    st->d_len = 0;
+    st->have_temporal = false;
+    if (enc_out) {
+      const size_t n = (size_t)st->B * seq_len * E->c.d_model;
+      float* tmp = nullptr;
+      CUDA_OK(cudaMalloc(&tmp, n * 4));
+      check_cuda(launch_act_to_f32(E->c.dtype, st->en, n, tmp, st->s), "convert");
+      CUDA_OK(cudaMemcpyAsync(enc_out, tmp, n * 4, cudaMemcpyDeviceToHost, st->s));
+      CUDA_OK(cudaStreamSynchronize(st->s));
+      cudaFree(tmp);
+    }
+    CUDA_OK(cudaStreamSynchronize(st->s));
+    check_device_err(st);
+  });
+}
+
+static void upload_act(mrtdf_stream* st, const float* x, void* dst) {
+  mrtdf_engine* E = st->eng;
+  const size_t n = (size_t)st->B * E->c.d_model;
+  CUDA_OK(cudaMemcpyAsync(st->stage_f32, x, n * 4, cudaMemcpyHostToDevice, st->s));
+  check_cuda(launch_f32_to_act(E->c.dtype, st->stage_f32, n, dst, st->s), "convert");
+}
+
+static void download_act(mrtdf_stream* st, const void* src, float* out) {
+  mrtdf_engine* E = st->eng;
+  const size_t n = (size_t)st->B * E->c.d_model;
+  check_cuda(launch_act_to_f32(E->c.dtype, src, n, st->stage_f32, st->s), "convert");
+  CUDA_OK(cudaMemcpyAsync(out, st->stage_f32, n * 4, cudaMemcpyDeviceToHost, st->s));
+}
+
+int mrtdf_temporal_step(mrtdf_stream* st, const float* x, int frame_idx, float* out) {
+  return guarded([&] {
+    if (!st) throw Error{MRTDF_ERR_INVALID, "NULL stream"};
+    mrtdf_engine* E = st->eng;
+    if (!st->encoded) throw Error{MRTDF_ERR_STATE, "temporal_step: call encode first (no cross-attention cache)"};
+    if (frame_idx < 0 || frame_idx >= E->c.max_frames) throw Error{MRTDF_ERR_RANGE, "frame_idx out of range"};
+    if (frame_idx != st->t_len) throw Error{MRTDF_ERR_STATE, "temporal_step: cache size mismatch"};
+    CUDA_OK(cudaSetDevice(E->device));
+    if (x) upload_act(st, x, st->tin);
+    else check_cuda(launch_embed_rows(E->c.dtype, E->emb, nullptr, st->B, E->c.d_model, st->tin, st->s, false), "pad");
+    enqueue_temporal(st, frame_idx);
+    st->t_len = frame_idx + 1;
+    st->have_temporal = true;
+    if (out) download_act(st, st->tx, out);
+    CUDA_OK(cudaStreamSynchronize(st->s));
+    check_device_err(st);
+  });
+}
+
+int mrtdf_depth_step(mrtdf_stream* st, const float* x, int depth_idx, float* logits) {
+  return guarded([&] {
+    if (!st) throw Error{MRTDF_ERR_INVALID, "NULL stream"};
+    mrtdf_engine* E = st->eng;
+    const mrtdf_config& c = E->c;
+    if (depth_idx < 0 || depth_idx >= c.rvq_depth) throw Error{MRTDF_ERR_RANGE, "depth_idx out of range"};
+    if (depth_idx != 0 && depth_idx != st->d_len) throw Error{MRTDF_ERR_STATE, "depth_step: cache size mismatch"};
+    CUDA_OK(cudaSetDevice(E->device));
+    const void* in;
+    if (x) {
+      upload_act(st, x, st->din);
+      in = st->din;
+    } else {
+      if (!st->have_temporal) throw Error{MRTDF_ERR_STATE, "depth_step: no temporal output to start from"};
+      in = st->tx;
+    }
+    enqueue_depth(st, depth_idx, in, 0, c.vocab_size);
+    st->d_len = depth_idx + 1;
+    if (logits)
+      CUDA_OK(cudaMemcpyAsync(logits, st->logits, (size_t)st->B * c.vocab_size * 4, cudaMemcpyDeviceToHost, st->s));
+    CUDA_OK(cudaStreamSynchronize(st->s));
+    check_device_err(st);
+  });
+}
+
+int mrtdf_token_embedding(mrtdf_engine* E, const int32_t* ids, int n, float* out) {
+  return guarded([&] {
+    if (!E || !ids || !out || n <= 0) throw Error{MRTDF_ERR_INVALID, "bad argument"};
+    if (!E->loaded) throw Error{MRTDF_ERR_STATE, "weights not loaded"};
+    for (int i = 0; i < n; ++i)
+      if (ids[i] < 0 || ids[i] >= E->c.vocab_size) throw Error{MRTDF_ERR_INVALID, "token id out of range"};
+    CUDA_OK(cudaSetDevice(E->device));
+    const size_t dn = (size_t)n * E->c.d_model;
+    int32_t* dids = nullptr;
+    void* act = nullptr;
+    float* f = nullptr;
+    CUDA_OK(cudaMalloc(&dids, (size_t)n * 4));
+    CUDA_OK(cudaMalloc(&act, dn * E->esize));
+    CUDA_OK(cudaMalloc(&f, dn * 4));
+    CUDA_OK(cudaMemcpy(dids, ids, (size_t)n * 4, cudaMemcpyHostToDevice));
+    check_cuda(launch_embed_rows(E->c.dtype, E->emb, dids, n, E->c.d_model, act, 0, false), "embed");
+    check_cuda(launch_act_to_f32(E->c.dtype, act, dn, f, 0), "convert");
+    CUDA_OK(cudaMemcpy(out, f, dn * 4, cudaMemcpyDeviceToHost));
+    cudaFree(dids);
+    cudaFree(act);
+    cudaFree(f);
+  });
+}
+
+int mrtdf_sample(mrtdf_engine* E, const float* logits, int cfg, int frame, int level, const mrtdf_gen_opts* o,
+                 const float* uniforms, int32_t* token) {
+  return guarded([&] {
+    if (!E || !logits || !o || !token) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    if (!E->loaded) throw Error{MRTDF_ERR_STATE, "weights not loaded"};
+    const mrtdf_config& c = E->c;
+    if (level < 0 || level >= c.rvq_depth || frame < 0) throw Error{MRTDF_ERR_RANGE, "level / frame out of range"};
+    if (!o->use_vocab_masks && (size_t)c.vocab_size * 4 > 160 * 1024)
+      throw Error{MRTDF_ERR_INVALID, "unmasked sampling supports vocab_size <= 40960"};
+    CUDA_OK(cudaSetDevice(E->device));
+    const int rows = cfg ? 2 : 1;
+    const size_t V = c.vocab_size, d = c.d_model;
+    float *dl = nullptr, *du = nullptr;
+    uint64_t* ds = nullptr;
+    int32_t* dt = nullptr;
+    void *din = nullptr, *fs = nullptr, *tin = nullptr;
+    int* err = nullptr;
+    CUDA_OK(cudaMalloc(&dl, rows * V * 4));
+    CUDA_OK(cudaMalloc(&ds, 8));
+    CUDA_OK(cudaMalloc(&dt, 4));
+    CUDA_OK(cudaMalloc(&din, rows * d * E->esize));
+    CUDA_OK(cudaMalloc(&fs, rows * d * E->esize));
+    CUDA_OK(cudaMalloc(&tin, rows * d * E->esize));
+    CUDA_OK(cudaMalloc(&err, 4));
+    CUDA_OK(cudaMemset(err, 0, 4));
+    CUDA_OK(cudaMemcpy(dl, logits, rows * V * 4, cudaMemcpyHostToDevice));
+    CUDA_OK(cudaMemcpy(ds, &o->seed, 8, cudaMemcpyHostToDevice));
+    if (uniforms) {
+      CUDA_OK(cudaMalloc(&du, V * 4));
+      CUDA_OK(cudaMemcpy(du, uniforms, V * 4, cudaMemcpyHostToDevice));
+    }
+    int lo, hi;
+    level_range(c, o->use_vocab_masks != 0, level, lo, hi);
+    SampleParams sp{};
+    sp.logits = dl; sp.logits_stride = (int)V; sp.col_offset = 0; sp.lo = lo; sp.hi = hi; sp.rows_per_seq = rows;
+    sp.w = o->guidance_weight; sp.temperature = o->temperature; sp.top_k = o->top_k; sp.seeds = ds;
+    sp.step = (uint32_t)(frame * c.rvq_depth + level);
+    sp.uniforms = du;  // one row of V draws for this step
+    sp.uni_seq_stride = 0; sp.forced = nullptr; sp.tokens = dt; sp.tok_stride = 0; sp.tok_index = 0;
+    sp.emb = E->emb; sp.d = (int)d; sp.V = (int)V; sp.din = din; sp.fsum = fs; sp.tin = tin; sp.depth = c.rvq_depth;
+    sp.is_first = 1; sp.is_last = 0; sp.err = err;
+    check_cuda(launch_sample(c.dtype, sp, 1, 0, false), "sample");
+    CUDA_OK(cudaMemcpy(token, dt, 4, cudaMemcpyDeviceToHost));
+    cudaFree(dl); cudaFree(ds); cudaFree(dt); cudaFree(din); cudaFree(fs); cudaFree(tin); cudaFree(err);
+    if (du) cudaFree(du);
+  });
+}
+
+int mrtdf_generate_tokens_dev(mrtdf_stream* st, const int32_t* enc_ids_dev, int seq_len, const mrtdf_gen_opts* o,
+                              const uint64_t* seeds, int32_t* out_ids_dev) {
+  return guarded([&] {
+    if (!st || !enc_ids_dev || !out_ids_dev) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    validate_opts(st, o, seq_len);
+    mrtdf_engine* E = st->eng;
+    const mrtdf_config& c = E->c;
+    CUDA_OK(cudaSetDevice(E->device));
+    CUDA_OK(cudaMemcpyAsync(st->ids, enc_ids_dev, (size_t)st->B * seq_len * 4, cudaMemcpyDeviceToDevice, st->s));
+    upload_seeds(st, o, seeds);
+    upload_uniforms(st, o);
+    st->S = seq_len;
+    run_chunk(st, seq_len, *o);
+    // tokens (nseq, max_frames, depth) -> out (nseq, num_frames, depth)
+    CUDA_OK(cudaMemcpy2DAsync(out_ids_dev, (size_t)o->num_frames * c.rvq_depth * 4, st->tokens,
+                              (size_t)c.max_frames * c.rvq_depth * 4, (size_t)o->num_frames * c.rvq_depth * 4,
+                              st->nseq, cudaMemcpyDeviceToDevice, st->s));
+    st->encoded = true;
+    st->t_len = o->num_frames;
+    st->d_len = c.rvq_depth;
+    st->have_temporal = true;
+  });
+}
+
+int mrtdf_generate_tokens(mrtdf_stream* st, const int32_t* enc_ids, int seq_len, const mrtdf_gen_opts* o,
+                          const uint64_t* seeds, int32_t* out_ids) {
+  return guarded([&] {
+    if (!st || !enc_ids || !out_ids) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    validate_opts(st, o, seq_len);
+    mrtdf_engine* E = st->eng;
+    const mrtdf_config& c = E->c;
+    CUDA_OK(cudaSetDevice(E->device));
+    upload_ids(st, enc_ids, seq_len);
+    upload_seeds(st, o, seeds);
+    upload_uniforms(st, o);
+    st->S = seq_len;
+    run_chunk(st, seq_len, *o);
+    CUDA_OK(cudaMemcpy2DAsync(out_ids, (size_t)o->num_frames * c.rvq_depth * 4, st->tokens,
+                              (size_t)c.max_frames * c.rvq_depth * 4, (size_t)o->num_frames * c.rvq_depth * 4,
+                              st->nseq, cudaMemcpyDeviceToHost, st->s));
+    CUDA_OK(cudaStreamSynchronize(st->s));
+    check_device_err(st);
+    st->encoded = true;
+    st->t_len = o->num_frames;
+    st->d_len = c.rvq_depth;
+    st->have_temporal = true;
+  });
+}
+
+int mrtdf_teacher_forced_logits(mrtdf_stream* st, const int32_t* enc_ids, int seq_len, const int32_t* tokens,
+                                int num_frames, float* logits) {
+  return guarded([&] {
+    if (!st || !enc_ids || !tokens || !logits) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    if (st->nseq != 1) throw Error{MRTDF_ERR_INVALID, "teacher forcing needs a single-sequence stream"};
+    mrtdf_engine* E = st->eng;
+    const mrtdf_config& c = E->c;
+    if (num_frames <= 0 || num_frames > c.max_frames) throw Error{MRTDF_ERR_RANGE, "num_frames out of range"};
+    if (seq_len <= 0 || seq_len > c.max_encoder_length) throw Error{MRTDF_ERR_RANGE, "seq_len out of range"};
+    for (int i = 0; i < num_frames * c.rvq_depth; ++i)
+      if (tokens[i] < 0 || tokens[i] >= c.vocab_size) throw Error{MRTDF_ERR_INVALID, "forced token out of range"};
+    CUDA_OK(cudaSetDevice(E->device));
+    upload_ids(st, enc_ids, seq_len);
+    st->S = seq_len;
+    mrtdf_gen_opts o{};
+    o.num_frames = num_frames;
+    o.rvq_depth = c.rvq_depth;
+    upload_seeds(st, &o, nullptr);
+    enqueue_encode(st, seq_len);
+    check_cuda(launch_embed_rows(c.dtype, E->emb, nullptr, st->B, c.d_model, st->tin, st->s, false), "pad");
+    const size_t V = c.vocab_size;
+    for (int f = 0; f < num_frames; ++f) {
+      enqueue_temporal(st, f);
+      for (int l = 0; l < c.rvq_depth; ++l) {
+        enqueue_depth(st, l, l == 0 ? st->tx : st->din, 0, c.vocab_size);
+        CUDA_OK(cudaMemcpyAsync(logits + ((size_t)f * c.rvq_depth + l) * st->B * V, st->logits,
+                                (size_t)st->B * V * 4, cudaMemcpyDeviceToHost, st->s));
+        const int32_t tok = tokens[(size_t)f * c.rvq_depth + l];
+        CUDA_OK(cudaMemcpyAsync(st->forced, &tok, 4, cudaMemcpyHostToDevice, st->s));
+        enqueue_sample(st, f, l, o, false, 0, c.vocab_size, true);
+        CUDA_OK(cudaStreamSynchronize(st->s));  // `tok` is a local
+      }
+    }
+    CUDA_OK(cudaStreamSynchronize(st->s));
+    check_device_err(st);
+    st->encoded = true;
+    st->t_len = num_frames;
+    st->d_len = c.rvq_depth;
+    st->have_temporal = true;
+  });
+}
+
+int mrtdf_bench_gemv(mrtdf_stream* st, const mrtdf_gen_opts* o, int reps, float* ms_per_rep,
+                     long long* launches_per_rep, double* bytes_per_rep) {
+  return guarded([&] {
+    if (!st || !o || reps <= 0 || !ms_per_rep || !launches_per_rep || !bytes_per_rep)
+      throw Error{MRTDF_ERR_INVALID, "bad argument"};
+    if (!st->encoded) throw Error{MRTDF_ERR_STATE, "run a chunk (or encode) first"};
+    validate_opts(st, o, st->S);
+    CUDA_OK(cudaSetDevice(st->eng->device));
+    cudaGraph_t g = nullptr;
+    st->gemv_only = true;
+    st->gemv_launches = 0;
+    st->gemv_bytes = 0.0;
+    CUDA_OK(cudaStreamBeginCapture(st->s, cudaStreamCaptureModeThreadLocal));
+    try {
+      enqueue_chunk(st, st->S, *o);
+    } catch (...) {
+      st->gemv_only = false;
+      cudaStreamEndCapture(st->s, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    st->gemv_only = false;
+    CUDA_OK(cudaStreamEndCapture(st->s, &g));
+    cudaGraphExec_t ex = nullptr;
+    const cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    check_cuda(e, "cudaGraphInstantiate");
+    cudaEvent_t a, b;
+    CUDA_OK(cudaEventCreate(&a));
+    CUDA_OK(cudaEventCreate(&b));
+    CUDA_OK(cudaGraphLaunch(ex, st->s));  // warm-up
+    CUDA_OK(cudaEventRecord(a, st->s));
+    for (int r = 0; r < reps; ++r) CUDA_OK(cudaGraphLaunch(ex, st->s));
+    CUDA_OK(cudaEventRecord(b, st->s));
+    CUDA_OK(cudaEventSynchronize(b));
+    float ms = 0.f;
+    CUDA_OK(cudaEventElapsedTime(&ms, a, b));
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    cudaGraphExecDestroy(ex);
+    *ms_per_rep = ms / reps;
+    *launches_per_rep = st->gemv_launches;
+    *bytes_per_rep = st->gemv_bytes;
+    check_device_err(st);
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,825 @@
+// TEST INFRASTRUCTURE ONLY.
+//
+// CPU oracle for the Depthformer chunk-decoding hot path: a plain C++
+// restatement of the reference's eager MLX code, used by tests/ (parity
+// checks against the CUDA engine), by bench.py's `cpu_baseline` and
+// `--impl reference` legs (timed CPU baseline) and by
+// __graft_entry__.smoke(). The engine never links, loads or calls it.
+//
+// Reference: rhymeswithlion/magenta-realtime-mlx-cpp (v0.1.0). The reference
+// cannot be built here (it needs MLX 0.31.1, absent with no network), so
+// this file restates it; every function names the lines it follows.
+// Parity status: the integer/index parts (vocab ranges, relative-position
+// buckets, encoder-input layout, context roll, RVQ id maps, sinusoid table,
+// CFG formula) are pinned to the reference's own known answers (tests/
+// test_oracle_kat.py); the floating-point transformer numerics are
+// **parity unpinned** - no reference test or runnable reference pins
+// logits, so the oracle follows the code line by line instead.
+//
+// Two numeric modes:
+//   fp32 - every op in float32.
+//   bf16 - MLX's bf16 semantics: weights rounded to bf16 at load
+//          (modules.cpp:47-54) and every op output rounded to bf16
+//          (round-to-nearest-even); reductions inside matmul, rms_norm and
+//          SDPA accumulate in float32. Rounding points are marked R(...).
+//
+// Built by oracle/build_oracle.py into oracle/_build/liboracle.so with
+// -O3 -march=x86-64-v3 -fopenmp.
+
+#include <fcntl.h>
+#include <omp.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <limits>
+#include <map>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "oracle.h"
+
+namespace oracle {
+
+static thread_local std::string g_err;
+
+// ---------------------------------------------------------------------------
+// Configuration: the field order of mrtdf_config (include/mrtdf.h), which
+// mirrors DepthformerConfig (depthformer/model.h:47-68).
+// ---------------------------------------------------------------------------
+struct Cfg {
+  int V, d, dk, dff, H, Le, Lt, Ld, Smax, depth, tnb, tmd, dnb, dmd, cb, off, Tmax, dtype;
+  int inner() const { return H * dk; }
+};
+
+static Cfg cfg_from_ints(const int* c) {
+  Cfg k;
+  int* dst = &k.V;
+  for (int i = 0; i < 18; ++i) dst[i] = c[i];
+  return k;
+}
+
+// ---------------------------------------------------------------------------
+// safetensors reader (the format MLX's load_safetensors reads,
+// weights.cpp:29-35): 8-byte little-endian header length, JSON header,
+// raw little-endian tensor bytes. F32 and BF16 tensors are accepted.
+// ---------------------------------------------------------------------------
+struct TensorInfo {
+  std::string dtype;
+  std::vector<int64_t> shape;
+  uint64_t begin = 0, end = 0;
+};
+
+struct JsonCursor {
+  const char* p;
+  const char* e;
+  void ws() { while (p < e && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p; }
+  bool eat(char c) { ws(); if (p < e && *p == c) { ++p; return true; } return false; }
+  void need(char c) { if (!eat(c)) throw std::runtime_error(std::string("safetensors header: expected '") + c + "'"); }
+  std::string str() {
+    ws();
+    if (p >= e || *p != '"') throw std::runtime_error("safetensors header: expected string");
+    ++p;
+    std::string out;
+    while (p < e && *p != '"') {
+      if (*p == '\\' && p + 1 < e) { ++p; }
+      out.push_back(*p++);
+    }
+    if (p >= e) throw std::runtime_error("safetensors header: unterminated string");
+    ++p;
+    return out;
+  }
+  int64_t num() {
+    ws();
+    char* q = nullptr;
+    long long v = std::strtoll(p, &q, 10);
+    if (q == p) throw std::runtime_error("safetensors header: expected number");
+    p = q;
+    return v;
+  }
+  void skip_value() {
+    ws();
+    if (p >= e) throw std::runtime_error("safetensors header: truncated");
+    if (*p == '"') { str(); return; }
+    if (*p == '{') {
+      ++p;
+      if (eat('}')) return;
+      do { str(); need(':'); skip_value(); } while (eat(','));
+      need('}');
+      return;
+    }
+    if (*p == '[') {
+      ++p;
+      if (eat(']')) return;
+      do { skip_value(); } while (eat(','));
+      need(']');
+      return;
+    }
+    while (p < e && *p != ',' && *p != '}' && *p != ']') ++p;
+  }
+};
+
+struct SafeTensors {
+  std::map<std::string, TensorInfo> info;
+  const uint8_t* data = nullptr;
+  size_t data_size = 0;
+  void* map = nullptr;
+  size_t map_size = 0;
+
+  explicit SafeTensors(const char* path) {
+    int fd = ::open(path, O_RDONLY);
+    if (fd < 0) throw std::runtime_error(std::string("cannot open ") + path);
+    struct stat st;
+    if (fstat(fd, &st) != 0 || st.st_size < 8) { ::close(fd); throw std::runtime_error("bad safetensors file"); }
+    map_size = (size_t)st.st_size;
+    map = mmap(nullptr, map_size, PROT_READ, MAP_PRIVATE, fd, 0);
+    ::close(fd);
+    if (map == MAP_FAILED) { map = nullptr; throw std::runtime_error("mmap failed"); }
+    const uint8_t* b = (const uint8_t*)map;
+    uint64_t hlen = 0;
+    std::memcpy(&hlen, b, 8);
+    if (hlen + 8 > map_size) throw std::runtime_error("safetensors header length out of range");
+    JsonCursor c{(const char*)b + 8, (const char*)b + 8 + hlen};
+    c.need('{');
+    if (!c.eat('}')) {
+      do {
+        std::string key = c.str();
+        c.need(':');
+        if (key == "__metadata__") { c.skip_value(); continue; }
+        TensorInfo ti;
+        c.need('{');
+        do {
+          std::string f = c.str();
+          c.need(':');
+          if (f == "dtype") ti.dtype = c.str();
+          else if (f == "shape") {
+            c.need('[');
+            if (!c.eat(']')) { do { ti.shape.push_back(c.num()); } while (c.eat(',')); c.need(']'); }
+          } else if (f == "data_offsets") {
+            c.need('['); ti.begin = (uint64_t)c.num(); c.need(','); ti.end = (uint64_t)c.num(); c.need(']');
+          } else c.skip_value();
+        } while (c.eat(','));
+        c.need('}');
+        info[key] = ti;
+      } while (c.eat(','));
+      c.need('}');
+    }
+    data = b + 8 + hlen;
+    data_size = map_size - 8 - hlen;
+  }
+  ~SafeTensors() { if (map) munmap(map, map_size); }
+
+  // Tensor `key` as float32, checking the element count (weights.cpp:37-44
+  // throws std::out_of_range for a missing key).
+  std::vector<float> get(const std::string& key, int64_t expect_numel) const {
+    auto it = info.find(key);
+    if (it == info.end()) throw std::out_of_range("missing key \"" + key + "\"");
+    const TensorInfo& t = it->second;
+    int64_t n = 1;
+    for (auto s : t.shape) n *= s;
+    if (n != expect_numel) throw std::runtime_error("shape mismatch for " + key);
+    if (t.end > data_size || t.begin > t.end) throw std::runtime_error("offsets out of range for " + key);
+    std::vector<float> out((size_t)n);
+    if (t.dtype == "F32") {
+      if (t.end - t.begin != (uint64_t)n * 4) throw std::runtime_error("size mismatch for " + key);
+      std::memcpy(out.data(), data + t.begin, (size_t)n * 4);
+    } else if (t.dtype == "BF16") {
+      if (t.end - t.begin != (uint64_t)n * 2) throw std::runtime_error("size mismatch for " + key);
+      const uint16_t* s = (const uint16_t*)(data + t.begin);
+      for (int64_t i = 0; i < n; ++i) { uint32_t u = (uint32_t)s[i] << 16; std::memcpy(&out[i], &u, 4); }
+    } else {
+      throw std::runtime_error("unsupported dtype " + t.dtype + " for " + key);
+    }
+    return out;
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Numeric helpers
+// ---------------------------------------------------------------------------
+struct Round {
+  bool bf;
+  float operator()(float x) const { return bf ? bf16_round(x) : x; }
+  void vec(float* x, size_t n) const { if (bf) for (size_t i = 0; i < n; ++i) x[i] = bf16_round(x[i]); }
+};
+
+typedef float v8f __attribute__((vector_size(32)));
+
+static inline v8f load8(const float* p) { v8f v; std::memcpy(&v, p, 32); return v; }
+static inline float hsum8(v8f v) {
+  float s = 0.f;
+  for (int i = 0; i < 8; ++i) s += v[i];
+  return s;
+}
+
+static inline float dot(const float* a, const float* b, int K) {
+  v8f acc = {0, 0, 0, 0, 0, 0, 0, 0};
+  int k = 0;
+  for (; k + 8 <= K; k += 8) acc += load8(a + k) * load8(b + k);
+  float s = hsum8(acc);
+  for (; k < K; ++k) s += a[k] * b[k];
+  return s;
+}
+
+// C[m][n] = sum_k A[m][k] * W[n][k] (Linear::operator(), modules.cpp:98-100:
+// y = x @ W^T with W stored (out, in)). float32 accumulation.
+static void gemm_nt(const float* A, int M, int K, const float* W, int N, float* C) {
+  const int NB = 64;
+  const int nblk = (N + NB - 1) / NB;
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int jb = 0; jb < nblk; ++jb) {
+    const int j0 = jb * NB, j1 = std::min(N, j0 + NB);
+    for (int i0 = 0; i0 < M; i0 += 4) {
+      const int mi = std::min(4, M - i0);
+      for (int j = j0; j < j1; j += 4) {
+        const int nj = std::min(4, j1 - j);
+        if (mi == 4 && nj == 4 && (K % 8) == 0) {
+          v8f acc[4][4];
+          for (int a = 0; a < 4; ++a)
+            for (int b = 0; b < 4; ++b) acc[a][b] = (v8f){0, 0, 0, 0, 0, 0, 0, 0};
+          const float* a0 = A + (size_t)i0 * K;
+          const float* w0 = W + (size_t)j * K;
+          for (int k = 0; k < K; k += 8) {
+            v8f av[4], wv[4];
+            for (int a = 0; a < 4; ++a) av[a] = load8(a0 + (size_t)a * K + k);
+            for (int b = 0; b < 4; ++b) wv[b] = load8(w0 + (size_t)b * K + k);
+            for (int a = 0; a < 4; ++a)
+              for (int b = 0; b < 4; ++b) acc[a][b] += av[a] * wv[b];
+          }
+          for (int a = 0; a < 4; ++a)
+            for (int b = 0; b < 4; ++b) C[(size_t)(i0 + a) * N + j + b] = hsum8(acc[a][b]);
+        } else {
+          for (int a = 0; a < mi; ++a)
+            for (int b = 0; b < nj; ++b)
+              C[(size_t)(i0 + a) * N + j + b] = dot(A + (size_t)(i0 + a) * K, W + (size_t)(j + b) * K, K);
+        }
+      }
+    }
+  }
+}
+
+// Linear applied to M rows, output rounded to the compute dtype.
+struct Lin {
+  int out = 0, in = 0;
+  std::vector<float> w;  // (out, in), the file layout
+  void apply(const float* x, int M, float* y, const Round& R) const {
+    gemm_nt(x, M, in, w.data(), out, y);
+    R.vec(y, (size_t)M * out);
+  }
+};
+
+// RMSNorm (modules.cpp:62-84, eps 1e-6 at modules.cpp:342-346): MLX's
+// fast::rms_norm computes r = rsqrt(mean(x^2) + eps) in float32 and writes
+// w * (T)(x * r), i.e. R(w * R(x * r)).
+static void rms_norm(const float* x, int M, int d, const std::vector<float>& w, float* y, const Round& R) {
+  for (int m = 0; m < M; ++m) {
+    const float* xr = x + (size_t)m * d;
+    float acc = 0.f;
+    for (int i = 0; i < d; ++i) acc += xr[i] * xr[i];
+    const float r = 1.0f / std::sqrt(acc / (float)d + 1e-6f);
+    float* yr = y + (size_t)m * d;
+    for (int i = 0; i < d; ++i) yr[i] = R(w[i] * R(xr[i] * r));
+  }
+}
+
+// gelu_approx (nn_ops.h:66-84): constants cast to the input dtype, every
+// op of the compiled chain rounded to that dtype:
+// 0.5 * (x * (1 + tanh(c0 * (x * (1 + c1 * x^2))))).
+static inline float gelu_approx(float x, const Round& R) {
+  const float c0 = R(0.7978845608028654f), c1 = R(0.044715f);
+  const float x2 = R(x * x);
+  const float t1 = R(c1 * x2);
+  const float t2 = R(1.0f + t1);
+  const float t3 = R(x * t2);
+  const float inner = R(c0 * t3);
+  const float th = R(std::tanh(inner));
+  const float u = R(1.0f + th);
+  const float v = R(x * u);
+  return R(0.5f * v);
+}
+
+// T5 relative-position bucket, unidirectional (modules.cpp:139-174):
+// n = max(-(k - q), 0); exact below max_exact = nb/2, log-spaced above,
+// capped at nb - 1. float32 log as in mx::log.
+int relative_bucket(int rel, int num_buckets, int max_distance) {
+  int n = -rel;
+  if (n < 0) n = 0;
+  const int eff = num_buckets;
+  const int max_exact = eff / 2;
+  if (n < max_exact) return n;
+  const float log_ratio = std::log((float)max_distance / (float)max_exact);
+  const float v = (float)max_exact + (std::log((float)n / (float)max_exact) / log_ratio) * (float)(eff - max_exact);
+  int b = (int)v;  // astype(int32) truncates toward zero
+  return std::min(b, eff - 1);
+}
+
+// ---------------------------------------------------------------------------
+// Model
+// ---------------------------------------------------------------------------
+struct EncLayer {
+  std::vector<float> n_attn, n_ffn;
+  Lin q, k, v, o, wi0, wi1, wo;
+};
+struct DecLayer {
+  bool cross = false;
+  std::vector<float> n_self, n_cross, n_ffn;
+  Lin q, k, v, o, cq, ck, cv, co, wi0, wi1, wo;
+};
+
+struct Model {
+  Cfg c;
+  Round R;
+  std::vector<float> emb;  // (V, d)
+  std::vector<float> pe;   // (Smax, d) float32 (model.cpp:54-80)
+  std::vector<EncLayer> enc;
+  std::vector<float> enc_norm;
+  std::vector<float> trel, drel;  // (nb, H)
+  std::vector<DecLayer> tl, dl;
+  std::vector<float> dec_norm;
+  Lin lm;
+
+  // decode state (one stream of B rows)
+  int B = 0, S = 0;
+  bool encoded = false;
+  int t_len = 0, d_len = 0;
+  std::vector<float> enc_out;                    // (B, S, d)
+  std::vector<std::vector<float>> ck, cv;        // per temporal layer (B, H, S, dk)
+  std::vector<std::vector<float>> tk, tv;        // per temporal layer (B, H, Tmax, dk)
+  std::vector<std::vector<float>> dk_, dv_;      // per depth layer (B, H, depth, dk)
+  std::vector<float> last_temporal;              // (B, d)
+};
+
+static std::vector<float> sinusoid_table(int max_length, int features) {
+  // build_sinusoidal_position_embedding (model.cpp:54-80), float32 on host.
+  std::vector<float> data((size_t)max_length * features, 0.f);
+  const int half = features / 2;
+  const float min_scale = 1.0f, max_scale = 10000.0f;
+  const float scale_factor = -std::log(max_scale / min_scale) / (float)(half - 1);
+  std::vector<float> div(half);
+  for (int i = 0; i < half; ++i) div[i] = min_scale * std::exp((float)i * scale_factor);
+  for (int pos = 0; pos < max_length; ++pos) {
+    float* row = &data[(size_t)pos * features];
+    for (int i = 0; i < half; ++i) {
+      const float angle = (float)pos * div[i];
+      row[i] = std::sin(angle);
+      row[half + i] = std::cos(angle);
+    }
+  }
+  return data;
+}
+
+static void load_lin(const SafeTensors& st, const std::string& key, int out, int in, Lin& l, const Round& R) {
+  l.out = out;
+  l.in = in;
+  l.w = st.get(key + ".weight", (int64_t)out * in);
+  R.vec(l.w.data(), l.w.size());
+}
+static std::vector<float> load_vec(const SafeTensors& st, const std::string& key, int64_t n, const Round& R) {
+  std::vector<float> v = st.get(key, n);
+  R.vec(v.data(), v.size());
+  return v;
+}
+
+// Depthformer constructor wiring and key names (model.cpp:173-198,
+// modules.cpp:62-70, 90-96, 106-108, 118-134, 215-220, 232-241, 339-347,
+// 364-382).
+static Model* load_model(const char* path, const Cfg& c) {
+  SafeTensors st(path);
+  Model* m = new Model();
+  m->c = c;
+  m->R = Round{c.dtype == 1};
+  const Round& R = m->R;
+  const int d = c.d, in = c.inner(), ff = c.dff;
+  m->emb = load_vec(st, "token_embedding.weight", (int64_t)c.V * d, R);
+  m->pe = sinusoid_table(c.Smax, d);
+  m->enc.resize(c.Le);
+  for (int i = 0; i < c.Le; ++i) {
+    const std::string p = "encoder_layers." + std::to_string(i) + ".";
+    EncLayer& L = m->enc[i];
+    L.n_attn = load_vec(st, p + "pre_attn_norm.weight", d, R);
+    L.n_ffn = load_vec(st, p + "pre_ffn_norm.weight", d, R);
+    load_lin(st, p + "self_attn.q_proj", in, d, L.q, R);
+    load_lin(st, p + "self_attn.k_proj", in, d, L.k, R);
+    load_lin(st, p + "self_attn.v_proj", in, d, L.v, R);
+    load_lin(st, p + "self_attn.o_proj", d, in, L.o, R);
+    load_lin(st, p + "ffn.wi_0", ff, d, L.wi0, R);
+    load_lin(st, p + "ffn.wi_1", ff, d, L.wi1, R);
+    load_lin(st, p + "ffn.wo", d, ff, L.wo, R);
+  }
+  m->enc_norm = load_vec(st, "encoder_norm.weight", d, R);
+  m->trel = load_vec(st, "temporal_rel_pos.relative_attention_bias.weight", (int64_t)c.tnb * c.H, R);
+  m->drel = load_vec(st, "depth_rel_pos.relative_attention_bias.weight", (int64_t)c.dnb * c.H, R);
+  auto load_dec = [&](const std::string& fam, int count, bool cross, std::vector<DecLayer>& out) {
+    out.resize(count);
+    for (int i = 0; i < count; ++i) {
+      const std::string p = fam + "." + std::to_string(i) + ".";
+      DecLayer& L = out[i];
+      L.cross = cross;
+      L.n_self = load_vec(st, p + "pre_self_attn_norm.weight", d, R);
+      L.n_ffn = load_vec(st, p + "pre_ffn_norm.weight", d, R);
+      load_lin(st, p + "self_attn.q_proj", in, d, L.q, R);
+      load_lin(st, p + "self_attn.k_proj", in, d, L.k, R);
+      load_lin(st, p + "self_attn.v_proj", in, d, L.v, R);
+      load_lin(st, p + "self_attn.o_proj", d, in, L.o, R);
+      if (cross) {
+        L.n_cross = load_vec(st, p + "pre_cross_attn_norm.weight", d, R);
+        load_lin(st, p + "cross_attn.q_proj", in, d, L.cq, R);
+        load_lin(st, p + "cross_attn.k_proj", in, d, L.ck, R);
+        load_lin(st, p + "cross_attn.v_proj", in, d, L.cv, R);
+        load_lin(st, p + "cross_attn.o_proj", d, in, L.co, R);
+      }
+      load_lin(st, p + "ffn.wi_0", ff, d, L.wi0, R);
+      load_lin(st, p + "ffn.wi_1", ff, d, L.wi1, R);
+      load_lin(st, p + "ffn.wo", d, ff, L.wo, R);
+    }
+  };
+  load_dec("temporal_layers", c.Lt, true, m->tl);
+  load_dec("depth_layers", c.Ld, false, m->dl);
+  m->dec_norm = load_vec(st, "decoder_norm.weight", d, R);
+  load_lin(st, "lm_head", c.V, d, m->lm, R);
+  return m;
+}
+
+// Gated FFN (modules.cpp:222-226): wo(R(gelu(R(wi_0 x)) * R(wi_1 x))).
+static void ffn(const Model& m, const Lin& wi0, const Lin& wi1, const Lin& wo, const float* n, int M, float* out) {
+  const Round& R = m.R;
+  std::vector<float> a((size_t)M * wi0.out), b((size_t)M * wi1.out);
+  wi0.apply(n, M, a.data(), R);
+  wi1.apply(n, M, b.data(), R);
+  for (size_t i = 0; i < a.size(); ++i) a[i] = R(gelu_approx(a[i], R) * b[i]);
+  wo.apply(a.data(), M, out, R);
+}
+
+// Single-query scaled-dot-product attention with scale 1.0 and an optional
+// additive bias (modules.cpp:289-290, 316-317): float32 scores and softmax,
+// output rounded to the compute dtype.
+static void attend_one(const float* q, const float* K, const float* Vv, int T, int dk, const float* bias,
+                       float* out, const Round& R) {
+  std::vector<float> s(T);
+  float mx = -std::numeric_limits<float>::infinity();
+  for (int j = 0; j < T; ++j) {
+    float acc = 0.f;
+    for (int c = 0; c < dk; ++c) acc += q[c] * K[(size_t)j * dk + c];
+    if (bias) acc += bias[j];
+    s[j] = acc;
+    mx = std::max(mx, acc);
+  }
+  float sum = 0.f;
+  for (int j = 0; j < T; ++j) { s[j] = std::exp(s[j] - mx); sum += s[j]; }
+  for (int c = 0; c < dk; ++c) {
+    float acc = 0.f;
+    for (int j = 0; j < T; ++j) acc += s[j] * Vv[(size_t)j * dk + c];
+    out[c] = R(acc / sum);
+  }
+}
+
+// Depthformer::encode (model.cpp:226-241) with EncoderLayer
+// (modules.cpp:349-358), then the cross K/V projection of every temporal
+// layer (MultiHeadAttention::project_kv, modules.cpp:323-333), which the
+// reference performs on frame 0 of temporal_step (modules.cpp:258-278).
+static void encode(Model& m, const int32_t* ids, int B, int S) {
+  const Cfg& c = m.c;
+  const Round& R = m.R;
+  const int d = c.d, in = c.inner(), H = c.H, dk = c.dk;
+  const size_t M = (size_t)B * S;
+  std::vector<float> x(M * d), n(M * d), q(M * in), k(M * in), v(M * in), o(M * in), h(M * d);
+  for (int b = 0; b < B; ++b)
+    for (int s = 0; s < S; ++s) {
+      const int id = ids[(size_t)b * S + s];
+      const float* e = &m.emb[(size_t)id * d];
+      const float* p = &m.pe[(size_t)s * d];
+      float* xr = &x[((size_t)b * S + s) * d];
+      for (int i = 0; i < d; ++i) xr[i] = R(e[i] + R(p[i]));
+    }
+  for (const EncLayer& L : m.enc) {
+    rms_norm(x.data(), (int)M, d, L.n_attn, n.data(), R);
+    L.q.apply(n.data(), (int)M, q.data(), R);
+    L.k.apply(n.data(), (int)M, k.data(), R);
+    L.v.apply(n.data(), (int)M, v.data(), R);
+#pragma omp parallel
+    {
+      std::vector<float> Kh((size_t)S * dk), Vh((size_t)S * dk), qh(dk), oh(dk);
+#pragma omp for collapse(2) schedule(dynamic, 4)
+      for (int b = 0; b < B; ++b)
+        for (int hh = 0; hh < H; ++hh) {
+          // thread-private copies of this head's K, V: (S, dk)
+          for (int s = 0; s < S; ++s)
+            for (int cc = 0; cc < dk; ++cc) {
+              Kh[(size_t)s * dk + cc] = k[((size_t)b * S + s) * in + hh * dk + cc];
+              Vh[(size_t)s * dk + cc] = v[((size_t)b * S + s) * in + hh * dk + cc];
+            }
+          for (int i = 0; i < S; ++i) {
+            for (int cc = 0; cc < dk; ++cc) qh[cc] = q[((size_t)b * S + i) * in + hh * dk + cc];
+            attend_one(qh.data(), Kh.data(), Vh.data(), S, dk, nullptr, oh.data(), R);
+            for (int cc = 0; cc < dk; ++cc) o[((size_t)b * S + i) * in + hh * dk + cc] = oh[cc];
+          }
+        }
+    }
+    L.o.apply(o.data(), (int)M, h.data(), R);
+    for (size_t i = 0; i < M * d; ++i) x[i] = R(x[i] + h[i]);
+    rms_norm(x.data(), (int)M, d, L.n_ffn, n.data(), R);
+    ffn(m, L.wi0, L.wi1, L.wo, n.data(), (int)M, h.data());
+    for (size_t i = 0; i < M * d; ++i) x[i] = R(x[i] + h[i]);
+  }
+  m.enc_out.assign(M * d, 0.f);
+  rms_norm(x.data(), (int)M, d, m.enc_norm, m.enc_out.data(), R);
+  m.B = B;
+  m.S = S;
+  m.ck.assign(c.Lt, {});
+  m.cv.assign(c.Lt, {});
+  for (int l = 0; l < c.Lt; ++l) {
+    m.tl[l].ck.apply(m.enc_out.data(), (int)M, k.data(), R);
+    m.tl[l].cv.apply(m.enc_out.data(), (int)M, v.data(), R);
+    m.ck[l].assign((size_t)B * H * S * dk, 0.f);
+    m.cv[l].assign((size_t)B * H * S * dk, 0.f);
+    for (int b = 0; b < B; ++b)
+      for (int s = 0; s < S; ++s)
+        for (int hh = 0; hh < H; ++hh)
+          for (int cc = 0; cc < dk; ++cc) {
+            const size_t src = ((size_t)b * S + s) * in + hh * dk + cc;
+            const size_t dst = (((size_t)b * H + hh) * S + s) * dk + cc;
+            m.ck[l][dst] = k[src];
+            m.cv[l][dst] = v[src];
+          }
+  }
+  m.tk.assign(c.Lt, std::vector<float>((size_t)B * H * c.Tmax * dk, 0.f));
+  m.tv.assign(c.Lt, std::vector<float>((size_t)B * H * c.Tmax * dk, 0.f));
+  m.dk_.assign(c.Ld, std::vector<float>((size_t)B * H * c.depth * dk, 0.f));
+  m.dv_.assign(c.Ld, std::vector<float>((size_t)B * H * c.depth * dk, 0.f));
+  m.t_len = 0;
+  m.d_len = 0;
+  m.encoded = true;
+}
+
+// One DecoderLayer::forward for B rows at cache position `pos`
+// (modules.cpp:384-408): pre-norm self-attention with relative-position
+// bias over the concatenated cache (modules.cpp:271-275), optional pre-norm
+// cross-attention over the cached cross K/V (modules.cpp:258-261), pre-norm
+// gated FFN, residual adds rounded to the compute dtype.
+static void decoder_layer(const Model& m, const DecLayer& L, float* x, int B, int pos, int cap, float* Kc, float* Vc,
+                          const float* bias /* (H, pos+1) */, const float* CK, const float* CV, int S) {
+  const Cfg& c = m.c;
+  const Round& R = m.R;
+  const int d = c.d, in = c.inner(), H = c.H, dk = c.dk;
+  std::vector<float> n((size_t)B * d), q((size_t)B * in), k((size_t)B * in), v((size_t)B * in), o((size_t)B * in),
+      h((size_t)B * d);
+  rms_norm(x, B, d, L.n_self, n.data(), R);
+  L.q.apply(n.data(), B, q.data(), R);
+  L.k.apply(n.data(), B, k.data(), R);
+  L.v.apply(n.data(), B, v.data(), R);
+  for (int b = 0; b < B; ++b)
+    for (int hh = 0; hh < H; ++hh)
+      for (int cc = 0; cc < dk; ++cc) {
+        const size_t dst = (((size_t)b * H + hh) * cap + pos) * dk + cc;
+        Kc[dst] = k[(size_t)b * in + hh * dk + cc];
+        Vc[dst] = v[(size_t)b * in + hh * dk + cc];
+      }
+  for (int b = 0; b < B; ++b)
+    for (int hh = 0; hh < H; ++hh) {
+      const size_t base = ((size_t)b * H + hh) * cap * dk;
+      attend_one(&q[(size_t)b * in + hh * dk], Kc + base, Vc + base, pos + 1, dk, bias + (size_t)hh * (pos + 1),
+                 &o[(size_t)b * in + hh * dk], R);
+    }
+  L.o.apply(o.data(), B, h.data(), R);
+  for (size_t i = 0; i < (size_t)B * d; ++i) x[i] = R(x[i] + h[i]);
+  if (L.cross) {
+    rms_norm(x, B, d, L.n_cross, n.data(), R);
+    L.cq.apply(n.data(), B, q.data(), R);
+    for (int b = 0; b < B; ++b)
+      for (int hh = 0; hh < H; ++hh) {
+        const size_t base = ((size_t)b * H + hh) * S * dk;
+        attend_one(&q[(size_t)b * in + hh * dk], CK + base, CV + base, S, dk, nullptr, &o[(size_t)b * in + hh * dk], R);
+      }
+    L.co.apply(o.data(), B, h.data(), R);
+    for (size_t i = 0; i < (size_t)B * d; ++i) x[i] = R(x[i] + h[i]);
+  }
+  rms_norm(x, B, d, L.n_ffn, n.data(), R);
+  ffn(m, L.wi0, L.wi1, L.wo, n.data(), B, h.data());
+  for (size_t i = 0; i < (size_t)B * d; ++i) x[i] = R(x[i] + h[i]);
+}
+
+// Bias for query position q over keys 0..q: (H, q+1), the
+// RelativePositionBias::operator()(1, q+1, q) gather (modules.cpp:178-191,
+// model.cpp:302-320), values already in the compute dtype.
+static std::vector<float> step_bias(const std::vector<float>& table, int nb, int maxd, int H, int q) {
+  std::vector<float> b((size_t)H * (q + 1));
+  for (int j = 0; j <= q; ++j) {
+    const int bucket = relative_bucket(j - q, nb, maxd);
+    for (int hh = 0; hh < H; ++hh) b[(size_t)hh * (q + 1) + j] = table[(size_t)bucket * H + hh];
+  }
+  return b;
+}
+
+// Depthformer::temporal_step, eager path (model.cpp:493-513).
+static void temporal_step(Model& m, const float* xin, int f, float* out) {
+  const Cfg& c = m.c;
+  std::vector<float> x(xin, xin + (size_t)m.B * c.d);
+  m.R.vec(x.data(), x.size());
+  const std::vector<float> bias = step_bias(m.trel, c.tnb, c.tmd, c.H, f);
+  for (int l = 0; l < c.Lt; ++l)
+    decoder_layer(m, m.tl[l], x.data(), m.B, f, c.Tmax, m.tk[l].data(), m.tv[l].data(), bias.data(), m.ck[l].data(),
+                  m.cv[l].data(), m.S);
+  m.t_len = f + 1;
+  m.last_temporal = x;
+  std::memcpy(out, x.data(), x.size() * 4);
+}
+
+// Depthformer::depth_step, eager path (model.cpp:638-659): 4 layers,
+// decoder_norm, lm_head -> (B, V).
+static void depth_step(Model& m, const float* xin, int di, float* logits) {
+  const Cfg& c = m.c;
+  std::vector<float> x(xin, xin + (size_t)m.B * c.d);
+  m.R.vec(x.data(), x.size());
+  const std::vector<float> bias = step_bias(m.drel, c.dnb, c.dmd, c.H, di);
+  for (int l = 0; l < c.Ld; ++l)
+    decoder_layer(m, m.dl[l], x.data(), m.B, di, c.depth, m.dk_[l].data(), m.dv_[l].data(), bias.data(), nullptr,
+                  nullptr, 0);
+  m.d_len = di + 1;
+  std::vector<float> n((size_t)m.B * c.d);
+  rms_norm(x.data(), m.B, c.d, m.dec_norm, n.data(), m.R);
+  m.lm.apply(n.data(), m.B, logits, m.R);
+}
+
+// One sampling step (decode.cpp:465-474 with cfg_combine 71-85,
+// apply_vocab_mask 87-91, top_k_logits 104-122, sample_with_temperature
+// 124-148). `logits` is (rows, V); rows == 2 applies CFG, rows == 1 takes
+// row 0. `u` holds V uniforms for the Gumbel noise.
+static int sample_step(const float* logits, int rows, int V, int level, bool masked, int cb, int off, float w,
+                       float T, int top_k, const float* u) {
+  const float ninf = -std::numeric_limits<float>::infinity();
+  std::vector<float> g(V);
+  for (int i = 0; i < V; ++i) g[i] = rows == 2 ? cfg_mix(logits[i], logits[V + i], w) : logits[i];
+  if (masked) {
+    const int lo = off + level * cb, hi = lo + cb;
+    for (int i = 0; i < V; ++i)
+      if (i < lo || i >= hi) g[i] = ninf;
+  }
+  auto argmax_first = [&](const std::vector<float>& a) {
+    int best = 0;
+    for (int i = 1; i < (int)a.size(); ++i)
+      if (a[i] > a[best]) best = i;
+    return best;
+  };
+  if (T == 0.0f) return argmax_first(g);
+  for (int i = 0; i < V; ++i) g[i] = div_temperature(g[i], T);
+  if (top_k > 0) {
+    std::vector<float> s(g);
+    const int k = std::min(top_k, V);
+    std::nth_element(s.begin(), s.begin() + (k - 1), s.end(), std::greater<float>());
+    const float thr = s[k - 1];  // min of the top-k values (decode.cpp:119-121)
+    for (int i = 0; i < V; ++i)
+      if (g[i] < thr) g[i] = ninf;
+  }
+  for (int i = 0; i < V; ++i) g[i] = (g[i] == ninf) ? ninf : add_noise(g[i], gumbel_from_uniform(u[i]));
+  return argmax_first(g);
+}
+
+// generate_tokens, non-speculative path (decode.cpp:239-573): frame 0
+// input = embedding of PAD (0), depth 0 input = temporal output, depth d > 0
+// input = embedding of the sampled token for every row, next temporal input
+// = R(R-summed embeddings / rvq_depth) (decode.cpp:383-386, 476-477, 484).
+// `forced` (optional) replaces the sampled tokens (teacher forcing);
+// `logits_out` (optional) receives (F, depth, B, V).
+static void generate(Model& m, const int32_t* ids, int B, int S, int F, float w, float T, int top_k, bool masked,
+                     uint64_t seed, const float* uniforms, const int32_t* forced, int32_t* out_ids,
+                     float* logits_out) {
+  const Cfg& c = m.c;
+  const Round& R = m.R;
+  const int d = c.d, D = c.depth, V = c.V;
+  encode(m, ids, B, S);
+  std::vector<float> tin((size_t)B * d), tout((size_t)B * d), din((size_t)B * d), sum((size_t)B * d),
+      logits((size_t)B * V), u(V);
+  for (int b = 0; b < B; ++b) std::memcpy(&tin[(size_t)b * d], &m.emb[0], d * 4);  // PAD = 0
+  for (int f = 0; f < F; ++f) {
+    temporal_step(m, tin.data(), f, tout.data());
+    din = tout;
+    std::fill(sum.begin(), sum.end(), 0.f);
+    for (int l = 0; l < D; ++l) {
+      depth_step(m, din.data(), l, logits.data());
+      if (logits_out) std::memcpy(logits_out + ((size_t)f * D + l) * B * V, logits.data(), logits.size() * 4);
+      int tok;
+      if (forced) {
+        tok = forced[(size_t)f * D + l];
+      } else {
+        const uint32_t step = (uint32_t)(f * D + l);
+        for (int i = 0; i < V; ++i)
+          u[i] = uniforms ? uniforms[(size_t)step * V + i] : philox_uniform(seed, step, (uint32_t)i);
+        tok = sample_step(logits.data(), B, V, l, masked, c.cb, c.off, w, T, top_k, u.data());
+      }
+      if (out_ids) out_ids[(size_t)f * D + l] = tok;
+      for (int b = 0; b < B; ++b) std::memcpy(&din[(size_t)b * d], &m.emb[(size_t)tok * d], d * 4);
+      for (size_t i = 0; i < sum.size(); ++i) sum[i] = R(sum[i] + din[i]);
+    }
+    for (size_t i = 0; i < sum.size(); ++i) tin[i] = R(sum[i] / (float)D);
+  }
+}
+
+}  // namespace oracle
+
+// ---------------------------------------------------------------------------
+// C interface for ctypes (tests/, bench.py).
+// ---------------------------------------------------------------------------
+using namespace oracle;
+
+#define ORC_TRY(body)                 \
+  try {                               \
+    body;                             \
+    return 0;                         \
+  } catch (const std::exception& e) { \
+    g_err = e.what();                 \
+    return 1;                         \
+  }
+
+extern "C" {
+
+const char* orc_last_error() { return g_err.c_str(); }
+
+int orc_num_threads() { return omp_get_max_threads(); }
+void orc_set_num_threads(int n) { omp_set_num_threads(n); }
+
+void* orc_create(const char* path, const int* cfg_ints) {
+  try {
+    return load_model(path, cfg_from_ints(cfg_ints));
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return nullptr;
+  }
+}
+
+void orc_destroy(void* m) { delete (Model*)m; }
+
+int orc_encode(void* mp, const int32_t* ids, int B, int S, float* enc_out) {
+  ORC_TRY({
+    Model& m = *(Model*)mp;
+    if (S > m.c.Smax) throw std::out_of_range("seq_len exceeds max_encoder_length");
+    encode(m, ids, B, S);
+    if (enc_out) std::memcpy(enc_out, m.enc_out.data(), m.enc_out.size() * 4);
+  })
+}
+
+int orc_temporal_step(void* mp, const float* x, int f, float* out) {
+  ORC_TRY({
+    Model& m = *(Model*)mp;
+    if (!m.encoded) throw std::runtime_error("temporal_step before encode");
+    if (f != m.t_len || f >= m.c.Tmax) throw std::runtime_error("temporal_step: frame index out of order");
+    std::vector<float> pad;
+    if (!x) {
+      pad.resize((size_t)m.B * m.c.d);
+      for (int b = 0; b < m.B; ++b) std::memcpy(&pad[(size_t)b * m.c.d], &m.emb[0], m.c.d * 4);
+      x = pad.data();
+    }
+    temporal_step(m, x, f, out);
+  })
+}
+
+int orc_depth_step(void* mp, const float* x, int di, float* logits) {
+  ORC_TRY({
+    Model& m = *(Model*)mp;
+    if (!m.encoded) throw std::runtime_error("depth_step before encode");
+    if (di != 0 && di != m.d_len) throw std::runtime_error("depth_step: depth index out of order");
+    if (di >= m.c.depth) throw std::runtime_error("depth_step: depth index out of range");
+    if (!x) x = m.last_temporal.data();
+    depth_step(m, x, di, logits);
+  })
+}
+
+int orc_generate(void* mp, const int32_t* ids, int B, int S, int F, float w, float T, int top_k, int masked,
+                 uint64_t seed, const float* uniforms, int32_t* out_ids) {
+  ORC_TRY({
+    generate(*(Model*)mp, ids, B, S, F, w, T, top_k, masked != 0, seed, uniforms, nullptr, out_ids, nullptr);
+  })
+}
+
+int orc_teacher_forced(void* mp, const int32_t* ids, int B, int S, int F, const int32_t* tokens, float* logits) {
+  ORC_TRY({
+    generate(*(Model*)mp, ids, B, S, F, 0.f, 0.f, 0, 0, 0, nullptr, tokens, nullptr, logits);
+  })
+}
+
+int orc_sample(const float* logits, int rows, int V, int level, int masked, int cb, int off, float w, float T,
+               int top_k, const float* u, int32_t* tok) {
+  ORC_TRY({ *tok = sample_step(logits, rows, V, level, masked != 0, cb, off, w, T, top_k, u); })
+}
+
+int orc_relative_bucket(int rel, int nb, int maxd) { return relative_bucket(rel, nb, maxd); }
+
+void orc_sinusoid(int max_length, int features, float* out) {
+  std::vector<float> t = sinusoid_table(max_length, features);
+  std::memcpy(out, t.data(), t.size() * 4);
+}
+
+float orc_bf16_round(float x) { return bf16_round(x); }
+float orc_philox_uniform(uint64_t seed, uint32_t step, uint32_t idx) { return philox_uniform(seed, step, idx); }
+void orc_philox4x32_10(const uint32_t* ctr, const uint32_t* key, uint32_t* out) { philox4x32_10(ctr, key, out); }
+float orc_exact_log(float x) { return exact_log(x); }
+float orc_gumbel(float u) { return gumbel_from_uniform(u); }
+float orc_cfg_mix(float c, float u, float w) { return cfg_mix(c, u, w); }
+float orc_gelu(float x, int bf16) { return gelu_approx(x, Round{bf16 != 0}); }
+
+}  // extern "C"

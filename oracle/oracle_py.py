@@ -1,0 +1,195 @@
+"""ctypes bindings of the CPU oracle (oracle/_build/liboracle.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, by bench.py's CPU-baseline
+legs and by __graft_entry__.smoke() as the checker. The engine never uses it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        from build_oracle import build  # noqa: E402  (same directory)
+
+        path = build()
+        L = ctypes.CDLL(path)
+        L.orc_last_error.restype = ctypes.c_char_p
+        L.orc_create.restype = ctypes.c_void_p
+        L.orc_create.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_int)]
+        L.orc_destroy.argtypes = [ctypes.c_void_p]
+        for n in ["orc_encode", "orc_temporal_step", "orc_depth_step", "orc_generate", "orc_teacher_forced"]:
+            getattr(L, n).restype = ctypes.c_int
+        L.orc_encode.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+        L.orc_temporal_step.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+        L.orc_depth_step.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+        L.orc_generate.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                   ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_uint64,
+                                   ctypes.c_void_p, ctypes.c_void_p]
+        L.orc_teacher_forced.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_void_p, ctypes.c_void_p]
+        L.orc_sample.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                 ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int,
+                                 ctypes.c_void_p, ctypes.c_void_p]
+        L.orc_relative_bucket.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        L.orc_sinusoid.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+        L.orc_bf16_round.restype = ctypes.c_float
+        L.orc_bf16_round.argtypes = [ctypes.c_float]
+        L.orc_philox_uniform.restype = ctypes.c_float
+        L.orc_philox_uniform.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32]
+        L.orc_philox4x32_10.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        L.orc_exact_log.restype = ctypes.c_float
+        L.orc_exact_log.argtypes = [ctypes.c_float]
+        L.orc_gumbel.restype = ctypes.c_float
+        L.orc_gumbel.argtypes = [ctypes.c_float]
+        L.orc_cfg_mix.restype = ctypes.c_float
+        L.orc_cfg_mix.argtypes = [ctypes.c_float, ctypes.c_float, ctypes.c_float]
+        L.orc_gelu.restype = ctypes.c_float
+        L.orc_gelu.argtypes = [ctypes.c_float, ctypes.c_int]
+        L.orc_set_num_threads.argtypes = [ctypes.c_int]
+        _lib = L
+    return _lib
+
+
+def _p(a: Optional[np.ndarray]):
+    return None if a is None else a.ctypes.data
+
+
+def _check(rc: int):
+    if rc != 0:
+        raise RuntimeError("oracle: " + lib().orc_last_error().decode())
+
+
+class Oracle:
+    """CPU restatement of the Depthformer (fp32 or bf16-emulating)."""
+
+    def __init__(self, safetensors_path: str, cfg_ints):
+        arr = (ctypes.c_int * 18)(*cfg_ints)
+        h = lib().orc_create(safetensors_path.encode(), arr)
+        if not h:
+            raise RuntimeError("oracle: " + lib().orc_last_error().decode())
+        self.h = h
+        self.cfg = list(cfg_ints)
+        self.V, self.d, self.depth = cfg_ints[0], cfg_ints[1], cfg_ints[9]
+        self.rows = 0
+
+    def encode(self, ids: np.ndarray) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        B, S = ids.shape
+        out = np.empty((B, S, self.d), np.float32)
+        _check(lib().orc_encode(self.h, _p(ids), B, S, _p(out)))
+        self.rows = B
+        return out
+
+    def temporal_step(self, x: Optional[np.ndarray], f: int) -> np.ndarray:
+        xin = None if x is None else np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty((self.rows, self.d), np.float32)
+        _check(lib().orc_temporal_step(self.h, _p(xin), f, _p(out)))
+        return out
+
+    def depth_step(self, x: Optional[np.ndarray], l: int) -> np.ndarray:
+        xin = None if x is None else np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty((self.rows, self.V), np.float32)
+        _check(lib().orc_depth_step(self.h, _p(xin), l, _p(out)))
+        return out
+
+    def generate(self, ids: np.ndarray, num_frames: int, w: float, temperature: float, top_k: int, masked: bool,
+                 seed: int, uniforms: Optional[np.ndarray] = None) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        B, S = ids.shape
+        out = np.empty((num_frames, self.depth), np.int32)
+        u = None if uniforms is None else np.ascontiguousarray(uniforms, dtype=np.float32)
+        _check(lib().orc_generate(self.h, _p(ids), B, S, num_frames, w, temperature, top_k, int(masked), seed, _p(u),
+                                  _p(out)))
+        self.rows = B
+        return out
+
+    def teacher_forced(self, ids: np.ndarray, tokens: np.ndarray, num_frames: int) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        B, S = ids.shape
+        toks = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        out = np.empty((num_frames, self.depth, B, self.V), np.float32)
+        _check(lib().orc_teacher_forced(self.h, _p(ids), B, S, num_frames, _p(toks), _p(out)))
+        self.rows = B
+        return out
+
+    def close(self):
+        if self.h:
+            lib().orc_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def sample(logits: np.ndarray, level: int, masked: bool, codebook: int, offset: int, w: float, temperature: float,
+           top_k: int, uniforms: np.ndarray) -> int:
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    rows, V = logits.shape
+    u = np.ascontiguousarray(uniforms, dtype=np.float32)
+    tok = np.zeros(1, np.int32)
+    _check(lib().orc_sample(_p(logits), rows, V, level, int(masked), codebook, offset, w, temperature, top_k, _p(u),
+                            _p(tok)))
+    return int(tok[0])
+
+
+def relative_bucket(rel: int, num_buckets: int, max_distance: int) -> int:
+    return lib().orc_relative_bucket(rel, num_buckets, max_distance)
+
+
+def sinusoid(max_length: int, features: int) -> np.ndarray:
+    out = np.empty((max_length, features), np.float32)
+    lib().orc_sinusoid(max_length, features, _p(out))
+    return out
+
+
+def philox_uniform(seed: int, step: int, idx: int) -> float:
+    return lib().orc_philox_uniform(seed, step, idx)
+
+
+def philox4x32_10(ctr, key):
+    c = np.asarray(ctr, np.uint32)
+    k = np.asarray(key, np.uint32)
+    o = np.zeros(4, np.uint32)
+    lib().orc_philox4x32_10(_p(c), _p(k), _p(o))
+    return o
+
+
+def gumbel(u: float) -> float:
+    return lib().orc_gumbel(u)
+
+
+def exact_log(x: float) -> float:
+    return lib().orc_exact_log(x)
+
+
+def cfg_mix(c: float, u: float, w: float) -> float:
+    return lib().orc_cfg_mix(c, u, w)
+
+
+def gelu(x: float, bf16: bool) -> float:
+    return lib().orc_gelu(x, int(bf16))
+
+
+def bf16_round(x: float) -> float:
+    return lib().orc_bf16_round(x)
+
+
+def set_num_threads(n: int):
+    lib().orc_set_num_threads(n)
+
+
+def num_threads() -> int:
+    return lib().orc_num_threads()

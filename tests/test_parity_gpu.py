@@ -1,0 +1,248 @@
+"""Parity of the CUDA engine (through the C ABI) against the CPU oracle.
+
+Tolerances: teacher-forced logits within 1e-4 max-abs
+in fp32 and 2e-2 in bf16; greedy ids bit-exact in fp32; sampled ids
+bit-exact given identical logits and draws.
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+
+from conftest import random_ids
+
+pytestmark = pytest.mark.gpu
+
+FP32_TOL = 1e-4
+BF16_TOL = 2e-2
+
+
+def _engine(mrtdf, path, name, dtype):
+    cfg = mrtdf.preset(name, dtype)
+    return cfg, mrtdf.Engine(cfg).load_safetensors(path)
+
+
+def _forced_tokens(cfg, F, seed):
+    rng = np.random.default_rng(seed)
+    return np.stack([cfg.codec_offset + np.arange(cfg.rvq_depth) * cfg.codebook_size
+                     + rng.integers(0, cfg.codebook_size, cfg.rvq_depth) for _ in range(F)]).astype(np.int32)
+
+
+# ---------------------------------------------------------------------------
+# tiny config: every path, both dtypes
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype,tol", [(0, FP32_TOL), (1, BF16_TOL)])
+def test_encode_matches_oracle(mrtdf, oracle, tiny_weights, dtype, tol):
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", dtype)
+    ids = random_ids(cfg, 2, cfg.max_encoder_length, seed=1)
+    st = mrtdf.Stream(eng, 1, True)
+    got = st.encode(ids, want_output=True)
+    want = oracle.Oracle(tiny_weights, cfg.as_ints()).encode(ids)
+    assert np.abs(got - want).max() <= tol
+
+
+@pytest.mark.parametrize("dtype,tol", [(0, FP32_TOL), (1, BF16_TOL)])
+def test_step_api_matches_oracle(mrtdf, oracle, tiny_weights, dtype, tol):
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", dtype)
+    ids = random_ids(cfg, 2, 60, seed=2)
+    st = mrtdf.Stream(eng, 1, True)
+    orc = oracle.Oracle(tiny_weights, cfg.as_ints())
+    st.encode(ids)
+    orc.encode(ids)
+    rng = np.random.default_rng(0)
+    x = None
+    for f in range(3):
+        a = st.temporal_step(x, f)
+        b = orc.temporal_step(x, f)
+        assert np.abs(a - b).max() <= tol * 4, f
+        d = None
+        for l in range(4):
+            la = st.depth_step(d, l)
+            lb = orc.depth_step(d, l)
+            assert np.abs(la - lb).max() <= tol, (f, l)
+            d = rng.standard_normal((2, cfg.d_model)).astype(np.float32) * 0.5
+        x = rng.standard_normal((2, cfg.d_model)).astype(np.float32) * 0.5
+
+
+@pytest.mark.parametrize("dtype,tol", [(0, FP32_TOL), (1, BF16_TOL)])
+@pytest.mark.parametrize("cfg_rows", [1, 2])
+def test_teacher_forced_logits(mrtdf, oracle, tiny_weights, dtype, tol, cfg_rows):
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", dtype)
+    F = 4
+    ids = random_ids(cfg, cfg_rows, cfg.max_encoder_length, seed=3)
+    toks = _forced_tokens(cfg, F, seed=4)
+    st = mrtdf.Stream(eng, 1, cfg_rows == 2)
+    got = st.teacher_forced_logits(ids, toks, F)
+    want = oracle.Oracle(tiny_weights, cfg.as_ints()).teacher_forced(ids, toks, F)
+    err = np.abs(got - want).max()
+    assert err <= tol, err
+
+
+def test_greedy_ids_bit_exact_fp32(mrtdf, oracle, tiny_weights):
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", 0)
+    F = cfg.max_frames
+    for rows, seed in [(1, 5), (2, 6)]:
+        ids = random_ids(cfg, rows, cfg.max_encoder_length, seed=seed)
+        st = mrtdf.Stream(eng, 1, rows == 2)
+        o = mrtdf.gen_opts(cfg, F, temperature=0.0, top_k=40, guidance_weight=4.0)
+        got = st.generate_tokens(ids, o)[0]
+        want = oracle.Oracle(tiny_weights, cfg.as_ints()).generate(ids, F, 4.0, 0.0, 40, True, 0)
+        np.testing.assert_array_equal(got, want)
+
+
+def test_sampled_ids_with_injected_draws_fp32(mrtdf, oracle, tiny_weights):
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", 0)
+    F = cfg.max_frames
+    ids = random_ids(cfg, 2, cfg.max_encoder_length, seed=7)
+    u = np.random.default_rng(8).uniform(1e-7, 1 - 1e-7, (F * cfg.rvq_depth, cfg.vocab_size)).astype(np.float32)
+    st = mrtdf.Stream(eng, 1, True)
+    o = mrtdf.gen_opts(cfg, F, temperature=1.1, top_k=40, guidance_weight=4.0, uniforms=u)
+    got = st.generate_tokens(ids, o)[0]
+    want = oracle.Oracle(tiny_weights, cfg.as_ints()).generate(ids, F, 4.0, 1.1, 40, True, 0, uniforms=u)
+    np.testing.assert_array_equal(got, want)
+
+
+def test_sampled_ids_with_philox_fp32(mrtdf, oracle, tiny_weights):
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", 0)
+    F = cfg.max_frames
+    ids = random_ids(cfg, 2, cfg.max_encoder_length, seed=9)
+    st = mrtdf.Stream(eng, 1, True)
+    o = mrtdf.gen_opts(cfg, F, temperature=1.1, top_k=40, guidance_weight=4.0, seed=1)
+    got = st.generate_tokens(ids, o)[0]
+    want = oracle.Oracle(tiny_weights, cfg.as_ints()).generate(ids, F, 4.0, 1.1, 40, True, 1)
+    np.testing.assert_array_equal(got, want)
+
+
+def test_sampler_bit_exact(mrtdf, oracle, tiny_weights):
+    """mrtdf_sample == oracle sampler on identical logits and draws."""
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", 0)
+    rng = np.random.default_rng(10)
+    V = cfg.vocab_size
+    for trial in range(120):
+        rows = 1 + trial % 2
+        logits = rng.standard_normal((rows, V)).astype(np.float32) * 3
+        if trial % 3 == 0:
+            logits = np.round(logits * 2) / 2  # many ties at the top-k threshold
+        T = [0.0, 1.1, 0.5, 2.0][trial % 4]
+        k = [40, 1, 0, 64, 7][trial % 5]
+        masked = trial % 7 != 0
+        level = trial % cfg.rvq_depth
+        u = rng.uniform(1e-7, 1 - 1e-7, V).astype(np.float32)
+        o = mrtdf.gen_opts(cfg, 1, temperature=T, top_k=k, guidance_weight=4.0, use_vocab_masks=masked)
+        got = eng.sample(logits, 0, level, o, uniforms=u)
+        want = oracle.sample(logits, level, masked, cfg.codebook_size, cfg.codec_offset, 4.0, T, k, u)
+        assert got == want, (trial, got, want)
+
+
+def test_sampler_philox_draws_match(mrtdf, oracle, tiny_weights):
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", 0)
+    rng = np.random.default_rng(11)
+    V = cfg.vocab_size
+    for trial in range(40):
+        logits = rng.standard_normal((2, V)).astype(np.float32)
+        frame, level, seed = trial % 5, trial % 16, 1000 + trial
+        u = np.array([oracle.philox_uniform(seed, frame * cfg.rvq_depth + level, i) for i in range(V)], np.float32)
+        o = mrtdf.gen_opts(cfg, 1, temperature=1.1, top_k=40, guidance_weight=4.0, seed=seed)
+        got = eng.sample(logits, frame, level, o, uniforms=None)
+        want = oracle.sample(logits, level, True, cfg.codebook_size, cfg.codec_offset, 4.0, 1.1, 40, u)
+        assert got == want
+
+
+def test_graph_replay_equals_stream_launches(mrtdf, tiny_weights):
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", 1)
+    ids = random_ids(cfg, 2, cfg.max_encoder_length, seed=12)
+    o = mrtdf.gen_opts(cfg, cfg.max_frames, seed=3)
+    st = mrtdf.Stream(eng, 1, True)
+    a = st.generate_tokens(ids, o)
+    b = st.generate_tokens(ids, o)  # graph replay
+    os.environ["MRTDF_GRAPH"] = "0"
+    try:
+        c = st.generate_tokens(ids, o)
+    finally:
+        del os.environ["MRTDF_GRAPH"]
+    np.testing.assert_array_equal(a, b)
+    np.testing.assert_array_equal(a, c)
+    o2 = mrtdf.gen_opts(cfg, cfg.max_frames, seed=4)
+    assert not np.array_equal(a, st.generate_tokens(ids, o2))
+
+
+def test_multi_sequence_stream_equals_single(mrtdf, tiny_weights):
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", 1)
+    F = cfg.max_frames
+    ids_a = random_ids(cfg, 2, cfg.max_encoder_length, seed=13)
+    ids_b = random_ids(cfg, 2, cfg.max_encoder_length, seed=14)
+    o = mrtdf.gen_opts(cfg, F)
+    multi = mrtdf.Stream(eng, 2, True).generate_tokens(np.concatenate([ids_a, ids_b]), o, seeds=[100, 101])
+    single = mrtdf.Stream(eng, 1, True)
+    np.testing.assert_array_equal(multi[0], single.generate_tokens(ids_a, o, seeds=[100])[0])
+    np.testing.assert_array_equal(multi[1], single.generate_tokens(ids_b, o, seeds=[101])[0])
+
+
+def test_call_order_errors(mrtdf, tiny_weights):
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", 1)
+    st = mrtdf.Stream(eng, 1, True)
+    with pytest.raises(mrtdf.MrtdfError) as e:
+        st.temporal_step(None, 0)
+    assert e.value.code == 4  # MRTDF_ERR_STATE: no cross-attention cache yet
+    st.encode(random_ids(cfg, 2, 20, seed=1))
+    with pytest.raises(mrtdf.MrtdfError) as e:
+        st.temporal_step(None, 1)
+    assert e.value.code == 4  # cache size mismatch (model.cpp:326-328)
+    st.temporal_step(None, 0)
+    with pytest.raises(mrtdf.MrtdfError) as e:
+        st.depth_step(None, cfg.rvq_depth)
+    assert e.value.code == 7  # MRTDF_ERR_RANGE
+    with pytest.raises(mrtdf.MrtdfError) as e:
+        st.encode(random_ids(cfg, 2, cfg.max_encoder_length + 1, seed=1))
+    assert e.value.code == 7  # seq_len exceeds max_encoder_length (model.cpp:216-218)
+    bad = random_ids(cfg, 2, 20, seed=1)
+    bad[0, 3] = cfg.vocab_size
+    with pytest.raises(mrtdf.MrtdfError) as e:
+        st.encode(bad)
+    assert e.value.code == 1
+
+
+# ---------------------------------------------------------------------------
+# benchmark architecture (hybrid: d 1024, 12/20/4 layers, vocab 16388)
+# ---------------------------------------------------------------------------
+def test_hybrid_bf16_teacher_forced(mrtdf, oracle, hybrid_weights):
+    cfg, eng = _engine(mrtdf, hybrid_weights, "hybrid", 1)
+    F = 2
+    ids = random_ids(cfg, 2, 1006, seed=20)
+    toks = _forced_tokens(cfg, F, seed=21)
+    got = mrtdf.Stream(eng, 1, True).teacher_forced_logits(ids, toks, F)
+    want = oracle.Oracle(hybrid_weights, cfg.as_ints()).teacher_forced(ids, toks, F)
+    err = np.abs(got - want).max()
+    assert err <= BF16_TOL, err
+
+
+def test_hybrid_fp32_teacher_forced_and_greedy(mrtdf, oracle, hybrid_weights):
+    cfg, eng = _engine(mrtdf, hybrid_weights, "hybrid", 0)
+    F = 2
+    ids = random_ids(cfg, 1, 1006, seed=0)
+    orc = oracle.Oracle(hybrid_weights, cfg.as_ints())
+    st = mrtdf.Stream(eng, 1, False)
+    toks = _forced_tokens(cfg, F, seed=22)
+    err = np.abs(st.teacher_forced_logits(ids, toks, F) - orc.teacher_forced(ids, toks, F)).max()
+    assert err <= FP32_TOL, err
+    o = mrtdf.gen_opts(cfg, F, temperature=0.0)
+    np.testing.assert_array_equal(st.generate_tokens(ids, o)[0], orc.generate(ids, F, 0.0, 0.0, 40, True, 0))
+
+
+def test_hybrid_bf16_chunk_properties(mrtdf, hybrid_weights):
+    """A full 50-frame chunk: ids in their level ranges, deterministic, seed-dependent."""
+    cfg, eng = _engine(mrtdf, hybrid_weights, "hybrid", 1)
+    ids = random_ids(cfg, 2, 1006, seed=23)
+    st = mrtdf.Stream(eng, 1, True)
+    o = mrtdf.gen_opts(cfg, 50, seed=1)
+    a = st.generate_tokens(ids, o)[0]
+    b = st.generate_tokens(ids, o)[0]
+    np.testing.assert_array_equal(a, b)
+    lo = cfg.codec_offset + np.arange(16) * cfg.codebook_size
+    assert np.all((a >= lo[None]) & (a < lo[None] + cfg.codebook_size))
+    rvq = mrtdf.llm_to_rvq(a, cfg.codebook_size, cfg.codec_offset)
+    assert rvq.min() >= 0 and rvq.max() < 1024
+    c = st.generate_tokens(ids, mrtdf.gen_opts(cfg, 50, seed=2))[0]
+    assert (a != c).mean() > 0.5
