@@ -203,6 +203,336 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_phase_kernel(const GemvPara
   }
 }
 
+// ---------------------------------------------------------------------------
+// bf16 GEMV phase on the tensor cores.
+//
+// CTA c owns units [c * units / G, (c + 1) * units / G): R rows of W, one
+// contiguous HBM range. Before griddepcontrol.wait the CTA
+//   * issues one TMA bulk copy per row into shared memory with a 16-byte row
+//     pad (so 8-row ldmatrix reads are bank-conflict free), all in flight at
+//     once, with an L2 eviction-priority hint (depth weights kept, temporal
+//     weights streamed);
+//   * loads its RMSNorm scale slice into registers.
+// After the wait it stages the input rows (RMS-normalised with the
+// reference's rounding) as bf16 in shared memory, then computes
+// Y[R, B] = W_slice[R, cols] . X^T with mma.sync m16n8k16 (rows as M, the
+// batch rows as N = 8, k split over the 8 warps), reduces the per-warp
+// partials through shared memory and applies the fused epilogue.
+// ---------------------------------------------------------------------------
+constexpr int kMmaMaxRows = 64;  // 4 m16 tiles per CTA
+
+__device__ __forceinline__ uint64_t l2_policy(bool keep) {
+  uint64_t pol;
+  if (keep) asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  else asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+__device__ __forceinline__ void bulk_g2s_hint(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4_g(uint32_t* r, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_m16n8k16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+struct MmaLayout {
+  int rstride;       // bytes per padded row (weights and inputs)
+  int w_bytes;       // max_rows * rstride, rounded up to 128
+  int x_bytes;       // 8 * rstride
+  int red_bytes;     // 8 warps * 4 tiles * 16 * 8 floats
+  int total;
+};
+
+__host__ __device__ inline MmaLayout mma_layout(int cols, int max_rows) {
+  MmaLayout L;
+  L.rstride = cols * 2 + 16;
+  L.w_bytes = ((max_rows * L.rstride) + 127) & ~127;
+  L.x_bytes = ((8 * L.rstride) + 127) & ~127;
+  L.red_bytes = 8 * 4 * 16 * 8 * 4;
+  L.total = L.w_bytes + L.x_bytes + L.red_bytes + 64;
+  return L;
+}
+
+template <bool NORM, int MODE>
+__global__ void __launch_bounds__(256) gemv_mma_kernel(const GemvParams p, const int max_rows) {
+  typedef __nv_bfloat16 T;
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int RPU = (MODE == kGemvGeglu) ? 2 : 1;
+  const MmaLayout L = mma_layout(p.cols, max_rows);
+  uint8_t* wsm = smem;
+  uint8_t* xsm = smem + L.w_bytes;
+  float* red = reinterpret_cast<float*>(smem + L.w_bytes + L.x_bytes);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.w_bytes + L.x_bytes + L.red_bytes);
+  __shared__ float wred[8][kGemvMaxB];
+  __shared__ float rstd[kGemvMaxB];
+  __shared__ int ok_flag;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = gridDim.x, c = blockIdx.x;
+  const int u0 = (int)(((long long)c * p.units) / G);
+  const int u1 = (int)(((long long)(c + 1) * p.units) / G);
+  const int R = (u1 - u0) * RPU;
+  const int row_bytes = p.cols * 2;
+  const int nchunk = p.cols >> 3;  // 16-byte chunks per row
+
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    ok_flag = 1;
+  }
+  __syncthreads();
+  if (warp == 0 && R > 0) {
+    const uint64_t pol = l2_policy(p.l2_keep != 0);
+    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(R * row_bytes));
+    __syncwarp();
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(p.W) + (size_t)u0 * RPU * row_bytes;
+    for (int r = lane; r < R; r += 32) bulk_g2s_hint(wsm + (size_t)r * L.rstride, src + (size_t)r * row_bytes,
+                                                    (uint32_t)row_bytes, bar, pol);
+  }
+  // constant RMSNorm scale slice -> registers before waiting on the producer
+  uint4 nw_reg[4];
+  if (NORM) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int ch = tid + i * 256;
+      nw_reg[i] = ch < nchunk ? reinterpret_cast<const uint4*>(p.norm_w)[ch] : make_uint4(0, 0, 0, 0);
+    }
+  }
+  pdl_launch_dependents();
+  pdl_wait();
+
+  // ---- inputs -> shared memory as bf16 (RMS-normalised when NORM) --------
+  const T* x = reinterpret_cast<const T*>(p.x);
+  if (NORM) {
+    float ss[kGemvMaxB];
+#pragma unroll
+    for (int b = 0; b < kGemvMaxB; ++b) ss[b] = 0.f;
+#pragma unroll
+    for (int b = 0; b < kGemvMaxB; ++b) {
+      if (b < p.B) {
+        for (int ch = tid; ch < nchunk; ch += 256) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(x + (size_t)b * p.x_stride + ch * 8);
+          float f[8];
+          Vec16<T>::unpack(raw, f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ss[b] = fmaf(f[e], f[e], ss[b]);
+          *reinterpret_cast<uint4*>(xsm + (size_t)b * L.rstride + ch * 16) = raw;
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < kGemvMaxB; ++b) {
+      const float v = warp_sum(ss[b]);
+      if (lane == 0) wred[warp][b] = v;
+    }
+    __syncthreads();
+    if (tid < kGemvMaxB) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) t += wred[w][tid];
+      rstd[tid] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)p.cols), 1e-6f)));
+    }
+    __syncthreads();
+#pragma unroll
+    for (int b = 0; b < kGemvMaxB; ++b) {
+      if (b < p.B) {
+        const float r = rstd[b];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int ch = tid + i * 256;
+          if (ch < nchunk) {
+            uint4* slot = reinterpret_cast<uint4*>(xsm + (size_t)b * L.rstride + ch * 16);
+            float f[8], w[8];
+            Vec16<T>::unpack(*slot, f);
+            Vec16<T>::unpack(nw_reg[i], w);
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float a0 = rnd<T>(__fmul_rn(w[2 * e], rnd<T>(__fmul_rn(f[2 * e], r))));
+              const float a1 = rnd<T>(__fmul_rn(w[2 * e + 1], rnd<T>(__fmul_rn(f[2 * e + 1], r))));
+              const __nv_bfloat162 pr = __floats2bfloat162_rn(a0, a1);
+              o[e] = *reinterpret_cast<const uint32_t*>(&pr);
+            }
+            *slot = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int b = 0; b < kGemvMaxB; ++b) {
+      if (b < p.B) {
+        for (int ch = tid; ch < nchunk; ch += 256)
+          *reinterpret_cast<uint4*>(xsm + (size_t)b * L.rstride + ch * 16) =
+              *reinterpret_cast<const uint4*>(x + (size_t)b * p.x_stride + ch * 8);
+      }
+    }
+  }
+  if (tid == 0 && R > 0) ok_flag = mbar_wait_bounded(bar, 0, p.err);
+  __syncthreads();
+  if (!ok_flag || R == 0) return;
+
+  // ---- tensor-core product: warp w takes k-steps [w*KS/8, (w+1)*KS/8) ----
+  const int MT = (R + 15) >> 4;
+  const int KS = p.cols >> 4;
+  const int k0 = (warp * KS) >> 3, k1 = ((warp + 1) * KS) >> 3;
+  const int g = lane >> 2, t = lane & 3;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  const uint32_t wbase = smem_u32(wsm);
+  const uint32_t xrow = smem_u32(xsm) + (uint32_t)(g * L.rstride);
+  const bool gval = g < p.B;
+  for (int ks = k0; ks < k1; ++ks) {
+    uint32_t b0 = 0u, b1 = 0u;
+    if (gval) {
+      asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b0) : "r"(xrow + (uint32_t)((ks * 16 + 2 * t) * 2)));
+      asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b1) : "r"(xrow + (uint32_t)((ks * 16 + 8 + 2 * t) * 2)));
+    }
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      if (mt < MT) {
+        const int row = min(mt * 16 + (lane & 15), R - 1);
+        uint32_t a[4];
+        ldsm_x4_g(a, wbase + (uint32_t)(row * L.rstride + (ks * 2 + (lane >> 4)) * 16));
+        mma_m16n8k16(acc[mt], a, b0, b1);
+      }
+    }
+  }
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt) {
+    if (mt < MT) {
+      float* rp = red + ((size_t)(warp * 4 + mt) * 16) * 8;
+      rp[g * 8 + 2 * t] = acc[mt][0];
+      rp[g * 8 + 2 * t + 1] = acc[mt][1];
+      rp[(g + 8) * 8 + 2 * t] = acc[mt][2];
+      rp[(g + 8) * 8 + 2 * t + 1] = acc[mt][3];
+    }
+  }
+  __syncthreads();
+
+  // ---- cross-warp reduction + fused epilogue: one thread per (unit, row b)
+  const int nunits = u1 - u0;
+  for (int idx = tid; idx < nunits * p.B; idx += 256) {
+    const int uu = idx / p.B, b = idx - uu * p.B;
+    float v[RPU];
+#pragma unroll
+    for (int q = 0; q < RPU; ++q) {
+      const int rr = uu * RPU + q;
+      const int mt = rr >> 4, row = rr & 15;
+      float sacc = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) sacc += red[((w * 4 + mt) * 16 + row) * 8 + b];
+      v[q] = sacc;
+    }
+    const int u = u0 + uu;
+    if (MODE == kGemvStore) {
+      reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + p.out_offset + u] = from_f<T>(v[0]);
+    } else if (MODE == kGemvLogits) {
+      reinterpret_cast<float*>(p.out)[(size_t)b * p.out_stride + p.out_offset + u] = rnd<T>(v[0]);
+    } else if (MODE == kGemvResid) {
+      const float rv = to_f(reinterpret_cast<const T*>(p.resid)[(size_t)b * p.resid_stride + u]);
+      reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + u] = from_f<T>(__fadd_rn(rv, rnd<T>(v[0])));
+    } else if (MODE == kGemvGeglu) {
+      const float a = rnd<T>(v[0]);
+      const float gg = rnd<T>(v[RPU - 1]);
+      reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + u] = from_f<T>(__fmul_rn(gelu_approx<T>(a), gg));
+    } else {  // kGemvQKV
+      const int sect = u / p.inner, rr = u - sect * p.inner;
+      if (sect == 0) {
+        reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + rr] = from_f<T>(v[0]);
+      } else {
+        const int h = rr >> 6, cc = rr & 63;
+        T* cache = reinterpret_cast<T*>(sect == 1 ? p.kc : p.vc);
+        cache[(((size_t)b * p.H + h) * p.cap + p.pos) * 64 + cc] = from_f<T>(v[0]);
+      }
+    }
+  }
+}
+
+// Grid for the tensor-core GEMV: at least one CTA per SM when there are
+// enough units, and no CTA with more rows than fit its shared memory.
+static void mma_plan(int units, int rpu, int cols, int num_sms, int* grid, int* max_rows) {
+  const int rstride = cols * 2 + 16;
+  int cap_rows = (190 * 1024) / rstride;
+  cap_rows = min(cap_rows, kMmaMaxRows);
+  cap_rows -= cap_rows % rpu;
+  int G = min(units, num_sms);
+  const int need = (units * rpu + cap_rows - 1) / cap_rows;
+  if (need > G) G = need;
+  *grid = G;
+  *max_rows = ((units + G - 1) / G) * rpu;
+}
+
+template <bool NORM, int MODE>
+static cudaError_t launch_mma_t(const GemvParams& p, int num_sms, cudaStream_t s, bool pdl) {
+  int grid, max_rows;
+  mma_plan(p.units, MODE == kGemvGeglu ? 2 : 1, p.cols, num_sms, &grid, &max_rows);
+  if (max_rows > kMmaMaxRows || grid <= 0) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = mma_layout(p.cols, max_rows).total;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<NORM, MODE>, p, max_rows);
+}
+
+static cudaError_t launch_gemv_mma(int mode, bool norm, const GemvParams& p, int num_sms, cudaStream_t s, bool pdl) {
+  if (p.cols % 16 != 0 || p.cols > 4096 || p.B > kGemvMaxB) return cudaErrorInvalidValue;
+  switch (mode) {
+    case kGemvStore:
+      return norm ? launch_mma_t<true, kGemvStore>(p, num_sms, s, pdl) : launch_mma_t<false, kGemvStore>(p, num_sms, s, pdl);
+    case kGemvResid:
+      return norm ? launch_mma_t<true, kGemvResid>(p, num_sms, s, pdl) : launch_mma_t<false, kGemvResid>(p, num_sms, s, pdl);
+    case kGemvQKV:
+      return launch_mma_t<true, kGemvQKV>(p, num_sms, s, pdl);
+    case kGemvGeglu:
+      return launch_mma_t<true, kGemvGeglu>(p, num_sms, s, pdl);
+    case kGemvLogits:
+      return launch_mma_t<true, kGemvLogits>(p, num_sms, s, pdl);
+  }
+  return cudaErrorInvalidValue;
+}
+
+static cudaError_t set_mma_limits() {
+  cudaError_t e = cudaSuccess;
+  auto set = [&](const void* f) {
+    cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (r != cudaSuccess) e = r;
+  };
+  set((const void*)gemv_mma_kernel<true, kGemvStore>);
+  set((const void*)gemv_mma_kernel<false, kGemvStore>);
+  set((const void*)gemv_mma_kernel<true, kGemvResid>);
+  set((const void*)gemv_mma_kernel<false, kGemvResid>);
+  set((const void*)gemv_mma_kernel<true, kGemvQKV>);
+  set((const void*)gemv_mma_kernel<true, kGemvGeglu>);
+  set((const void*)gemv_mma_kernel<true, kGemvLogits>);
+  return e;
+}
+
 size_t gemv_smem_bytes(int B, int cols) {
   return (size_t)kGemvStages * kGemvStageBytes + (((size_t)B * cols * 4 + 15) & ~(size_t)15) + kGemvStages * 8;
 }
@@ -250,12 +580,13 @@ static cudaError_t dispatch_b(int mode, bool norm, const GemvParams& p, int grid
   return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_gemv(int dtype, int mode, bool norm, const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
-  const int ebytes = dtype == 1 ? 2 : 4;
+cudaError_t launch_gemv(int dtype, int mode, bool norm, const GemvParams& p, int num_sms, cudaStream_t s, bool pdl) {
+  if (p.units <= 0) return cudaSuccess;
+  if (dtype == 1) return launch_gemv_mma(mode, norm, p, num_sms, s, pdl);
   const int rpu = mode == kGemvGeglu ? 2 : 1;
-  if (p.cols % (16 / ebytes) != 0 || rpu * p.cols * ebytes > kGemvStageBytes) return cudaErrorInvalidValue;
-  if (grid <= 0) return cudaSuccess;
-  return dtype == 1 ? dispatch_b<__nv_bfloat16>(mode, norm, p, grid, s, pdl) : dispatch_b<float>(mode, norm, p, grid, s, pdl);
+  if (p.cols % 4 != 0 || rpu * p.cols * 4 > kGemvStageBytes) return cudaErrorInvalidValue;
+  const int grid = p.units < num_sms ? p.units : num_sms;
+  return dispatch_b<float>(mode, norm, p, grid, s, pdl);
 }
 
 template <typename T, int BMAX>
@@ -286,7 +617,7 @@ static cudaError_t set_limits_t() {
 }
 
 cudaError_t gemv_set_smem_limits() {
-  cudaError_t e = set_limits_t<__nv_bfloat16>();
+  cudaError_t e = set_mma_limits();
   if (e != cudaSuccess) return e;
   return set_limits_t<float>();
 }
@@ -320,12 +651,20 @@ __global__ void __launch_bounds__(128) attn_self_kernel(const AttnParams p) {
     const int j = j0 + lane;
     float sc = -INFINITY;
     if (j < p.T) {
-      const T* kr = K + (size_t)j * 64;
-      float acc = 0.f;
-#pragma unroll 16
-      for (int cc = 0; cc < 64; ++cc) acc = fmaf(qs[warp][cc], to_f(kr[cc]), acc);
-      if (bias) acc += bias[j];
-      sc = acc;
+      // 16-byte loads of key row j, four independent partial sums
+      const uint4* kr = reinterpret_cast<const uint4*>(K + (size_t)j * 64);
+      constexpr int EPC = Vec16<T>::N;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ch = 0; ch < 64 / EPC; ++ch) {
+        float kv[EPC];
+        Vec16<T>::unpack(kr[ch], kv);
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) acc[e & 3] = fmaf(qs[warp][ch * EPC + e], kv[e], acc[e & 3]);
+      }
+      float a = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      if (bias) a += bias[j];
+      sc = a;
     }
     const float cm = warp_max(sc);
     const float nm = fmaxf(m, cm);

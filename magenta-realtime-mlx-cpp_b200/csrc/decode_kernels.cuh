@@ -32,6 +32,7 @@ struct GemvParams {
   int x_stride, out_stride, resid_stride;
   int out_offset;
   int inner, H, cap, pos;  // kGemvQKV
+  int l2_keep;             // 1: keep these weights in L2 (evict_last), 0: stream them (evict_first)
 };
 
 // Bytes of one TMA stage of the GEMV kernel and the number of stages.
@@ -41,8 +42,11 @@ constexpr int kGemvThreads = 256;
 constexpr int kGemvMaxB = 8;
 
 size_t gemv_smem_bytes(int B, int cols);
-// Launch the GEMV phase over `grid` CTAs. dtype: 0 fp32, 1 bf16.
-cudaError_t launch_gemv(int dtype, int mode, bool norm, const GemvParams& p, int grid, cudaStream_t s, bool pdl);
+// Launch the GEMV phase. dtype 1 (bf16) runs the tensor-core kernel over
+// enough CTAs (at least num_sms when there are that many units) that each
+// CTA's rows fit in shared memory; dtype 0 (fp32) runs the CUDA-core kernel
+// over min(units, num_sms) CTAs.
+cudaError_t launch_gemv(int dtype, int mode, bool norm, const GemvParams& p, int num_sms, cudaStream_t s, bool pdl);
 cudaError_t gemv_set_smem_limits();
 
 struct AttnParams {

@@ -13,6 +13,7 @@
 
 #include "common.cuh"
 #include "encoder_kernels.cuh"
+#include "gemm_epilogue.cuh"
 
 namespace mrtdf {
 
@@ -51,36 +52,6 @@ __device__ __forceinline__ void mma_bf16(float* c, const uint32_t* a, uint32_t b
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
-}
-
-// ---------------------------------------------------------------------------
-// Shared epilogue: a pair of adjacent output columns (n, n + 1), n even.
-// ---------------------------------------------------------------------------
-template <typename T, int EPI>
-__device__ __forceinline__ void epi_pair(const GemmParams& p, int m, int n, float v0, float v1) {
-  if (m >= p.M || n >= p.N) return;
-  T* out = reinterpret_cast<T*>(p.out);
-  if (EPI == kEpiStore) {
-    out[(size_t)m * p.ldo + n] = from_f<T>(v0);
-    out[(size_t)m * p.ldo + n + 1] = from_f<T>(v1);
-  } else if (EPI == kEpiResid) {
-    T* o = out + (size_t)m * p.ldo + n;
-    o[0] = from_f<T>(__fadd_rn(to_f(o[0]), rnd<T>(v0)));
-    o[1] = from_f<T>(__fadd_rn(to_f(o[1]), rnd<T>(v1)));
-  } else if (EPI == kEpiGeglu) {
-    const float a = rnd<T>(v0), g = rnd<T>(v1);
-    out[(size_t)m * p.ldo + (n >> 1)] = from_f<T>(__fmul_rn(gelu_approx<T>(a), g));
-  } else {  // kEpiCrossKV
-    const int two_inner = 2 * p.inner;
-    const int layer = n / two_inner, within = n - layer * two_inner;
-    const int kv = within / p.inner, rr = within - kv * p.inner;
-    const int h = rr >> 6, cc = rr & 63;
-    const int b = m / p.S, s = m - b * p.S;
-    T* cache = reinterpret_cast<T*>(kv == 0 ? p.ck : p.cv);
-    T* dst = cache + ((((size_t)layer * p.B + b) * p.H + h) * p.Smax + s) * 64 + cc;
-    dst[0] = from_f<T>(v0);
-    dst[1] = from_f<T>(v1);
-  }
 }
 
 // ---------------------------------------------------------------------------
@@ -277,8 +248,8 @@ cudaError_t launch_gemm(int dtype, int epi, const GemmParams& p, cudaStream_t s,
 // ---------------------------------------------------------------------------
 // Encoder self-attention, bf16: flash-attention style. CTA = 64 queries of
 // one (row, head), 4 warps x 16 query rows; K/V tiles of 64 keys
-// double-buffered by cp.async; S = Q K^T and O += P V on mma.sync with P
-// rounded to bf16; online softmax in fp32 (scale 1.0, no mask).
+// double-buffered by cp.async; S = Q K^T and O += P V on mma.sync; online
+// softmax in fp32 (scale 1.0, no mask).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int swz64(int row, int chunk) { return row * 64 + ((chunk ^ (row & 7)) << 3); }
 
@@ -383,8 +354,11 @@ __global__ void __launch_bounds__(128) enc_attn_bf16_kernel(const EncAttnParams 
       scale[r] = (m_r[r] == -INFINITY) ? 0.f : expf(m_r[r] - nm[r]);
       m_r[r] = nm[r];
     }
+    // P is split as P_hi + P_lo with both halves bf16 (P_lo = bf16(P -
+    // P_hi)), and O += P_hi V + P_lo V: the probabilities keep ~16 mantissa
+    // bits, so the tensor-core result matches softmax in fp32.
     float ls[2] = {0.f, 0.f};
-    uint32_t pf[4][4];
+    uint32_t pf[4][4], pl[4][4];
 #pragma unroll
     for (int ni = 0; ni < 8; ++ni) {
       const float p0 = expf(s[ni][0] - nm[0]), p1 = expf(s[ni][1] - nm[0]);
@@ -392,13 +366,14 @@ __global__ void __launch_bounds__(128) enc_attn_bf16_kernel(const EncAttnParams 
       ls[0] += p0 + p1;
       ls[1] += p2 + p3;
       const int kk = ni >> 1;
-      if ((ni & 1) == 0) {
-        pf[kk][0] = pack_bf16(p0, p1);
-        pf[kk][1] = pack_bf16(p2, p3);
-      } else {
-        pf[kk][2] = pack_bf16(p0, p1);
-        pf[kk][3] = pack_bf16(p2, p3);
-      }
+      const int slot = (ni & 1) * 2;
+      const uint32_t h01 = pack_bf16(p0, p1), h23 = pack_bf16(p2, p3);
+      pf[kk][slot] = h01;
+      pf[kk][slot + 1] = h23;
+      const float r0 = p0 - __uint_as_float(h01 << 16), r1 = p1 - __uint_as_float(h01 & 0xffff0000u);
+      const float r2 = p2 - __uint_as_float(h23 << 16), r3 = p3 - __uint_as_float(h23 & 0xffff0000u);
+      pl[kk][slot] = pack_bf16(r0, r1);
+      pl[kk][slot + 1] = pack_bf16(r2, r3);
     }
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
@@ -424,6 +399,8 @@ __global__ void __launch_bounds__(128) enc_attn_bf16_kernel(const EncAttnParams 
         ldsm_x4_t(b0, b1, b2, b3, Vs + swz64(krow, ch));
         mma_bf16(o[2 * nj], pf[kk], b0, b1);
         mma_bf16(o[2 * nj + 1], pf[kk], b2, b3);
+        mma_bf16(o[2 * nj], pl[kk], b0, b1);
+        mma_bf16(o[2 * nj + 1], pl[kk], b2, b3);
       }
     }
     __syncthreads();

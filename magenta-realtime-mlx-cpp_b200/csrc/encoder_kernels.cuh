@@ -28,6 +28,9 @@ struct GemmParams {
 
 cudaError_t launch_gemm(int dtype, int epi, const GemmParams& p, cudaStream_t s, bool pdl);
 cudaError_t gemm_set_smem_limits();
+// bf16 GEMM on tcgen05 tensor cores with TMA-fed operands (gemm_tc.cu).
+cudaError_t launch_gemm_tc(int epi, const GemmParams& p, int* err, cudaStream_t s, bool pdl);
+cudaError_t gemm_tc_set_smem_limits();
 
 struct EncAttnParams {
   const void* qkv;  // (B*S, 3*inner): q | k | v

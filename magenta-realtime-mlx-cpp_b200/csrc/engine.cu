@@ -85,6 +85,7 @@ struct mrtdf_engine {
   int esize = 2;  // bytes per element of the compute dtype
   bool loaded = false;
   bool pdl = true;
+  bool tc_gemm = true;  // encoder GEMMs on tcgen05 (MRTDF_TC_GEMM=0 selects mma.sync)
   Arena weights;
   void* emb = nullptr;
   void* enc_norm = nullptr;
@@ -352,8 +353,6 @@ static void upload_weights(mrtdf_engine* E, const WeightSource& src) {
 // ---------------------------------------------------------------------------
 namespace {
 
-int gemv_grid(const mrtdf_engine* E, int units) { return std::min(units, E->num_sms); }
-
 void gemv(mrtdf_stream* st, int mode, bool norm, GemvParams p) {
   mrtdf_engine* E = st->eng;
   p.err = st->err;
@@ -366,7 +365,7 @@ void gemv(mrtdf_stream* st, int mode, bool norm, GemvParams p) {
   if (norm) bytes += (double)p.cols * es;
   st->gemv_launches += 1;
   st->gemv_bytes += bytes;
-  check_cuda(launch_gemv(E->c.dtype, mode, norm, p, gemv_grid(E, p.units), st->s, E->pdl), "gemv launch");
+  check_cuda(launch_gemv(E->c.dtype, mode, norm, p, E->num_sms, st->s, E->pdl), "gemv launch");
 }
 
 size_t act_bytes(const mrtdf_engine* E, size_t n) { return n * E->esize; }
@@ -374,7 +373,8 @@ size_t act_bytes(const mrtdf_engine* E, size_t n) { return n * E->esize; }
 // One DecoderLayer::forward for the stream's B rows at cache position
 // `pos` (modules.cpp:384-408). x_in is read, the layer output lands in xr.
 void enqueue_decoder_layer(mrtdf_stream* st, const DecLayerDev& L, const void* x_in, void* xr, void* kc, void* vc,
-                           int cap, int pos, const float* bias, int bias_stride, const void* ck, const void* cv) {
+                           int cap, int pos, const float* bias, int bias_stride, const void* ck, const void* cv,
+                           bool l2_keep) {
   mrtdf_engine* E = st->eng;
   const mrtdf_config& c = E->c;
   const int d = c.d_model, in = E->inner(), ff = c.d_ff;
@@ -382,7 +382,7 @@ void enqueue_decoder_layer(mrtdf_stream* st, const DecLayerDev& L, const void* x
   // 1. pre-norm + fused q/k/v, k/v appended to the cache at `pos`
   p.W = L.wqkv; p.x = x_in; p.norm_w = L.n_self; p.out = st->qb; p.kc = kc; p.vc = vc;
   p.units = 3 * in; p.cols = d; p.x_stride = d; p.out_stride = in; p.inner = in; p.H = c.num_heads;
-  p.cap = cap; p.pos = pos;
+  p.cap = cap; p.pos = pos; p.l2_keep = l2_keep;
   gemv(st, kGemvQKV, true, p);
   // 2. self attention with relative-position bias (scale 1.0)
   AttnParams a{};
@@ -392,13 +392,13 @@ void enqueue_decoder_layer(mrtdf_stream* st, const DecLayerDev& L, const void* x
   // 3. o_proj + residual
   p = GemvParams{};
   p.W = L.wo; p.x = st->ao; p.out = xr; p.resid = x_in; p.units = d; p.cols = in; p.x_stride = in;
-  p.out_stride = d; p.resid_stride = d;
+  p.out_stride = d; p.resid_stride = d; p.l2_keep = l2_keep;
   gemv(st, kGemvResid, false, p);
   if (ck) {
     // 4. pre-norm + cross q
     p = GemvParams{};
     p.W = L.wcq; p.x = xr; p.norm_w = L.n_cross; p.out = st->qb; p.units = in; p.cols = d; p.x_stride = d;
-    p.out_stride = in;
+    p.out_stride = in; p.l2_keep = l2_keep;
     gemv(st, kGemvStore, true, p);
     // 5. cross attention over the cached encoder K/V
     AttnParams ca{};
@@ -409,18 +409,18 @@ void enqueue_decoder_layer(mrtdf_stream* st, const DecLayerDev& L, const void* x
     // 6. cross o_proj + residual
     p = GemvParams{};
     p.W = L.wco; p.x = st->ao; p.out = xr; p.resid = xr; p.units = d; p.cols = in; p.x_stride = in;
-    p.out_stride = d; p.resid_stride = d;
+    p.out_stride = d; p.resid_stride = d; p.l2_keep = l2_keep;
     gemv(st, kGemvResid, false, p);
   }
   // 7. pre-norm + wi_0 / wi_1 + gelu * gate
   p = GemvParams{};
   p.W = L.wi; p.x = xr; p.norm_w = L.n_ffn; p.out = st->hb; p.units = ff; p.cols = d; p.x_stride = d;
-  p.out_stride = ff;
+  p.out_stride = ff; p.l2_keep = l2_keep;
   gemv(st, kGemvGeglu, true, p);
   // 8. wo + residual
   p = GemvParams{};
   p.W = L.wout; p.x = st->hb; p.out = xr; p.resid = xr; p.units = d; p.cols = ff; p.x_stride = ff;
-  p.out_stride = d; p.resid_stride = d;
+  p.out_stride = d; p.resid_stride = d; p.l2_keep = l2_keep;
   gemv(st, kGemvResid, false, p);
 }
 
@@ -440,7 +440,8 @@ void enqueue_temporal(mrtdf_stream* st, int f) {
     const uint8_t* ck = (const uint8_t*)st->ck + act_bytes(E, ccs * l);
     const uint8_t* cv = (const uint8_t*)st->cv + act_bytes(E, ccs * l);
     enqueue_decoder_layer(st, E->tl[l], l == 0 ? st->tin : st->tx, st->tx, tk, tv, c.max_frames, f,
-                          E->tbias + (size_t)f * c.num_heads * c.max_frames, c.max_frames, ck, cv);
+                          E->tbias + (size_t)f * c.num_heads * c.max_frames, c.max_frames, ck, cv,
+                          /*l2_keep=*/false);
   }
 }
 
@@ -453,17 +454,24 @@ void enqueue_depth(mrtdf_stream* st, int level, const void* x_in, int lo, int hi
     uint8_t* dk = (uint8_t*)st->dk + act_bytes(E, dcs * l);
     uint8_t* dv = (uint8_t*)st->dv + act_bytes(E, dcs * l);
     enqueue_decoder_layer(st, E->dl[l], l == 0 ? x_in : st->dx, st->dx, dk, dv, c.rvq_depth, level,
-                          E->dbias + (size_t)level * c.num_heads * c.rvq_depth, c.rvq_depth, nullptr, nullptr);
+                          E->dbias + (size_t)level * c.num_heads * c.rvq_depth, c.rvq_depth, nullptr, nullptr,
+                          /*l2_keep=*/true);
   }
   GemvParams p{};
   p.W = (const uint8_t*)E->lm_head + act_bytes(E, (size_t)lo * c.d_model);
   p.x = st->dx; p.norm_w = E->dec_norm; p.out = st->logits; p.units = hi - lo; p.cols = c.d_model;
-  p.x_stride = c.d_model; p.out_stride = c.vocab_size; p.out_offset = lo;
+  p.x_stride = c.d_model; p.out_stride = c.vocab_size; p.out_offset = lo; p.l2_keep = 1;
   gemv(st, kGemvLogits, true, p);
 }
 
 // encode: embed + PE, encoder layers, encoder_norm, cross K/V of every
 // temporal layer (model.cpp:226-241, modules.cpp:323-333).
+cudaError_t encoder_gemm(mrtdf_stream* st, int epi, const GemmParams& g) {
+  mrtdf_engine* E = st->eng;
+  if (E->tc_gemm && E->c.dtype == MRTDF_DTYPE_BF16) return launch_gemm_tc(epi, g, st->err, st->s, E->pdl);
+  return launch_gemm(E->c.dtype, epi, g, st->s, E->pdl);
+}
+
 void enqueue_encode(mrtdf_stream* st, int S) {
   mrtdf_engine* E = st->eng;
   const mrtdf_config& c = E->c;
@@ -478,25 +486,25 @@ void enqueue_encode(mrtdf_stream* st, int S) {
     check_cuda(launch_rmsnorm_rows(dt, st->ex, L.n_attn, M, d, st->en, st->s, pdl), "rmsnorm");
     GemmParams g{};
     g.A = st->en; g.W = L.wqkv; g.out = st->eqkv; g.M = M; g.N = 3 * in; g.K = d; g.lda = d; g.ldo = 3 * in;
-    check_cuda(launch_gemm(dt, kEpiStore, g, st->s, pdl), "gemm qkv");
+    check_cuda(encoder_gemm(st, kEpiStore, g), "gemm qkv");
     EncAttnParams a{st->eqkv, st->eo, st->B, S, c.num_heads, in};
     check_cuda(launch_enc_attention(dt, a, st->s, pdl), "enc attention");
     g = GemmParams{};
     g.A = st->eo; g.W = L.wo; g.out = st->ex; g.M = M; g.N = d; g.K = in; g.lda = in; g.ldo = d;
-    check_cuda(launch_gemm(dt, kEpiResid, g, st->s, pdl), "gemm o");
+    check_cuda(encoder_gemm(st, kEpiResid, g), "gemm o");
     check_cuda(launch_rmsnorm_rows(dt, st->ex, L.n_ffn, M, d, st->en, st->s, pdl), "rmsnorm");
     g = GemmParams{};
     g.A = st->en; g.W = L.wi; g.out = st->eh; g.M = M; g.N = 2 * ff; g.K = d; g.lda = d; g.ldo = ff;
-    check_cuda(launch_gemm(dt, kEpiGeglu, g, st->s, pdl), "gemm wi");
+    check_cuda(encoder_gemm(st, kEpiGeglu, g), "gemm wi");
     g = GemmParams{};
     g.A = st->eh; g.W = L.wout; g.out = st->ex; g.M = M; g.N = d; g.K = ff; g.lda = ff; g.ldo = d;
-    check_cuda(launch_gemm(dt, kEpiResid, g, st->s, pdl), "gemm wo");
+    check_cuda(encoder_gemm(st, kEpiResid, g), "gemm wo");
   }
   check_cuda(launch_rmsnorm_rows(dt, st->ex, E->enc_norm, M, d, st->en, st->s, pdl), "encoder_norm");
   GemmParams g{};
   g.A = st->en; g.W = E->wckv; g.out = nullptr; g.M = M; g.N = c.num_temporal_layers * 2 * in; g.K = d; g.lda = d;
   g.ck = st->ck; g.cv = st->cv; g.S = S; g.B = st->B; g.H = c.num_heads; g.Smax = c.max_encoder_length; g.inner = in;
-  check_cuda(launch_gemm(dt, kEpiCrossKV, g, st->s, pdl), "gemm cross kv");
+  check_cuda(encoder_gemm(st, kEpiCrossKV, g), "gemm cross kv");
 }
 
 void enqueue_sample(mrtdf_stream* st, int f, int level, const mrtdf_gen_opts& o, bool masked, int lo, int hi,
@@ -686,8 +694,10 @@ int mrtdf_create(const mrtdf_config* cfg, int device, mrtdf_engine** out) {
     E->num_sms = prop.multiProcessorCount;
     E->esize = cfg->dtype == MRTDF_DTYPE_BF16 ? 2 : 4;
     E->pdl = env_flag("MRTDF_PDL", true);
+    E->tc_gemm = env_flag("MRTDF_TC_GEMM", true);
     CUDA_OK(gemv_set_smem_limits());
     CUDA_OK(gemm_set_smem_limits());
+    CUDA_OK(gemm_tc_set_smem_limits());
     CUDA_OK(sample_set_smem_limits());
     *out = E.release();
   });

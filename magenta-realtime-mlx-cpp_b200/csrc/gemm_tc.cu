@@ -1,0 +1,267 @@
+// bf16 encoder GEMM on the 5th-generation tensor cores: C = A W^T with A
+// (M, K) and W (N, K) both K-major, fp32 accumulation in tensor memory.
+//
+// One 128 x 128 output tile per CTA, 128 threads:
+//   warp 0 lane 0  TMA producer: 2-D tiled loads (128 rows x 64 k, 128-byte
+//                  swizzle) of A and W into a 3-stage shared-memory ring,
+//                  completion counted on a `full` mbarrier per stage;
+//   warp 1 lane 0  MMA issuer: 4 x tcgen05.mma (M 128, N 128, K 16) per
+//                  stage into a 128-column TMEM accumulator; tcgen05.commit
+//                  frees the stage (`empty` mbarrier) once the MMAs that read
+//                  it retire, and signals `done` after the last k-tile;
+//   all 4 warps    epilogue: tcgen05.ld (32 lanes x 16 columns per load)
+//                  from the warp's TMEM lane quarter, then the fused epilogue
+//                  (store / residual add / GEGLU / cross-K/V scatter).
+// No cluster, no multicast. Every mbarrier wait is bounded and reports a
+// timeout in the stream's error word; TMEM is always released.
+//
+// Descriptor formats follow the sm_100 UMMA definitions (CUTLASS
+// cute/arch/mma_sm100_desc.hpp): shared-memory descriptor = start >> 4,
+// LBO (16-byte units) at bit 16, SBO at bit 32, version 1 at bit 46,
+// layout type at bit 61 (2 = 128-byte swizzle); instruction descriptor =
+// D format at bit 4, A / B formats at bits 7 / 10, N >> 3 at bit 17,
+// M >> 4 at bit 24.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "encoder_kernels.cuh"
+#include "gemm_epilogue.cuh"
+
+namespace mrtdf {
+
+namespace tc {
+
+constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_BYTES = BN * BK * 2;  // 16 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /* 1024-byte alignment slack */ + 256 /* barriers */;
+constexpr uint32_t TMEM_COLS = 128;
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu)  // start address
+         | ((uint64_t)1 << 16)                // LBO (unused for swizzled K-major)
+         | ((uint64_t)(1024 >> 4) << 32)      // SBO: 8 rows x 128 B
+         | ((uint64_t)1 << 46)                // version (sm_100)
+         | ((uint64_t)2 << 61);               // SWIZZLE_128B
+}
+
+constexpr uint32_t kIdesc = (1u << 4)              // D: f32
+                            | (1u << 7)            // A: bf16
+                            | (1u << 10)           // B: bf16
+                            | ((uint32_t)(BN >> 3) << 17)
+                            | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+template <int EPI>
+__global__ void __launch_bounds__(128, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmParams p, int* err) {
+  extern __shared__ uint8_t tc_smem_raw[];
+  // 1024-byte aligned base for the 128-byte-swizzled tiles
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* done = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  __shared__ int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bm = blockIdx.y * BM, bn = blockIdx.x * BN;
+  const int KT = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 32) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  pdl_launch_dependents();
+  pdl_wait();
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer ----
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES, round = kt / STAGES;
+      if (round > 0 && !mbar_wait_bounded(&empty[s], (uint32_t)((round - 1) & 1), err)) {
+        abort_flag = 1;
+        break;
+      }
+      uint8_t* sa = smem + s * STAGE_BYTES;
+      mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+      tma_load_2d(sa, &tmA, kt * BK, bm, &full[s]);
+      tma_load_2d(sa + A_BYTES, &tmB, kt * BK, bn, &full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES, round = kt / STAGES;
+      if (!mbar_wait_bounded(&full[s], (uint32_t)(round & 1), err)) {
+        abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+      const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+      for (int j = 0; j < BK / 16; ++j) {
+        // K-major 128B-swizzled tiles: the k-th 16-element slice starts 32 B further
+        mma_f16(tmem, smem_desc_sw128(sa + j * 32), smem_desc_sw128(sb + j * 32), kIdesc, (kt | j) != 0);
+      }
+      mma_commit(&empty[s]);
+    }
+    mma_commit(done);
+  }
+  __syncwarp();
+  // ---- epilogue: all four warps ----
+  // the TMEM loads below are .sync.aligned: decide CTA-uniformly
+  const bool ok = __syncthreads_and(mbar_wait_bounded(done, 0, err) ? 1 : 0) && !abort_flag;
+  tc_fence_after();
+  if (ok) {
+    const int row = bm + warp * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      uint32_t r[16];
+      tmem_ld16(lane_base + (uint32_t)c, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; i += 2)
+        epi_pair<__nv_bfloat16, EPI>(p, row, bn + c + i, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major (rows, cols) matrix with leading
+// dimension ld (elements): box 64 columns x 128 rows, 128-byte swizzle,
+// zero fill outside the matrix.
+bool make_map(CUtensorMap* m, const void* base, int rows, int cols, int ld) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BM};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int EPI>
+cudaError_t launch_t(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int* err, cudaStream_t s,
+                     bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.N + BN - 1) / BN, (p.M + BM - 1) / BM);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EPI>, a, b, p, err);
+}
+
+}  // namespace tc
+
+cudaError_t gemm_tc_set_smem_limits() {
+  cudaError_t e = cudaSuccess;
+  auto set = [&](const void* f) {
+    cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM);
+    if (r != cudaSuccess) e = r;
+  };
+  set((const void*)tc::gemm_tc_kernel<kEpiStore>);
+  set((const void*)tc::gemm_tc_kernel<kEpiResid>);
+  set((const void*)tc::gemm_tc_kernel<kEpiGeglu>);
+  set((const void*)tc::gemm_tc_kernel<kEpiCrossKV>);
+  return e;
+}
+
+cudaError_t launch_gemm_tc(int epi, const GemmParams& p, int* err, cudaStream_t s, bool pdl) {
+  if (p.M <= 0 || p.N <= 0) return cudaSuccess;
+  if (p.N % 2 != 0 || p.K % 8 != 0 || p.lda % 8 != 0) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(p.A) & 15) || (reinterpret_cast<uintptr_t>(p.W) & 15)) return cudaErrorInvalidValue;
+  CUtensorMap a, b;
+  if (!tc::make_map(&a, p.A, p.M, p.K, p.lda) || !tc::make_map(&b, p.W, p.N, p.K, p.K)) return cudaErrorInvalidValue;
+  switch (epi) {
+    case kEpiStore: return tc::launch_t<kEpiStore>(a, b, p, err, s, pdl);
+    case kEpiResid: return tc::launch_t<kEpiResid>(a, b, p, err, s, pdl);
+    case kEpiGeglu: return tc::launch_t<kEpiGeglu>(a, b, p, err, s, pdl);
+    case kEpiCrossKV: return tc::launch_t<kEpiCrossKV>(a, b, p, err, s, pdl);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace mrtdf

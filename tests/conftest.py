@@ -10,7 +10,8 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PKG = os.path.join(ROOT, "magenta-realtime-mlx-cpp_b200")
 ORACLE = os.path.join(ROOT, "oracle")
-for p in (ROOT, PKG, ORACLE):
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+for p in (ROOT, PKG, ORACLE, GOLDEN):
     if p not in sys.path:
         sys.path.insert(0, p)
 
