@@ -214,12 +214,13 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_phase_kernel(const GemvPara
 //     weights streamed);
 //   * loads its RMSNorm scale slice into registers.
 // After the wait it stages the input rows (RMS-normalised with the
-// reference's rounding) as bf16 in shared memory, then computes
+// reference's rounding) as bf16 in shared memory, lets the next kernel launch
+// (griddepcontrol.launch_dependents), then computes
 // Y[R, B] = W_slice[R, cols] . X^T with mma.sync m16n8k16 (rows as M, the
 // batch rows as N = 8, k split over the 8 warps), reduces the per-warp
 // partials through shared memory and applies the fused epilogue.
 // ---------------------------------------------------------------------------
-constexpr int kMmaMaxRows = 64;  // 4 m16 tiles per CTA
+constexpr int kMmaMaxRows = 32;  // 4 n8 tiles of weight rows per CTA
 
 __device__ __forceinline__ uint64_t l2_policy(bool keep) {
   uint64_t pol;
@@ -255,7 +256,7 @@ struct MmaLayout {
   int rstride;       // bytes per padded row (weights and inputs)
   int w_bytes;       // max_rows * rstride, rounded up to 128
   int x_bytes;       // 8 * rstride
-  int red_bytes;     // 8 warps * 4 tiles * 16 * 8 floats
+  int red_bytes;     // 8 warps * 8 n-tiles * 8 rows * 8 batch floats
   int total;
 };
 
@@ -264,13 +265,13 @@ __host__ __device__ inline MmaLayout mma_layout(int cols, int max_rows) {
   L.rstride = cols * 2 + 16;
   L.w_bytes = ((max_rows * L.rstride) + 127) & ~127;
   L.x_bytes = ((8 * L.rstride) + 127) & ~127;
-  L.red_bytes = 8 * 4 * 16 * 8 * 4;
+  L.red_bytes = 8 * 8 * 8 * 8 * 4;
   L.total = L.w_bytes + L.x_bytes + L.red_bytes + 64;
   return L;
 }
 
-template <bool NORM, int MODE>
-__global__ void __launch_bounds__(256) gemv_mma_kernel(const GemvParams p, const int max_rows) {
+template <int BMAX, int NT, bool NORM, int MODE>
+__global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, const int max_rows) {
   typedef __nv_bfloat16 T;
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int RPU = (MODE == kGemvGeglu) ? 2 : 1;
@@ -279,8 +280,8 @@ __global__ void __launch_bounds__(256) gemv_mma_kernel(const GemvParams p, const
   uint8_t* xsm = smem + L.w_bytes;
   float* red = reinterpret_cast<float*>(smem + L.w_bytes + L.x_bytes);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.w_bytes + L.x_bytes + L.red_bytes);
-  __shared__ float wred[8][kGemvMaxB];
-  __shared__ float rstd[kGemvMaxB];
+  __shared__ float wred[8][BMAX];
+  __shared__ float rstd[BMAX];
   __shared__ int ok_flag;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -291,6 +292,16 @@ __global__ void __launch_bounds__(256) gemv_mma_kernel(const GemvParams p, const
   const int row_bytes = p.cols * 2;
   const int nchunk = p.cols >> 3;  // 16-byte chunks per row
 
+  // constant RMSNorm scale slice -> registers first, ahead of the weight burst
+  uint4 nw_reg[2];
+  const T* x_ptr = reinterpret_cast<const T*>(p.x);
+  if (NORM) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int ch = tid + i * 256;
+      nw_reg[i] = ch < nchunk ? reinterpret_cast<const uint4*>(p.norm_w)[ch] : make_uint4(0, 0, 0, 0);
+    }
+  }
   if (tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
@@ -305,61 +316,69 @@ __global__ void __launch_bounds__(256) gemv_mma_kernel(const GemvParams p, const
     for (int r = lane; r < R; r += 32) bulk_g2s_hint(wsm + (size_t)r * L.rstride, src + (size_t)r * row_bytes,
                                                     (uint32_t)row_bytes, bar, pol);
   }
-  // constant RMSNorm scale slice -> registers before waiting on the producer
-  uint4 nw_reg[4];
-  if (NORM) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int ch = tid + i * 256;
-      nw_reg[i] = ch < nchunk ? reinterpret_cast<const uint4*>(p.norm_w)[ch] : make_uint4(0, 0, 0, 0);
-    }
-  }
-  pdl_launch_dependents();
   pdl_wait();
 
-  // ---- inputs -> shared memory as bf16 (RMS-normalised when NORM) --------
-  const T* x = reinterpret_cast<const T*>(p.x);
-  if (NORM) {
-    float ss[kGemvMaxB];
+  // ---- every global load of this phase, issued back to back -------------
+  // inputs: thread owns 16-byte chunks ch = tid + 256 i (i < 2: cols <= 4096)
+  uint4 xin[BMAX][2];
 #pragma unroll
-    for (int b = 0; b < kGemvMaxB; ++b) ss[b] = 0.f;
+  for (int b = 0; b < BMAX; ++b)
 #pragma unroll
-    for (int b = 0; b < kGemvMaxB; ++b) {
-      if (b < p.B) {
-        for (int ch = tid; ch < nchunk; ch += 256) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(x + (size_t)b * p.x_stride + ch * 8);
-          float f[8];
-          Vec16<T>::unpack(raw, f);
+    for (int i = 0; i < 2; ++i) {
+      const int ch = tid + i * 256;
+      xin[b][i] = (b < p.B && ch < nchunk) ? *reinterpret_cast<const uint4*>(x_ptr + (size_t)b * p.x_stride + ch * 8)
+                                          : make_uint4(0, 0, 0, 0);
+    }
+  // residual values of the epilogue (same thread -> (unit, row) mapping)
+  const int nunits = u1 - u0;
+  float resv[2];
+  if (MODE == kGemvResid) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) ss[b] = fmaf(f[e], f[e], ss[b]);
-          *reinterpret_cast<uint4*>(xsm + (size_t)b * L.rstride + ch * 16) = raw;
-        }
+    for (int i = 0; i < 2; ++i) {
+      const int idx = tid + i * 256;
+      resv[i] = 0.f;
+      if (idx < nunits * p.B) {
+        const int uu = idx / p.B, b = idx - uu * p.B;
+        resv[i] = to_f(reinterpret_cast<const T*>(p.resid)[(size_t)b * p.resid_stride + u0 + uu]);
       }
     }
+  }
+
+  // ---- inputs -> shared memory as bf16 (RMS-normalised when NORM) --------
+  if (NORM) {
+    float ss[BMAX];
 #pragma unroll
-    for (int b = 0; b < kGemvMaxB; ++b) {
-      const float v = warp_sum(ss[b]);
-      if (lane == 0) wred[warp][b] = v;
+    for (int b = 0; b < BMAX; ++b) {
+      ss[b] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        float f[8];
+        Vec16<T>::unpack(xin[b][i], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss[b] = fmaf(f[e], f[e], ss[b]);
+      }
+      ss[b] = warp_sum(ss[b]);
+    }
+    if (lane < BMAX) {
+      float v = ss[0];
+#pragma unroll
+      for (int b = 1; b < BMAX; ++b) v = lane == b ? ss[b] : v;
+      wred[warp][lane] = v;
     }
     __syncthreads();
-    if (tid < kGemvMaxB) {
-      float t = 0.f;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) t += wred[w][tid];
-      rstd[tid] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)p.cols), 1e-6f)));
-    }
-    __syncthreads();
-#pragma unroll
-    for (int b = 0; b < kGemvMaxB; ++b) {
+    for (int b = 0; b < BMAX; ++b) {
       if (b < p.B) {
-        const float r = rstd[b];
+        float t2 = 0.f;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int w = 0; w < 8; ++w) t2 += wred[w][b];
+        const float r = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(t2, (float)p.cols), 1e-6f)));
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
           const int ch = tid + i * 256;
           if (ch < nchunk) {
-            uint4* slot = reinterpret_cast<uint4*>(xsm + (size_t)b * L.rstride + ch * 16);
             float f[8], w[8];
-            Vec16<T>::unpack(*slot, f);
+            Vec16<T>::unpack(xin[b][i], f);
             Vec16<T>::unpack(nw_reg[i], w);
             uint32_t o[4];
 #pragma unroll
@@ -369,78 +388,116 @@ __global__ void __launch_bounds__(256) gemv_mma_kernel(const GemvParams p, const
               const __nv_bfloat162 pr = __floats2bfloat162_rn(a0, a1);
               o[e] = *reinterpret_cast<const uint32_t*>(&pr);
             }
-            *slot = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4*>(xsm + (size_t)b * L.rstride + ch * 16) = make_uint4(o[0], o[1], o[2], o[3]);
           }
         }
       }
     }
   } else {
 #pragma unroll
-    for (int b = 0; b < kGemvMaxB; ++b) {
-      if (b < p.B) {
-        for (int ch = tid; ch < nchunk; ch += 256)
-          *reinterpret_cast<uint4*>(xsm + (size_t)b * L.rstride + ch * 16) =
-              *reinterpret_cast<const uint4*>(x + (size_t)b * p.x_stride + ch * 8);
+    for (int b = 0; b < BMAX; ++b)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int ch = tid + i * 256;
+        if (b < p.B && ch < nchunk) *reinterpret_cast<uint4*>(xsm + (size_t)b * L.rstride + ch * 16) = xin[b][i];
       }
-    }
   }
-  if (tid == 0 && R > 0) ok_flag = mbar_wait_bounded(bar, 0, p.err);
   __syncthreads();
-  if (!ok_flag || R == 0) return;
+  // Let the next kernel launch only now: its weight prefetch then overlaps
+  // this kernel's product and epilogue instead of queueing in front of the
+  // latency-critical input loads above.
+  pdl_launch_dependents();
 
-  // ---- tensor-core product: warp w takes k-steps [w*KS/8, (w+1)*KS/8) ----
-  const int MT = (R + 15) >> 4;
+  // ---- tensor-core product --------------------------------------------
+  // D[16 x 8] = X[16 x 16] . W^T[16 x 8] per k-step: the batch rows are M
+  // (rows >= B are zero), eight weight rows are N, so one ldmatrix.x4 of W
+  // gives the B fragments of two k-steps. Warp w takes k-steps
+  // [w*KS/8, (w+1)*KS/8), two k-step pairs per iteration with every load of
+  // the iteration issued before its mma.
+  // NT (n-tiles of 8 weight rows) is a compile-time constant: runtime
+  // guards around the ldmatrix / mma blocks split the loop into small basic
+  // blocks and cost ~3x in this loop. Rows past R are clamped (their results
+  // are never read).
   const int KS = p.cols >> 4;
   const int k0 = (warp * KS) >> 3, k1 = ((warp + 1) * KS) >> 3;
   const int g = lane >> 2, t = lane & 3;
-  float acc[4][4];
+  const bool gval = g < p.B;
+  const uint32_t xrow = smem_u32(xsm) + (uint32_t)(g * L.rstride) + (uint32_t)(4 * t);
+  if (tid == 0 && R > 0) ok_flag = mbar_wait_bounded(bar, 0, p.err);
+  __syncthreads();
+  if (!ok_flag || R == 0) return;
+  float acc[NT][4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < NT; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
   const uint32_t wbase = smem_u32(wsm);
-  const uint32_t xrow = smem_u32(xsm) + (uint32_t)(g * L.rstride);
-  const bool gval = g < p.B;
-  for (int ks = k0; ks < k1; ++ks) {
-    uint32_t b0 = 0u, b1 = 0u;
-    if (gval) {
-      asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b0) : "r"(xrow + (uint32_t)((ks * 16 + 2 * t) * 2)));
-      asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b1) : "r"(xrow + (uint32_t)((ks * 16 + 8 + 2 * t) * 2)));
+  uint32_t rowaddr[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+    rowaddr[nt] = wbase + (uint32_t)(min(nt * 8 + (lane & 7), R - 1) * L.rstride + (lane >> 3) * 16);
+  // Rows g >= B of the A operand only feed rows of D that are never read,
+  // so every lane loads unconditionally.
+  int ks = k0;
+  for (; ks + 4 <= k1; ks += 4) {
+    uint32_t bw[2][NT][4];
+    uint32_t xa[4][2];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t xo = xrow + (uint32_t)((ks + q) * 32);
+      asm volatile("ld.shared.b32 %0, [%1];" : "=r"(xa[q][0]) : "r"(xo));
+      asm volatile("ld.shared.b32 %0, [%1];" : "=r"(xa[q][1]) : "r"(xo + 16));
     }
 #pragma unroll
-    for (int mt = 0; mt < 4; ++mt) {
-      if (mt < MT) {
-        const int row = min(mt * 16 + (lane & 15), R - 1);
-        uint32_t a[4];
-        ldsm_x4_g(a, wbase + (uint32_t)(row * L.rstride + (ks * 2 + (lane >> 4)) * 16));
-        mma_m16n8k16(acc[mt], a, b0, b1);
-      }
+    for (int pr = 0; pr < 2; ++pr)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) ldsm_x4_g(bw[pr][nt], rowaddr[nt] + (uint32_t)((ks + 2 * pr) * 32));
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t a[4] = {xa[q][0], 0u, xa[q][1], 0u};
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        mma_m16n8k16(acc[nt], a, bw[q >> 1][nt][2 * (q & 1)], bw[q >> 1][nt][2 * (q & 1) + 1]);
     }
   }
+  for (; ks < k1; ++ks) {  // remainder: fewer than 4 k-steps
+    uint32_t xa0, xa1;
+    const uint32_t xo = xrow + (uint32_t)(ks * 32);
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(xa0) : "r"(xo));
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(xa1) : "r"(xo + 16));
+    const uint32_t a[4] = {xa0, 0u, xa1, 0u};
 #pragma unroll
-  for (int mt = 0; mt < 4; ++mt) {
-    if (mt < MT) {
-      float* rp = red + ((size_t)(warp * 4 + mt) * 16) * 8;
-      rp[g * 8 + 2 * t] = acc[mt][0];
-      rp[g * 8 + 2 * t + 1] = acc[mt][1];
-      rp[(g + 8) * 8 + 2 * t] = acc[mt][2];
-      rp[(g + 8) * 8 + 2 * t + 1] = acc[mt][3];
+    for (int nt = 0; nt < NT; ++nt) {
+      uint32_t bw[4];
+      ldsm_x4_g(bw, rowaddr[nt] + (uint32_t)(ks * 32));  // k-steps ks, ks + 1 (the second is unused)
+      mma_m16n8k16(acc[nt], a, bw[0], bw[1]);
+    }
+  }
+  // thread (g, t), g < B, holds D[g][2t], D[g][2t+1] of each n-tile
+  if (gval) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float* rp = red + ((size_t)(warp * 8 + nt) * 8) * BMAX;
+      rp[(2 * t) * BMAX + g] = acc[nt][0];
+      rp[(2 * t + 1) * BMAX + g] = acc[nt][1];
     }
   }
   __syncthreads();
 
   // ---- cross-warp reduction + fused epilogue: one thread per (unit, row b)
-  const int nunits = u1 - u0;
-  for (int idx = tid; idx < nunits * p.B; idx += 256) {
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int idx = tid + i * 256;
+    if (idx >= nunits * p.B) break;
     const int uu = idx / p.B, b = idx - uu * p.B;
     float v[RPU];
 #pragma unroll
     for (int q = 0; q < RPU; ++q) {
       const int rr = uu * RPU + q;
-      const int mt = rr >> 4, row = rr & 15;
+      const int nt = rr >> 3, col = rr & 7;
       float sacc = 0.f;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) sacc += red[((w * 4 + mt) * 16 + row) * 8 + b];
+      for (int w = 0; w < 8; ++w) sacc += red[((w * 8 + nt) * 8 + col) * BMAX + b];
       v[q] = sacc;
     }
     const int u = u0 + uu;
@@ -449,8 +506,7 @@ __global__ void __launch_bounds__(256) gemv_mma_kernel(const GemvParams p, const
     } else if (MODE == kGemvLogits) {
       reinterpret_cast<float*>(p.out)[(size_t)b * p.out_stride + p.out_offset + u] = rnd<T>(v[0]);
     } else if (MODE == kGemvResid) {
-      const float rv = to_f(reinterpret_cast<const T*>(p.resid)[(size_t)b * p.resid_stride + u]);
-      reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + u] = from_f<T>(__fadd_rn(rv, rnd<T>(v[0])));
+      reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + u] = from_f<T>(__fadd_rn(resv[i], rnd<T>(v[0])));
     } else if (MODE == kGemvGeglu) {
       const float a = rnd<T>(v[0]);
       const float gg = rnd<T>(v[RPU - 1]);
@@ -482,11 +538,8 @@ static void mma_plan(int units, int rpu, int cols, int num_sms, int* grid, int* 
   *max_rows = ((units + G - 1) / G) * rpu;
 }
 
-template <bool NORM, int MODE>
-static cudaError_t launch_mma_t(const GemvParams& p, int num_sms, cudaStream_t s, bool pdl) {
-  int grid, max_rows;
-  mma_plan(p.units, MODE == kGemvGeglu ? 2 : 1, p.cols, num_sms, &grid, &max_rows);
-  if (max_rows > kMmaMaxRows || grid <= 0) return cudaErrorInvalidValue;
+template <int BMAX, int NT, bool NORM, int MODE>
+static cudaError_t launch_mma_nt(const GemvParams& p, int grid, int max_rows, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(256);
@@ -497,39 +550,78 @@ static cudaError_t launch_mma_t(const GemvParams& p, int num_sms, cudaStream_t s
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<NORM, MODE>, p, max_rows);
+  return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<BMAX, NT, NORM, MODE>, p, max_rows);
 }
 
-static cudaError_t launch_gemv_mma(int mode, bool norm, const GemvParams& p, int num_sms, cudaStream_t s, bool pdl) {
-  if (p.cols % 16 != 0 || p.cols > 4096 || p.B > kGemvMaxB) return cudaErrorInvalidValue;
+template <int BMAX, bool NORM, int MODE>
+static cudaError_t launch_mma_t(const GemvParams& p, int num_sms, cudaStream_t s, bool pdl) {
+  int grid, max_rows;
+  mma_plan(p.units, MODE == kGemvGeglu ? 2 : 1, p.cols, num_sms, &grid, &max_rows);
+  if (max_rows > kMmaMaxRows || grid <= 0) return cudaErrorInvalidValue;
+  switch ((max_rows + 7) / 8) {
+    case 1: return launch_mma_nt<BMAX, 1, NORM, MODE>(p, grid, max_rows, s, pdl);
+    case 2: return launch_mma_nt<BMAX, 2, NORM, MODE>(p, grid, max_rows, s, pdl);
+    case 3: return launch_mma_nt<BMAX, 3, NORM, MODE>(p, grid, max_rows, s, pdl);
+    default: return launch_mma_nt<BMAX, 4, NORM, MODE>(p, grid, max_rows, s, pdl);
+  }
+}
+
+template <int BMAX>
+static cudaError_t launch_gemv_mma_b(int mode, bool norm, const GemvParams& p, int num_sms, cudaStream_t s, bool pdl) {
   switch (mode) {
     case kGemvStore:
-      return norm ? launch_mma_t<true, kGemvStore>(p, num_sms, s, pdl) : launch_mma_t<false, kGemvStore>(p, num_sms, s, pdl);
+      return norm ? launch_mma_t<BMAX, true, kGemvStore>(p, num_sms, s, pdl)
+                  : launch_mma_t<BMAX, false, kGemvStore>(p, num_sms, s, pdl);
     case kGemvResid:
-      return norm ? launch_mma_t<true, kGemvResid>(p, num_sms, s, pdl) : launch_mma_t<false, kGemvResid>(p, num_sms, s, pdl);
+      return norm ? launch_mma_t<BMAX, true, kGemvResid>(p, num_sms, s, pdl)
+                  : launch_mma_t<BMAX, false, kGemvResid>(p, num_sms, s, pdl);
     case kGemvQKV:
-      return launch_mma_t<true, kGemvQKV>(p, num_sms, s, pdl);
+      return launch_mma_t<BMAX, true, kGemvQKV>(p, num_sms, s, pdl);
     case kGemvGeglu:
-      return launch_mma_t<true, kGemvGeglu>(p, num_sms, s, pdl);
+      return launch_mma_t<BMAX, true, kGemvGeglu>(p, num_sms, s, pdl);
     case kGemvLogits:
-      return launch_mma_t<true, kGemvLogits>(p, num_sms, s, pdl);
+      return launch_mma_t<BMAX, true, kGemvLogits>(p, num_sms, s, pdl);
   }
   return cudaErrorInvalidValue;
 }
 
-static cudaError_t set_mma_limits() {
+static cudaError_t launch_gemv_mma(int mode, bool norm, const GemvParams& p, int num_sms, cudaStream_t s, bool pdl) {
+  if (p.cols % 16 != 0 || p.cols > 4096 || p.B > kGemvMaxB || p.B <= 0) return cudaErrorInvalidValue;
+  if (p.B <= 2) return launch_gemv_mma_b<2>(mode, norm, p, num_sms, s, pdl);
+  if (p.B <= 4) return launch_gemv_mma_b<4>(mode, norm, p, num_sms, s, pdl);
+  return launch_gemv_mma_b<8>(mode, norm, p, num_sms, s, pdl);
+}
+
+template <int BMAX, int NT>
+static cudaError_t set_mma_limits_bn() {
   cudaError_t e = cudaSuccess;
   auto set = [&](const void* f) {
     cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (r != cudaSuccess) e = r;
   };
-  set((const void*)gemv_mma_kernel<true, kGemvStore>);
-  set((const void*)gemv_mma_kernel<false, kGemvStore>);
-  set((const void*)gemv_mma_kernel<true, kGemvResid>);
-  set((const void*)gemv_mma_kernel<false, kGemvResid>);
-  set((const void*)gemv_mma_kernel<true, kGemvQKV>);
-  set((const void*)gemv_mma_kernel<true, kGemvGeglu>);
-  set((const void*)gemv_mma_kernel<true, kGemvLogits>);
+  set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvStore>);
+  set((const void*)gemv_mma_kernel<BMAX, NT, false, kGemvStore>);
+  set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvResid>);
+  set((const void*)gemv_mma_kernel<BMAX, NT, false, kGemvResid>);
+  set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvQKV>);
+  set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvGeglu>);
+  set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvLogits>);
+  return e;
+}
+
+template <int BMAX>
+static cudaError_t set_mma_limits_b() {
+  cudaError_t e = set_mma_limits_bn<BMAX, 1>();
+  if (e == cudaSuccess) e = set_mma_limits_bn<BMAX, 2>();
+  if (e == cudaSuccess) e = set_mma_limits_bn<BMAX, 3>();
+  if (e == cudaSuccess) e = set_mma_limits_bn<BMAX, 4>();
+  return e;
+}
+
+static cudaError_t set_mma_limits() {
+  cudaError_t e = set_mma_limits_b<2>();
+  if (e == cudaSuccess) e = set_mma_limits_b<4>();
+  if (e == cudaSuccess) e = set_mma_limits_b<8>();
   return e;
 }
 
@@ -622,6 +714,18 @@ cudaError_t gemv_set_smem_limits() {
   return set_limits_t<float>();
 }
 
+// Two consecutive elements of T as floats (one 4- or 8-byte load).
+template <typename T>
+__device__ __forceinline__ float2 load2(const T* p);
+template <>
+__device__ __forceinline__ float2 load2<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+template <>
+__device__ __forceinline__ float2 load2<float>(const float* p) {
+  return *reinterpret_cast<const float2*>(p);
+}
+
 // ---------------------------------------------------------------------------
 // Self-attention for one new query (decode), one warp per (row, head):
 // lane j scores key j of each 32-key chunk, online softmax over chunks,
@@ -631,8 +735,8 @@ cudaError_t gemv_set_smem_limits() {
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(128) attn_self_kernel(const AttnParams p) {
-  pdl_launch_dependents();
   pdl_wait();
+  pdl_launch_dependents();
   __shared__ float qs[4][64];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gw = blockIdx.x * 4 + warp;
@@ -666,6 +770,11 @@ __global__ void __launch_bounds__(128) attn_self_kernel(const AttnParams p) {
       if (bias) a += bias[j];
       sc = a;
     }
+    // all V values this lane needs for the chunk, issued together
+    const int nj = min(32, p.T - j0);
+    float2 vv[32];
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) vv[jj] = jj < nj ? load2<T>(V + (size_t)(j0 + jj) * 64 + 2 * lane) : make_float2(0.f, 0.f);
     const float cm = warp_max(sc);
     const float nm = fmaxf(m, cm);
     const float scale = (m == -INFINITY) ? 0.f : expf(m - nm);
@@ -673,12 +782,11 @@ __global__ void __launch_bounds__(128) attn_self_kernel(const AttnParams p) {
     l = l * scale + warp_sum(pj);
     o0 *= scale;
     o1 *= scale;
-    const int nj = min(32, p.T - j0);
-    for (int jj = 0; jj < nj; ++jj) {
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) {
       const float pw = __shfl_sync(0xffffffffu, pj, jj);
-      const T* vr = V + (size_t)(j0 + jj) * 64;
-      o0 = fmaf(pw, to_f(vr[2 * lane]), o0);
-      o1 = fmaf(pw, to_f(vr[2 * lane + 1]), o1);
+      o0 = fmaf(pw, vv[jj].x, o0);
+      o1 = fmaf(pw, vv[jj].y, o1);
     }
     m = nm;
   }
@@ -695,8 +803,8 @@ __global__ void __launch_bounds__(128) attn_self_kernel(const AttnParams p) {
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(128) attn_cross_kernel(const AttnParams p) {
-  pdl_launch_dependents();
   pdl_wait();
+  pdl_launch_dependents();
   __shared__ float qs[64];
   __shared__ float wm[4], wl[4], wo[4][64];
   __shared__ int is_last;
@@ -726,6 +834,10 @@ __global__ void __launch_bounds__(128) attn_cross_kernel(const AttnParams p) {
       }
       sc = acc;
     }
+    const int nj = min(32, k1 - j0);
+    float2 vv[32];
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) vv[jj] = jj < nj ? load2<T>(V + (size_t)(j0 + jj) * 64 + 2 * lane) : make_float2(0.f, 0.f);
     const float cm = warp_max(sc);
     const float nm = fmaxf(m, cm);
     const float scale = (m == -INFINITY) ? 0.f : expf(m - nm);
@@ -733,12 +845,11 @@ __global__ void __launch_bounds__(128) attn_cross_kernel(const AttnParams p) {
     l = l * scale + warp_sum(pj);
     o0 *= scale;
     o1 *= scale;
-    const int nj = min(32, k1 - j0);
-    for (int jj = 0; jj < nj; ++jj) {
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) {
       const float pw = __shfl_sync(0xffffffffu, pj, jj);
-      const T* vr = V + (size_t)(j0 + jj) * 64;
-      o0 = fmaf(pw, to_f(vr[2 * lane]), o0);
-      o1 = fmaf(pw, to_f(vr[2 * lane + 1]), o1);
+      o0 = fmaf(pw, vv[jj].x, o0);
+      o1 = fmaf(pw, vv[jj].y, o1);
     }
     m = nm;
   }
@@ -818,17 +929,18 @@ cudaError_t launch_attn_cross(int dtype, const AttnParams& p, cudaStream_t s, bo
 }
 
 // ---------------------------------------------------------------------------
-// Sampler: one CTA of 1024 threads per sequence.
+// Sampler: one CTA of 256 threads per sequence.
 //   guided = CFG mix of the sequence's two rows (fp32), restricted to the
 //   candidate range [lo, hi) (the level's vocab mask); temperature 0 ->
 //   argmax (first index on ties); else scaled = guided / T, threshold = the
-//   top_k-th largest scaled value (radix select on order-preserving keys;
-//   ties at the threshold survive), token = argmax(scaled + Gumbel(u)) over
-//   the survivors. Then the embedding of the token becomes the next depth
-//   input of every row of the sequence and is added into the frame sum;
-//   on the last level the next temporal input R(sum / depth) is written.
+//   top_k-th largest scaled value (exact radix select over order-preserving
+//   keys, 8 bits per pass, warp-aggregated shared histogram; ties at the
+//   threshold survive), token = argmax(scaled + Gumbel(u)) over the
+//   survivors. Then the embedding of the token becomes the next depth input
+//   of every row of the sequence and is added into the frame sum; on the
+//   last level the next temporal input R(sum / depth) is written.
 // ---------------------------------------------------------------------------
-constexpr int kSampleThreads = 1024;
+constexpr int kSampleThreads = 256;
 
 __device__ __forceinline__ void argmax_combine(float& v, int& i, float v2, int i2) {
   if (v2 > v || (v2 == v && i2 < i)) {
@@ -839,13 +951,13 @@ __device__ __forceinline__ void argmax_combine(float& v, int& i, float v2, int i
 
 template <typename T>
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleParams p) {
-  pdl_launch_dependents();
   pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ __align__(16) float vals[];
   __shared__ unsigned hist[256];
   __shared__ unsigned sel_prefix, sel_k;
-  __shared__ float rv[32];
-  __shared__ int ri[32];
+  __shared__ float rv[kSampleThreads / 32];
+  __shared__ int ri[kSampleThreads / 32];
   __shared__ int tok_s;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int seq = blockIdx.x;
@@ -863,22 +975,27 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
       if (p.temperature != 0.0f) g = __fdiv_rn(g, p.temperature);
       vals[i] = g;
     }
+    if (tid == 0) {
+      sel_prefix = 0u;
+      sel_k = (unsigned)p.top_k;
+    }
     __syncthreads();
     float thr = -INFINITY;
     if (p.temperature != 0.0f && p.top_k > 0 && p.top_k < n) {
-      if (tid == 0) {
-        sel_prefix = 0u;
-        sel_k = (unsigned)p.top_k;
-      }
       unsigned mask = 0u;
       for (int pass = 0; pass < 4; ++pass) {
         const int shift = 24 - 8 * pass;
-        if (tid < 256) hist[tid] = 0u;
+        hist[tid] = 0u;
         __syncthreads();
         const unsigned prefix = sel_prefix;
-        for (int i = tid; i < n; i += kSampleThreads) {
-          const unsigned key = float_order_key(vals[i]);
-          if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        for (int i0 = 0; i0 < n; i0 += kSampleThreads) {
+          const int i = i0 + tid;
+          const unsigned key = i < n ? float_order_key(vals[i]) : 0u;
+          const bool in = i < n && (key & mask) == prefix;
+          const unsigned dg = in ? ((key >> shift) & 255u) : 256u + (unsigned)lane;  // unique no-op digit
+          // lanes holding the same digit add once, through their leader
+          const unsigned peers = __match_any_sync(0xffffffffu, dg);
+          if (in && lane == (__ffs(peers) - 1)) atomicAdd(&hist[dg], (unsigned)__popc(peers));
         }
         __syncthreads();
         if (warp == 0) {
@@ -892,14 +1009,12 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
           unsigned incl = tot;
 #pragma unroll
           for (int o = 1; o < 32; o <<= 1) {
-            const unsigned t = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += t;
+            const unsigned t2 = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t2;
           }
           const unsigned excl = incl - tot;
           const unsigned kk = sel_k;
-          const bool mine = excl < kk && incl >= kk;
-          const unsigned ballot = __ballot_sync(0xffffffffu, mine);
-          if (mine) {
+          if (excl < kk && incl >= kk) {
             unsigned cum = excl;
             int dg = 255 - 8 * lane;
             for (int q = 0; q < 8; ++q) {
@@ -912,7 +1027,6 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
             sel_prefix = prefix | ((unsigned)dg << shift);
             sel_k = kk - cum;
           }
-          (void)ballot;
         }
         mask |= 255u << shift;
         __syncthreads();
@@ -947,16 +1061,11 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
       ri[warp] = bi;
     }
     __syncthreads();
-    if (warp == 0) {
-      best = rv[lane];
-      bi = ri[lane];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
-        const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
-        argmax_combine(best, bi, v2, i2);
-      }
-      if (lane == 0) tok_s = p.lo + (bi == 0x7fffffff ? 0 : bi);
+    if (tid == 0) {
+      best = rv[0];
+      bi = ri[0];
+      for (int w = 1; w < kSampleThreads / 32; ++w) argmax_combine(best, bi, rv[w], ri[w]);
+      tok_s = p.lo + (bi == 0x7fffffff ? 0 : bi);
     }
     __syncthreads();
     token = tok_s;
@@ -967,18 +1076,25 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
   }
   if (tid == 0 && p.tokens) p.tokens[(size_t)seq * p.tok_stride + p.tok_index] = token;
 
-  const T* e = reinterpret_cast<const T*>(p.emb) + (size_t)token * p.d;
-  T* din = reinterpret_cast<T*>(p.din);
-  T* fs = reinterpret_cast<T*>(p.fsum);
-  T* tin = reinterpret_cast<T*>(p.tin);
-  for (int r = 0; r < p.rows_per_seq; ++r) {
-    const size_t row = (size_t)(r0 + r) * p.d;
-    for (int i = tid; i < p.d; i += kSampleThreads) {
-      const T ev = e[i];
-      din[row + i] = ev;
-      const float s = p.is_first ? to_f(ev) : rnd<T>(__fadd_rn(to_f(fs[row + i]), to_f(ev)));
-      fs[row + i] = from_f<T>(s);
-      if (p.is_last) tin[row + i] = from_f<T>(__fdiv_rn(s, (float)p.depth));
+  // embedding feedback, 16 bytes per thread per row
+  constexpr int EPC = Vec16<T>::N;
+  const uint4* e = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.emb) + (size_t)token * p.d);
+  const int nchunk = p.d / EPC;
+  for (int ch = tid; ch < nchunk; ch += kSampleThreads) {
+    const uint4 ev = e[ch];
+    float ef[EPC];
+    Vec16<T>::unpack(ev, ef);
+    for (int r = 0; r < p.rows_per_seq; ++r) {
+      const size_t off = (size_t)(r0 + r) * p.d + (size_t)ch * EPC;
+      *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.din) + off) = ev;
+      T* fs = reinterpret_cast<T*>(p.fsum) + off;
+      T* tin = reinterpret_cast<T*>(p.tin) + off;
+#pragma unroll
+      for (int q = 0; q < EPC; ++q) {
+        const float sum = p.is_first ? ef[q] : rnd<T>(__fadd_rn(to_f(fs[q]), ef[q]));
+        fs[q] = from_f<T>(sum);
+        if (p.is_last) tin[q] = from_f<T>(__fdiv_rn(sum, (float)p.depth));
+      }
     }
   }
 }
