@@ -15,6 +15,8 @@
 // accumulate in fp32.
 #include <cuda_bf16.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "decode_kernels.cuh"
 
@@ -714,81 +716,114 @@ cudaError_t gemv_set_smem_limits() {
   return set_limits_t<float>();
 }
 
-// Two consecutive elements of T as floats (one 4- or 8-byte load).
+// ---------------------------------------------------------------------------
+// Self-attention for one new query (decode), one warp per (row, head),
+// at most 64 keys (2 chunks of 32). Every load is issued right after the
+// dependency wait - q, key row j for lane j, and each lane's two value
+// columns of every key - so the kernel pays one L2 round trip; then lane j
+// scores key j, a warp softmax, and lane l accumulates output dims 2l, 2l+1.
+// Scale 1.0, additive bias (relative-position bias of this query position,
+// in the compute dtype's values).
+// ---------------------------------------------------------------------------
+constexpr int kSelfAttnMaxT = 64;
+
 template <typename T>
-__device__ __forceinline__ float2 load2(const T* p);
+__device__ __forceinline__ uint32_t load_pair_bits(const T* p);
 template <>
-__device__ __forceinline__ float2 load2<__nv_bfloat16>(const __nv_bfloat16* p) {
-  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+__device__ __forceinline__ uint32_t load_pair_bits<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return *reinterpret_cast<const uint32_t*>(p);
 }
+template <typename T>
+__device__ __forceinline__ float2 pair_from_bits(uint32_t v);
 template <>
-__device__ __forceinline__ float2 load2<float>(const float* p) {
-  return *reinterpret_cast<const float2*>(p);
+__device__ __forceinline__ float2 pair_from_bits<__nv_bfloat16>(uint32_t v) {
+  return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
 }
 
-// ---------------------------------------------------------------------------
-// Self-attention for one new query (decode), one warp per (row, head):
-// lane j scores key j of each 32-key chunk, online softmax over chunks,
-// lane l accumulates output dims 2l, 2l+1. Scale 1.0, additive bias
-// (relative-position bias of this query position, already in the compute
-// dtype's values).
-// ---------------------------------------------------------------------------
+template <typename T>
+struct PairReg {  // two consecutive elements kept in registers
+  typedef typename std::conditional<sizeof(T) == 2, uint32_t, float2>::type type;
+};
+
+template <typename T>
+__device__ __forceinline__ typename PairReg<T>::type load_pair(const T* p) {
+  if constexpr (sizeof(T) == 2) return load_pair_bits<T>(p);
+  else return *reinterpret_cast<const float2*>(p);
+}
+template <typename T>
+__device__ __forceinline__ float2 unpack_pair(typename PairReg<T>::type v) {
+  if constexpr (sizeof(T) == 2) return pair_from_bits<T>(v);
+  else return v;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(128) attn_self_kernel(const AttnParams p) {
   pdl_wait();
-  pdl_launch_dependents();
   __shared__ float qs[4][64];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gw = blockIdx.x * 4 + warp;
-  if (gw >= p.B * p.H) return;
-  const int b = gw / p.H, h = gw - b * p.H;
-  const T* q = reinterpret_cast<const T*>(p.q) + (size_t)b * p.inner + h * 64;
-  qs[warp][2 * lane] = to_f(q[2 * lane]);
-  qs[warp][2 * lane + 1] = to_f(q[2 * lane + 1]);
-  __syncwarp();
+  const bool active = gw < p.B * p.H;
+  const int b = active ? gw / p.H : 0, h = active ? gw - b * p.H : 0;
   const size_t base = ((size_t)b * p.H + h) * p.cap * 64;
   const T* K = reinterpret_cast<const T*>(p.K) + base;
   const T* V = reinterpret_cast<const T*>(p.V) + base;
-  const float* bias = p.bias ? p.bias + (size_t)h * p.bias_stride : nullptr;
-  float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
-  for (int j0 = 0; j0 < p.T; j0 += 32) {
-    const int j = j0 + lane;
-    float sc = -INFINITY;
-    if (j < p.T) {
-      // 16-byte loads of key row j, four independent partial sums
-      const uint4* kr = reinterpret_cast<const uint4*>(K + (size_t)j * 64);
-      constexpr int EPC = Vec16<T>::N;
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  constexpr int EPC = Vec16<T>::N;
+  // ---- all loads ----
+  const float2 qv = unpack_pair<T>(load_pair<T>(reinterpret_cast<const T*>(p.q) + (size_t)b * p.inner + h * 64 + 2 * lane));
+  uint4 kr[2][64 / EPC];
+  typename PairReg<T>::type vr[2][32];
 #pragma unroll
-      for (int ch = 0; ch < 64 / EPC; ++ch) {
-        float kv[EPC];
-        Vec16<T>::unpack(kr[ch], kv);
+  for (int c = 0; c < 2; ++c) {
+    const int j = c * 32 + lane;
+    const bool kv = active && j < p.T;
 #pragma unroll
-        for (int e = 0; e < EPC; ++e) acc[e & 3] = fmaf(qs[warp][ch * EPC + e], kv[e], acc[e & 3]);
-      }
-      float a = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-      if (bias) a += bias[j];
-      sc = a;
-    }
-    // all V values this lane needs for the chunk, issued together
-    const int nj = min(32, p.T - j0);
-    float2 vv[32];
-#pragma unroll
-    for (int jj = 0; jj < 32; ++jj) vv[jj] = jj < nj ? load2<T>(V + (size_t)(j0 + jj) * 64 + 2 * lane) : make_float2(0.f, 0.f);
-    const float cm = warp_max(sc);
-    const float nm = fmaxf(m, cm);
-    const float scale = (m == -INFINITY) ? 0.f : expf(m - nm);
-    const float pj = (j < p.T) ? expf(sc - nm) : 0.f;
-    l = l * scale + warp_sum(pj);
-    o0 *= scale;
-    o1 *= scale;
+    for (int ch = 0; ch < 64 / EPC; ++ch)
+      kr[c][ch] = kv ? reinterpret_cast<const uint4*>(K + (size_t)j * 64)[ch] : make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int jj = 0; jj < 32; ++jj) {
-      const float pw = __shfl_sync(0xffffffffu, pj, jj);
-      o0 = fmaf(pw, vv[jj].x, o0);
-      o1 = fmaf(pw, vv[jj].y, o1);
+      const int jv = c * 32 + jj;
+      vr[c][jj] = (active && jv < p.T) ? load_pair<T>(V + (size_t)jv * 64 + 2 * lane) : typename PairReg<T>::type{};
     }
-    m = nm;
+  }
+  const float bias0 = (active && p.bias && lane < p.T) ? p.bias[(size_t)h * p.bias_stride + lane] : 0.f;
+  const float bias1 = (active && p.bias && 32 + lane < p.T) ? p.bias[(size_t)h * p.bias_stride + 32 + lane] : 0.f;
+  pdl_launch_dependents();
+  if (!active) return;
+  qs[warp][2 * lane] = qv.x;
+  qs[warp][2 * lane + 1] = qv.y;
+  __syncwarp();
+  // ---- scores: lane j <-> key j of each chunk ----
+  float sc[2];
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const int j = c * 32 + lane;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ch = 0; ch < 64 / EPC; ++ch) {
+      float kf[EPC];
+      Vec16<T>::unpack(kr[c][ch], kf);
+#pragma unroll
+      for (int e = 0; e < EPC; ++e) acc[e & 3] = fmaf(qs[warp][ch * EPC + e], kf[e], acc[e & 3]);
+    }
+    float a = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    if (p.bias) a += (c == 0 ? bias0 : bias1);
+    sc[c] = j < p.T ? a : -INFINITY;
+  }
+  const float m = warp_max(fmaxf(sc[0], sc[1]));
+  const float p0 = lane < p.T ? expf(sc[0] - m) : 0.f;
+  const float p1 = 32 + lane < p.T ? expf(sc[1] - m) : 0.f;
+  const float l = warp_sum(p0 + p1);
+  float o0 = 0.f, o1 = 0.f;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const float pc = c == 0 ? p0 : p1;
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) {
+      const float pw = __shfl_sync(0xffffffffu, pc, jj);
+      const float2 v = unpack_pair<T>(vr[c][jj]);
+      o0 = fmaf(pw, v.x, o0);
+      o1 = fmaf(pw, v.y, o1);
+    }
   }
   T* out = reinterpret_cast<T*>(p.out) + (size_t)b * p.inner + h * 64;
   out[2 * lane] = from_f<T>(o0 / l);
@@ -804,40 +839,48 @@ __global__ void __launch_bounds__(128) attn_self_kernel(const AttnParams p) {
 template <typename T>
 __global__ void __launch_bounds__(128) attn_cross_kernel(const AttnParams p) {
   pdl_wait();
-  pdl_launch_dependents();
-  __shared__ float qs[64];
+  __shared__ float qs[4][64];
   __shared__ float wm[4], wl[4], wo[4][64];
   __shared__ int is_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int bh = blockIdx.x, sp = blockIdx.y;
   const int b = bh / p.H, h = bh - b * p.H;
-  if (threadIdx.x < 64) qs[threadIdx.x] = to_f(reinterpret_cast<const T*>(p.q)[(size_t)b * p.inner + h * 64 + threadIdx.x]);
-  __syncthreads();
   const size_t base = ((size_t)b * p.H + h) * p.cap * 64;
   const T* K = reinterpret_cast<const T*>(p.K) + base;
   const T* V = reinterpret_cast<const T*>(p.V) + base;
   const int k0 = (int)(((long long)sp * p.T) / p.nsplit), k1 = (int)(((long long)(sp + 1) * p.T) / p.nsplit);
+  constexpr int EPC = Vec16<T>::N;
   float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
+  bool first = true;
   for (int j0 = k0 + warp * 32; j0 < k1; j0 += 128) {
+    // ---- every load of this 32-key chunk (and q), back to back ----
     const int j = j0 + lane;
-    float sc = -INFINITY;
-    if (j < k1) {
-      const uint4* kr = reinterpret_cast<const uint4*>(K + (size_t)j * 64);
-      float acc = 0.f;
-      constexpr int EPC = Vec16<T>::N;
-#pragma unroll
-      for (int ch = 0; ch < 64 / EPC; ++ch) {
-        float kv[EPC];
-        Vec16<T>::unpack(kr[ch], kv);
-#pragma unroll
-        for (int e = 0; e < EPC; ++e) acc = fmaf(qs[ch * EPC + e], kv[e], acc);
-      }
-      sc = acc;
-    }
     const int nj = min(32, k1 - j0);
-    float2 vv[32];
+    uint4 kr[64 / EPC];
 #pragma unroll
-    for (int jj = 0; jj < 32; ++jj) vv[jj] = jj < nj ? load2<T>(V + (size_t)(j0 + jj) * 64 + 2 * lane) : make_float2(0.f, 0.f);
+    for (int ch = 0; ch < 64 / EPC; ++ch)
+      kr[ch] = j < k1 ? reinterpret_cast<const uint4*>(K + (size_t)j * 64)[ch] : make_uint4(0, 0, 0, 0);
+    typename PairReg<T>::type vr[32];
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj)
+      vr[jj] = jj < nj ? load_pair<T>(V + (size_t)(j0 + jj) * 64 + 2 * lane) : typename PairReg<T>::type{};
+    if (first) {
+      const float2 qv =
+          unpack_pair<T>(load_pair<T>(reinterpret_cast<const T*>(p.q) + (size_t)b * p.inner + h * 64 + 2 * lane));
+      qs[warp][2 * lane] = qv.x;
+      qs[warp][2 * lane + 1] = qv.y;
+      __syncwarp();
+      first = false;
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ch = 0; ch < 64 / EPC; ++ch) {
+      float kf[EPC];
+      Vec16<T>::unpack(kr[ch], kf);
+#pragma unroll
+      for (int e = 0; e < EPC; ++e) acc[e & 3] = fmaf(qs[warp][ch * EPC + e], kf[e], acc[e & 3]);
+    }
+    const float sc = j < k1 ? (acc[0] + acc[1]) + (acc[2] + acc[3]) : -INFINITY;
     const float cm = warp_max(sc);
     const float nm = fmaxf(m, cm);
     const float scale = (m == -INFINITY) ? 0.f : expf(m - nm);
@@ -848,11 +891,13 @@ __global__ void __launch_bounds__(128) attn_cross_kernel(const AttnParams p) {
 #pragma unroll
     for (int jj = 0; jj < 32; ++jj) {
       const float pw = __shfl_sync(0xffffffffu, pj, jj);
-      o0 = fmaf(pw, vv[jj].x, o0);
-      o1 = fmaf(pw, vv[jj].y, o1);
+      const float2 v = unpack_pair<T>(vr[jj]);
+      o0 = fmaf(pw, v.x, o0);
+      o1 = fmaf(pw, v.y, o1);
     }
     m = nm;
   }
+  pdl_launch_dependents();
   if (lane == 0) {
     wm[warp] = m;
     wl[warp] = l;
@@ -917,6 +962,7 @@ static cudaError_t launch_k(void (*kern)(const P), dim3 grid, dim3 block, size_t
 }
 
 cudaError_t launch_attn_self(int dtype, const AttnParams& p, cudaStream_t s, bool pdl) {
+  if (p.T > kSelfAttnMaxT) return cudaErrorInvalidValue;
   const dim3 grid((p.B * p.H + 3) / 4);
   return dtype == 1 ? launch_k(attn_self_kernel<__nv_bfloat16>, grid, dim3(128), 0, s, pdl, p)
                     : launch_k(attn_self_kernel<float>, grid, dim3(128), 0, s, pdl, p);

@@ -424,6 +424,10 @@ std::string config_check(const mrtdf_config& c) {
   if (c.max_frames <= 0 || c.rvq_depth <= 0 || c.max_encoder_length <= 0) return "lengths must be positive";
   if (c.dtype != MRTDF_DTYPE_FP32 && c.dtype != MRTDF_DTYPE_BF16) return "dtype must be fp32 or bf16";
   if (c.temporal_num_buckets < 2 || c.depth_num_buckets < 2) return "need at least 2 buckets";
+  // decode self-attention handles up to 64 keys; split-K cross attention up to
+  // 8 x 128 encoder positions
+  if (c.max_frames > 64 || c.rvq_depth > 64) return "max_frames and rvq_depth must be <= 64";
+  if (c.max_encoder_length > 1024) return "max_encoder_length must be <= 1024";
   return "";
 }
 
