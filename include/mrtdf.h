@@ -185,6 +185,32 @@ int mrtdf_sample(mrtdf_engine* eng, const float* logits, int cfg, int frame, int
  * `seeds` holds one seed per sequence (NULL: opts->seed + sequence index).
  * The whole chunk runs as one CUDA graph, captured on first use.
  */
+/*
+ * mrtdf_sample for callers that cannot allocate GPU memory. No counterpart
+ * in the reference: it exists for hosts that must not call cudaMalloc /
+ * cudaFree on their decode thread - a real-time audio callback, where the
+ * implicit device synchronisation and unbounded latency of an allocation
+ * would glitch playback, or an embedding application that reserves all GPU
+ * memory up front and forbids allocations afterwards.
+ *
+ * Same semantics and result as mrtdf_sample, but `logits_dev` ((cfg ? 2 : 1)
+ * x vocab_size float32), `uniforms_dev` (vocab_size floats, or NULL for the
+ * Philox draws of opts->seed) and `token_dev` (one int32) are DEVICE
+ * pointers owned by the caller, the work is queued on `stream` (a
+ * cudaStream_t, NULL = the legacy default stream) and the call does not
+ * wait for it. The sampler's scratch is a fixed 64 KiB device array inside
+ * the library, held by every GPU that loads it until the process exits:
+ * rows x d_model x dtype bytes must be <= 21,760 (MRTDF_ERR_RANGE
+ * otherwise); nothing in it needs to start at zero, each call writes what
+ * its kernel reads. The first call on a device looks up that array's address;
+ * make it before any stream capture. All calls on a device share the
+ * scratch, so calls that may overlap on the GPU race; serialise them (one
+ * stream). Allocates nothing: no cudaMalloc, cudaFree or allocating
+ * library routine.
+ */
+int mrtdf_sample_noalloc(mrtdf_engine* eng, const float* logits_dev, int cfg, int frame, int level,
+                         const mrtdf_gen_opts* opts, const float* uniforms_dev, int32_t* token_dev, void* stream);
+
 int mrtdf_generate_tokens(mrtdf_stream* st, const int32_t* enc_ids, int seq_len,
                           const mrtdf_gen_opts* opts, const uint64_t* seeds, int32_t* out_ids);
 

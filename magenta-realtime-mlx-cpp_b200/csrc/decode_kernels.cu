@@ -15,6 +15,7 @@
 // accumulate in fp32.
 #include <cuda_bf16.h>
 
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -1159,6 +1160,40 @@ cudaError_t launch_sample(int dtype, const SampleParams& p, int num_seq, cudaStr
   if (smem > (size_t)kSampleMaxSmem) return cudaErrorInvalidValue;
   return dtype == 1 ? launch_k(sample_kernel<__nv_bfloat16>, dim3(num_seq), dim3(kSampleThreads), smem, s, pdl, p)
                     : launch_k(sample_kernel<float>, dim3(num_seq), dim3(kSampleThreads), smem, s, pdl, p);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free sampling (mrtdf_sample_noalloc): the sampler's scratch -
+// the seed word, the error word and the three embedding-feedback rows it
+// writes - lives in this fixed device array instead of cudaMalloc'd buffers.
+// Every GPU that loads the library holds these 64 KiB until process exit;
+// all calls on a device share them, so calls that overlap on the GPU race.
+// Nothing in it has to start at zero: each call zeroes the error word and
+// writes the seed (stream-ordered, before its kernel), and the kernel writes
+// the feedback rows without reading them (first level, not last).
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_sample_scratch[kSampleScratchBytes];
+
+cudaError_t sample_scratch_address(int device, void** out) {
+  // One lookup per device, made with that device current: in host code the
+  // array's name is only a stand-in, its device address comes from the runtime.
+  static std::mutex mu;
+  static void* addr[128] = {};
+  if (device < 0 || device >= 128) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[device]) {
+    int prev = 0;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return e;
+    if (prev != device && (e = cudaSetDevice(device)) != cudaSuccess) return e;
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_sample_scratch);
+    if (prev != device) cudaSetDevice(prev);
+    if (e != cudaSuccess) return e;
+    addr[device] = p;
+  }
+  *out = addr[device];
+  return cudaSuccess;
 }
 
 // ---------------------------------------------------------------------------

@@ -96,6 +96,14 @@ size_t sample_smem_bytes(int n_candidates);
 cudaError_t sample_set_smem_limits();
 constexpr int kSampleMaxSmem = 160 * 1024;
 
+// Fixed device scratch of the allocation-free sampler: 256 bytes of words
+// (seed at 0, error word at 8) then three feedback rows of up to
+// kSampleScratchRowBytes each.
+constexpr size_t kSampleScratchBytes = 64 * 1024;
+constexpr size_t kSampleScratchRowBytes = (kSampleScratchBytes - 256) / 3 / 256 * 256;
+// Device address of that scratch on `device` (looked up once per device).
+cudaError_t sample_scratch_address(int device, void** out);
+
 // out[r, :] = emb[ids[r], :] for r < rows (ids == null: id 0 = PAD).
 cudaError_t launch_embed_rows(int dtype, const void* emb, const int32_t* ids, int rows, int d, void* out,
                               cudaStream_t s, bool pdl);

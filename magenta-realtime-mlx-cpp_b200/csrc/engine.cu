@@ -978,6 +978,48 @@ int mrtdf_sample(mrtdf_engine* E, const float* logits, int cfg, int frame, int l
   });
 }
 
+int mrtdf_sample_noalloc(mrtdf_engine* E, const float* logits_dev, int cfg, int frame, int level,
+                         const mrtdf_gen_opts* o, const float* uniforms_dev, int32_t* token_dev, void* stream) {
+  return guarded([&] {
+    if (!E || !logits_dev || !o || !token_dev) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    if (!E->loaded) throw Error{MRTDF_ERR_STATE, "weights not loaded"};
+    const mrtdf_config& c = E->c;
+    if (level < 0 || level >= c.rvq_depth || frame < 0) throw Error{MRTDF_ERR_RANGE, "level / frame out of range"};
+    if (!o->use_vocab_masks && (size_t)c.vocab_size * 4 > kSampleMaxSmem)
+      throw Error{MRTDF_ERR_INVALID, "unmasked sampling supports vocab_size <= 40960"};
+    const int rows = cfg ? 2 : 1;
+    const size_t row_bytes = (size_t)rows * c.d_model * E->esize;
+    if (row_bytes > kSampleScratchRowBytes)
+      throw Error{MRTDF_ERR_RANGE, "mrtdf_sample_noalloc: rows x d_model x dtype bytes = " + std::to_string(row_bytes) +
+                                       " exceeds its fixed scratch of " + std::to_string(kSampleScratchRowBytes) +
+                                       " bytes per feedback row"};
+    CUDA_OK(cudaSetDevice(E->device));
+    void* scratch = nullptr;
+    CUDA_OK(sample_scratch_address(E->device, &scratch));
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    uint8_t* base = reinterpret_cast<uint8_t*>(scratch);
+    uint64_t* seed = reinterpret_cast<uint64_t*>(base);
+    int* err = reinterpret_cast<int*>(base + 8);
+    // the error word must start at zero; the seed is this call's
+    CUDA_OK(cudaMemsetAsync(err, 0, 4, s));
+    CUDA_OK(cudaMemcpyAsync(seed, &o->seed, 8, cudaMemcpyHostToDevice, s));
+    int lo, hi;
+    level_range(c, o->use_vocab_masks != 0, level, lo, hi);
+    SampleParams sp{};
+    sp.logits = logits_dev; sp.logits_stride = c.vocab_size; sp.col_offset = 0; sp.lo = lo; sp.hi = hi;
+    sp.rows_per_seq = rows; sp.w = o->guidance_weight; sp.temperature = o->temperature; sp.top_k = o->top_k;
+    sp.seeds = seed; sp.step = (uint32_t)(frame * c.rvq_depth + level);
+    sp.uniforms = uniforms_dev; sp.uni_seq_stride = 0; sp.forced = nullptr;
+    sp.tokens = token_dev; sp.tok_stride = 0; sp.tok_index = 0;
+    sp.emb = E->emb; sp.d = c.d_model; sp.V = c.vocab_size;
+    sp.din = base + 256;
+    sp.fsum = base + 256 + kSampleScratchRowBytes;
+    sp.tin = base + 256 + 2 * kSampleScratchRowBytes;
+    sp.depth = c.rvq_depth; sp.is_first = 1; sp.is_last = 0; sp.err = err;
+    check_cuda(launch_sample(c.dtype, sp, 1, s, false), "sample launch");
+  });
+}
+
 int mrtdf_generate_tokens_dev(mrtdf_stream* st, const int32_t* enc_ids_dev, int seq_len, const mrtdf_gen_opts* o,
                               const uint64_t* seeds, int32_t* out_ids_dev) {
   return guarded([&] {

@@ -36,8 +36,8 @@ EXPORTS = [
     "mrtdf_last_error", "mrtdf_version", "mrtdf_config_preset", "mrtdf_write_random_safetensors", "mrtdf_create",
     "mrtdf_destroy", "mrtdf_load_safetensors", "mrtdf_load_random", "mrtdf_stream_create", "mrtdf_stream_destroy",
     "mrtdf_stream_rows", "mrtdf_encode", "mrtdf_temporal_step", "mrtdf_depth_step", "mrtdf_token_embedding",
-    "mrtdf_sample", "mrtdf_generate_tokens", "mrtdf_generate_tokens_dev", "mrtdf_teacher_forced_logits",
-    "mrtdf_stream_sync", "mrtdf_stream_cuda", "mrtdf_bench_gemv", "mrtdf_build_encoder_inputs", "mrtdf_context_roll",
+    "mrtdf_sample", "mrtdf_sample_noalloc", "mrtdf_generate_tokens", "mrtdf_generate_tokens_dev",
+    "mrtdf_teacher_forced_logits", "mrtdf_stream_sync", "mrtdf_stream_cuda", "mrtdf_bench_gemv", "mrtdf_build_encoder_inputs", "mrtdf_context_roll",
     "mrtdf_llm_to_rvq", "mrtdf_rvq_to_llm",
 ]
 
@@ -107,6 +107,9 @@ def lib() -> ctypes.CDLL:
                      "mrtdf_generate_tokens_dev", "mrtdf_teacher_forced_logits", "mrtdf_token_embedding",
                      "mrtdf_sample"]:
             getattr(L, name).restype = ctypes.c_int
+        L.mrtdf_sample_noalloc.restype = ctypes.c_int
+        L.mrtdf_sample_noalloc.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                           ctypes.POINTER(GenOpts), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         _lib = L
     return _lib
 
@@ -182,6 +185,14 @@ class Engine:
         _check(lib().mrtdf_sample(self.h, _fp(logits), int(rows == 2), frame, level, ctypes.byref(opts), _fp(u),
                                   _ip(tok)))
         return int(tok[0])
+
+    def sample_noalloc(self, logits_dev_ptr: int, cfg: bool, frame: int, level: int, opts: GenOpts,
+                       uniforms_dev_ptr: Optional[int], token_dev_ptr: int, stream: int = 0) -> None:
+        """mrtdf_sample on caller-owned device buffers, queued on `stream`
+        (a cudaStream_t as int) without waiting; allocates no GPU memory."""
+        _check(lib().mrtdf_sample_noalloc(self.h, ctypes.c_void_p(logits_dev_ptr), int(cfg), frame, level,
+                                          ctypes.byref(opts), ctypes.c_void_p(uniforms_dev_ptr or None),
+                                          ctypes.c_void_p(token_dev_ptr), ctypes.c_void_p(stream or None)))
 
     def close(self):
         if self.h:
