@@ -248,7 +248,50 @@ void* mrtdf_stream_cuda(mrtdf_stream* st);
 int mrtdf_bench_gemv(mrtdf_stream* st, const mrtdf_gen_opts* opts, int reps, float* ms_per_rep,
                      long long* launches_per_rep, double* bytes_per_rep);
 
+/*
+ * Measurement hook (no counterpart in the reference): the encoder pass
+ * (embed + PE, encoder layers, encoder_norm, cross-K/V projection of every
+ * temporal layer) for `rows` sequences of `seq_len` uniform-random ids
+ * (seed 2), captured as one CUDA graph and replayed `reps` times on a
+ * private stream. Reports ms per pass and the pass's algorithmic FLOPs
+ * (2 per multiply-add: linears, attention, cross-K/V). Allocates its own
+ * workspace (rows x seq_len activations + the cross-K/V cache) for the call.
+ */
+int mrtdf_bench_encoder(mrtdf_engine* eng, int rows, int seq_len, int reps, float* ms_per_rep,
+                        double* flops_per_rep);
+
+/*
+ * Measurement hook (no counterpart in the reference): `frames` x rvq_depth
+ * sequential depth steps (depth stack + decoder_norm + lm_head level slice
+ * + sampler with embedding feedback), each frame starting from an N(0, 1)
+ * temporal hidden state (seed 3) instead of a temporal step, captured as one
+ * graph and replayed `reps` times on the stream. Reports us per depth step,
+ * its algorithmic bytes (GEMV weights, inputs, outputs and the depth K/V
+ * reads) and kernel launches per step. Overwrites the stream's depth cache,
+ * token and feedback buffers.
+ */
+int mrtdf_bench_depth(mrtdf_stream* st, const mrtdf_gen_opts* opts, int frames, int reps, float* us_per_step,
+                      double* bytes_per_step, long long* launches_per_step);
+
 /* ---- streaming glue (System, system.cpp) ---------------------------------- */
+
+/*
+ * The System::generate_chunk loop (system.cpp:177-333) for `num_chunks`
+ * consecutive chunks without returning to the host: per chunk, encoder ids
+ * from the context (build_encoder_inputs_host, system.cpp:62-95), the chunk
+ * (generate_tokens), tokens -> RVQ codes (llm_to_rvq, rvq.cpp:112-134) and
+ * the context roll (system.cpp:320-333), all on the stream.
+ * context_dev: (num_sequences, ctx_frames, rvq_depth) int32 RVQ codes,
+ * negative = empty, rolled in place; style_dev: (num_sequences,
+ * style_depth) int32 LLM ids; rvq_out_dev: (num_chunks, num_sequences,
+ * num_frames, rvq_depth) int32 codes. seeds: host (num_chunks *
+ * num_sequences) or NULL (opts->seed + chunk, + i << 32 for sequence i).
+ * Returns once the work is queued; mrtdf_stream_sync waits and reports
+ * device errors (a token outside its level's range: MRTDF_ERR_INVALID).
+ */
+int mrtdf_generate_stream_dev(mrtdf_stream* st, int32_t* context_dev, int ctx_frames, int enc_depth,
+                              const int32_t* style_dev, int style_depth, int num_chunks,
+                              const mrtdf_gen_opts* opts, const uint64_t* seeds, int32_t* rvq_out_dev);
 
 /*
  * build_encoder_inputs_host (system.cpp:62-95): context (ctx_frames,

@@ -23,6 +23,8 @@
 
 namespace mrtdf {
 
+constexpr int kSelfAttnMaxT = 64;  // keys of a decode self-attention (2 chunks of 32)
+
 // ---------------------------------------------------------------------------
 // GEMV phase kernel
 //
@@ -273,6 +275,78 @@ __host__ __device__ inline MmaLayout mma_layout(int cols, int max_rows) {
   return L;
 }
 
+// Self-attention of one query row and head over keys [0, T), T <= 64, by
+// one warp: the arithmetic of attn_self_kernel (lane j scores key j of each
+// 32-key chunk, warp softmax, lane l accumulates output dims 2l, 2l + 1),
+// with every load through L2 only (ld.global.cg): q and the newest key /
+// value were written by other CTAs of the running kernel.
+__device__ __forceinline__ float2 bf16x2_bits_to_float2(uint32_t v) {
+  return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
+
+__device__ __forceinline__ void attn_warp_bf16(const __nv_bfloat16* q, const __nv_bfloat16* K,
+                                               const __nv_bfloat16* V, const float* bias, int T,
+                                               __nv_bfloat16* out, int lane, float* qs) {
+  const uint32_t qbits = __ldcg(reinterpret_cast<const unsigned int*>(q) + lane);
+  uint4 kr[8];
+#pragma unroll
+  for (int ch = 0; ch < 8; ++ch)
+    kr[ch] = lane < T ? __ldcg(reinterpret_cast<const uint4*>(K + (size_t)lane * 64) + ch) : make_uint4(0, 0, 0, 0);
+  const float bias0 = (bias && lane < T) ? bias[lane] : 0.f;
+  const float bias1 = (bias && 32 + lane < T) ? bias[32 + lane] : 0.f;
+  const float2 qv = bf16x2_bits_to_float2(qbits);
+  qs[2 * lane] = qv.x;
+  qs[2 * lane + 1] = qv.y;
+  __syncwarp();
+  float sc[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const int j = c * 32 + lane;
+    if (c == 1) {
+      if (T <= 32) break;  // no second chunk of keys
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch)
+        kr[ch] = j < T ? __ldcg(reinterpret_cast<const uint4*>(K + (size_t)j * 64) + ch) : make_uint4(0, 0, 0, 0);
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      float kf[8];
+      Vec16<__nv_bfloat16>::unpack(kr[ch], kf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e & 3] = fmaf(qs[ch * 8 + e], kf[e], acc[e & 3]);
+    }
+    float a = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    if (bias) a += (c == 0 ? bias0 : bias1);
+    sc[c] = j < T ? a : -INFINITY;
+  }
+  const float m = warp_max(fmaxf(sc[0], sc[1]));
+  const float p0 = lane < T ? expf(sc[0] - m) : 0.f;
+  const float p1 = 32 + lane < T ? expf(sc[1] - m) : 0.f;
+  const float l = warp_sum(p0 + p1);
+  float o0 = 0.f, o1 = 0.f;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    if (c * 32 >= T) break;  // keys past T add exact zeros
+    uint32_t vr[32];
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) {
+      const int jv = c * 32 + jj;
+      vr[jj] = jv < T ? __ldcg(reinterpret_cast<const unsigned int*>(V + (size_t)jv * 64) + lane) : 0u;
+    }
+    const float pc = c == 0 ? p0 : p1;
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) {
+      const float pw = __shfl_sync(0xffffffffu, pc, jj);
+      const float2 v = bf16x2_bits_to_float2(vr[jj]);
+      o0 = fmaf(pw, v.x, o0);
+      o1 = fmaf(pw, v.y, o1);
+    }
+  }
+  out[2 * lane] = __float2bfloat16_rn(o0 / l);
+  out[2 * lane + 1] = __float2bfloat16_rn(o1 / l);
+}
+
 template <int BMAX, int NT, bool NORM, int MODE>
 __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, const int max_rows) {
   typedef __nv_bfloat16 T;
@@ -441,29 +515,40 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
     rowaddr[nt] = wbase + (uint32_t)(min(nt * 8 + (lane & 7), R - 1) * L.rstride + (lane >> 3) * 16);
   // Rows g >= B of the A operand only feed rows of D that are never read,
   // so every lane loads unconditionally.
-  int ks = k0;
-  for (; ks + 4 <= k1; ks += 4) {
-    uint32_t bw[2][NT][4];
-    uint32_t xa[4][2];
+  // Software pipeline over groups of two k-steps (one ldmatrix.x4 per n-tile
+  // holds both k-steps' B fragments): the loads of group i + 1 are issued
+  // before the MMAs of group i, two register buffers in turn. The load after
+  // the last group re-reads that group (clamped index) instead of branching.
+  const int ngr = (k1 - k0) >> 1;
+  uint32_t bA[NT][4], xA[4], bB[NT][4], xB[4];
+  auto load_group = [&](uint32_t(&b)[NT][4], uint32_t(&x)[4], int kk) {
+    const uint32_t xo = xrow + (uint32_t)(kk * 32);
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(x[0]) : "r"(xo));
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(x[1]) : "r"(xo + 16));
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(x[2]) : "r"(xo + 32));
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(x[3]) : "r"(xo + 48));
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t xo = xrow + (uint32_t)((ks + q) * 32);
-      asm volatile("ld.shared.b32 %0, [%1];" : "=r"(xa[q][0]) : "r"(xo));
-      asm volatile("ld.shared.b32 %0, [%1];" : "=r"(xa[q][1]) : "r"(xo + 16));
+    for (int nt = 0; nt < NT; ++nt) ldsm_x4_g(b[nt], rowaddr[nt] + (uint32_t)(kk * 32));
+  };
+  auto mma_group = [&](const uint32_t(&b)[NT][4], const uint32_t(&x)[4]) {
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const uint32_t a[4] = {x[2 * q], 0u, x[2 * q + 1], 0u};
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) mma_m16n8k16(acc[nt], a, b[nt][2 * q], b[nt][2 * q + 1]);
     }
-#pragma unroll
-    for (int pr = 0; pr < 2; ++pr)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) ldsm_x4_g(bw[pr][nt], rowaddr[nt] + (uint32_t)((ks + 2 * pr) * 32));
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t a[4] = {xa[q][0], 0u, xa[q][1], 0u};
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-        mma_m16n8k16(acc[nt], a, bw[q >> 1][nt][2 * (q & 1)], bw[q >> 1][nt][2 * (q & 1) + 1]);
-    }
+  };
+  if (ngr > 0) load_group(bA, xA, k0);
+  int gi = 0;
+  for (; gi + 2 <= ngr; gi += 2) {
+    load_group(bB, xB, k0 + 2 * (gi + 1));
+    mma_group(bA, xA);
+    load_group(bA, xA, k0 + 2 * min(gi + 2, ngr - 1));
+    mma_group(bB, xB);
   }
-  for (; ks < k1; ++ks) {  // remainder: fewer than 4 k-steps
+  if (gi < ngr) mma_group(bA, xA);
+  if ((k1 - k0) & 1) {  // one k-step left
+    const int ks = k1 - 1;
     uint32_t xa0, xa1;
     const uint32_t xo = xrow + (uint32_t)(ks * 32);
     asm volatile("ld.shared.b32 %0, [%1];" : "=r"(xa0) : "r"(xo));
@@ -525,6 +610,51 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
       }
     }
   }
+  if constexpr (MODE == kGemvQKVAttn) {
+    // Arrival ticket per head: this CTA adds the number of that head's
+    // q/k/v rows it produced; the CTA that brings a head to 3 x 64 rows
+    // runs the head's attention for every batch row (warp b -> row b).
+    __shared__ int att_heads[4];
+    __shared__ int att_n;
+    __syncthreads();  // every epilogue store of the CTA is issued
+    if (tid == 0) {
+      int hs[4], cnt[4], nh = 0;
+      for (int u = u0; u < u1; ++u) {
+        const int h = (u % p.inner) >> 6;
+        int k = 0;
+        while (k < nh && hs[k] != h) ++k;
+        if (k == nh) {
+          if (nh == 4) break;  // unreachable: a CTA holds <= 32 consecutive rows
+          hs[nh] = h;
+          cnt[nh] = 0;
+          ++nh;
+        }
+        ++cnt[k];
+      }
+      __threadfence();  // release this CTA's q/k/v stores before the tickets
+      int na = 0;
+      for (int k = 0; k < nh; ++k)
+        if (atomicAdd(&p.counters[hs[k]], cnt[k]) + cnt[k] == 3 * 64) {
+          att_heads[na++] = hs[k];
+          p.counters[hs[k]] = 0;  // complete; the next use is a later launch
+        }
+      __threadfence();  // acquire: the head's rows from other CTAs are visible
+      att_n = na;
+    }
+    __syncthreads();
+    float* qs = reinterpret_cast<float*>(wsm) + warp * 64;  // the weights are consumed
+    for (int i = 0; i < att_n; ++i) {
+      const int h = att_heads[i];
+      if (warp < p.B) {
+        const size_t base = (((size_t)warp * p.H + h) * p.cap) * 64;
+        attn_warp_bf16(reinterpret_cast<const T*>(p.out) + (size_t)warp * p.out_stride + h * 64,
+                       reinterpret_cast<const T*>(p.kc) + base, reinterpret_cast<const T*>(p.vc) + base,
+                       p.bias ? p.bias + (size_t)h * p.bias_stride : nullptr, p.pos + 1,
+                       reinterpret_cast<T*>(p.attn_out) + (size_t)warp * p.inner + h * 64, lane, qs);
+      }
+      __syncwarp();
+    }
+  }
 }
 
 // Grid for the tensor-core GEMV: at least one CTA per SM when there are
@@ -580,6 +710,9 @@ static cudaError_t launch_gemv_mma_b(int mode, bool norm, const GemvParams& p, i
                   : launch_mma_t<BMAX, false, kGemvResid>(p, num_sms, s, pdl);
     case kGemvQKV:
       return launch_mma_t<BMAX, true, kGemvQKV>(p, num_sms, s, pdl);
+    case kGemvQKVAttn:
+      if (p.pos + 1 > kSelfAttnMaxT || !p.counters || !p.attn_out || p.inner % 64 != 0) return cudaErrorInvalidValue;
+      return launch_mma_t<BMAX, true, kGemvQKVAttn>(p, num_sms, s, pdl);
     case kGemvGeglu:
       return launch_mma_t<BMAX, true, kGemvGeglu>(p, num_sms, s, pdl);
     case kGemvLogits:
@@ -607,6 +740,7 @@ static cudaError_t set_mma_limits_bn() {
   set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvResid>);
   set((const void*)gemv_mma_kernel<BMAX, NT, false, kGemvResid>);
   set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvQKV>);
+  set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvQKVAttn>);
   set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvGeglu>);
   set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvLogits>);
   return e;
@@ -726,7 +860,6 @@ cudaError_t gemv_set_smem_limits() {
 // Scale 1.0, additive bias (relative-position bias of this query position,
 // in the compute dtype's values).
 // ---------------------------------------------------------------------------
-constexpr int kSelfAttnMaxT = 64;
 
 template <typename T>
 __device__ __forceinline__ uint32_t load_pair_bits(const T* p);

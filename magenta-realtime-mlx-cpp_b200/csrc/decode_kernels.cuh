@@ -15,6 +15,8 @@ enum GemvMode : int {
   kGemvQKV = 2,     // fused q/k/v: q -> out, k/v -> cache at `pos`
   kGemvGeglu = 3,   // unit = (wi_0 row, wi_1 row): out[b, u] = R(gelu(R(a)) * R(b))
   kGemvLogits = 4,  // float out[b, off + u] = R(acc)
+  kGemvQKVAttn = 5, // kGemvQKV + the self-attention of each head, run by the
+                    // CTA whose q/k/v rows complete that head (bf16 only)
 };
 
 struct GemvParams {
@@ -33,6 +35,13 @@ struct GemvParams {
   int out_offset;
   int inner, H, cap, pos;  // kGemvQKV
   int l2_keep;             // 1: keep these weights in L2 (evict_last), 0: stream them (evict_first)
+  // kGemvQKVAttn: relative-position bias of this query (H, bias_stride) or
+  // null, attention output (B, inner), per-head arrival counters (H, zero
+  // between launches)
+  const float* bias;
+  int bias_stride;
+  void* attn_out;
+  int* counters;
 };
 
 // Bytes of one TMA stage of the GEMV kernel and the number of stages.

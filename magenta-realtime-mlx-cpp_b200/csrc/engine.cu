@@ -26,6 +26,7 @@
 
 #include "../../include/mrtdf.h"
 #include "decode_kernels.cuh"
+#include "glue_kernels.cuh"
 #include "device_errors.h"
 #include "encoder_kernels.cuh"
 #include "host_util.h"
@@ -86,6 +87,11 @@ struct mrtdf_engine {
   bool loaded = false;
   bool pdl = true;
   bool tc_gemm = true;  // encoder GEMMs on tcgen05 (MRTDF_TC_GEMM=0 selects mma.sync)
+  // bf16 decode self-attention inside the q/k/v kernel (MRTDF_FUSE_ATTN=1).
+  // Off by default: its per-head arrival tickets and the attention's loads
+  // add ~4 dependent L2 round trips to the q/k/v kernel, which measured
+  // slower than the separate attention launch.
+  bool fuse_attn = false;
   Arena weights;
   void* emb = nullptr;
   void* enc_norm = nullptr;
@@ -127,9 +133,12 @@ struct mrtdf_stream {
   int32_t* forced;  // (nseq)
   float* part;
   int* counters;
+  int* head_cnt;  // (H) arrival counters of the fused q/k/v + attention kernel
   int* err;
   float* uniforms = nullptr;
   size_t uniforms_cap = 0;
+  uint64_t* seed_table = nullptr;  // per-chunk seeds of mrtdf_generate_stream_dev
+  size_t seed_table_cap = 0;
   // host state
   bool encoded = false;
   int S = 0;
@@ -363,6 +372,7 @@ void gemv(mrtdf_stream* st, int mode, bool norm, GemvParams p) {
   double bytes = (double)p.units * rpu * p.cols * es + (double)p.B * p.cols * es;
   bytes += (double)p.B * p.units * (mode == kGemvLogits ? 4.0 : es) * (mode == kGemvResid ? 2.0 : 1.0);
   if (norm) bytes += (double)p.cols * es;
+  if (mode == kGemvQKVAttn) bytes += 2.0 * p.B * p.H * (p.pos + 1) * 64.0 * es;  // fused attention's K/V reads
   st->gemv_launches += 1;
   st->gemv_bytes += bytes;
   check_cuda(launch_gemv(E->c.dtype, mode, norm, p, E->num_sms, st->s, E->pdl), "gemv launch");
@@ -383,12 +393,18 @@ void enqueue_decoder_layer(mrtdf_stream* st, const DecLayerDev& L, const void* x
   p.W = L.wqkv; p.x = x_in; p.norm_w = L.n_self; p.out = st->qb; p.kc = kc; p.vc = vc;
   p.units = 3 * in; p.cols = d; p.x_stride = d; p.out_stride = in; p.inner = in; p.H = c.num_heads;
   p.cap = cap; p.pos = pos; p.l2_keep = l2_keep;
-  gemv(st, kGemvQKV, true, p);
-  // 2. self attention with relative-position bias (scale 1.0)
-  AttnParams a{};
-  a.q = st->qb; a.K = kc; a.V = vc; a.bias = bias; a.bias_stride = bias_stride; a.out = st->ao; a.err = st->err;
-  a.B = st->B; a.H = c.num_heads; a.cap = cap; a.T = pos + 1; a.inner = in; a.nsplit = 1;
-  if (!st->gemv_only) check_cuda(launch_attn_self(c.dtype, a, st->s, E->pdl), "attn_self launch");
+  // 2. self attention with relative-position bias (scale 1.0): in bf16 fused
+  // into the q/k/v kernel (the CTA completing a head attends it)
+  if (E->fuse_attn && c.dtype == MRTDF_DTYPE_BF16) {
+    p.bias = bias; p.bias_stride = bias_stride; p.attn_out = st->ao; p.counters = st->head_cnt;
+    gemv(st, kGemvQKVAttn, true, p);
+  } else {
+    gemv(st, kGemvQKV, true, p);
+    AttnParams a{};
+    a.q = st->qb; a.K = kc; a.V = vc; a.bias = bias; a.bias_stride = bias_stride; a.out = st->ao; a.err = st->err;
+    a.B = st->B; a.H = c.num_heads; a.cap = cap; a.T = pos + 1; a.inner = in; a.nsplit = 1;
+    if (!st->gemv_only) check_cuda(launch_attn_self(c.dtype, a, st->s, E->pdl), "attn_self launch");
+  }
   // 3. o_proj + residual
   p = GemvParams{};
   p.W = L.wo; p.x = st->ao; p.out = xr; p.resid = x_in; p.units = d; p.cols = in; p.x_stride = in;
@@ -695,6 +711,7 @@ int mrtdf_create(const mrtdf_config* cfg, int device, mrtdf_engine** out) {
     E->esize = cfg->dtype == MRTDF_DTYPE_BF16 ? 2 : 4;
     E->pdl = env_flag("MRTDF_PDL", true);
     E->tc_gemm = env_flag("MRTDF_TC_GEMM", true);
+    E->fuse_attn = env_flag("MRTDF_FUSE_ATTN", false);
     CUDA_OK(gemv_set_smem_limits());
     CUDA_OK(gemm_set_smem_limits());
     CUDA_OK(gemm_tc_set_smem_limits());
@@ -786,6 +803,7 @@ int mrtdf_stream_create(mrtdf_engine* E, int num_sequences, int cfg, mrtdf_strea
         {(void**)&st->tokens, (size_t)num_sequences * c.max_frames * c.rvq_depth * 4},
         {(void**)&st->seeds, (size_t)num_sequences * 8}, {(void**)&st->forced, (size_t)num_sequences * 4},
         {(void**)&st->part, B * H * kCrossSplit * 66 * 4}, {(void**)&st->counters, B * H * 4},
+        {(void**)&st->head_cnt, H * 4},
         {(void**)&st->err, 64}};
     size_t total = 0;
     for (auto& p : plan) total += (p.second + 255) & ~(size_t)255;
@@ -803,6 +821,7 @@ int mrtdf_stream_destroy(mrtdf_stream* st) {
     cudaSetDevice(st->eng->device);
     cudaStreamSynchronize(st->s);
     if (st->uniforms) cudaFree(st->uniforms);
+    if (st->seed_table) cudaFree(st->seed_table);
     delete st;
   });
 }
@@ -1044,6 +1063,59 @@ int mrtdf_generate_tokens_dev(mrtdf_stream* st, const int32_t* enc_ids_dev, int 
   });
 }
 
+int mrtdf_generate_stream_dev(mrtdf_stream* st, int32_t* context_dev, int ctx_frames, int enc_depth,
+                              const int32_t* style_dev, int style_depth, int num_chunks, const mrtdf_gen_opts* o,
+                              const uint64_t* seeds, int32_t* rvq_out_dev) {
+  return guarded([&] {
+    if (!st || !context_dev || !o || !rvq_out_dev || (style_depth > 0 && !style_dev))
+      throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    mrtdf_engine* E = st->eng;
+    const mrtdf_config& c = E->c;
+    if (ctx_frames <= 0 || enc_depth <= 0 || enc_depth > c.rvq_depth || style_depth < 0 || num_chunks <= 0)
+      throw Error{MRTDF_ERR_INVALID, "bad sizes"};
+    const int S = ctx_frames * enc_depth + style_depth;
+    validate_opts(st, o, S);
+    if (o->uniforms) throw Error{MRTDF_ERR_INVALID, "streaming draws with Philox (no injected uniforms)"};
+    if (o->num_frames > ctx_frames) throw Error{MRTDF_ERR_INVALID, "a chunk is longer than the context"};
+    GlueParams gp{};
+    gp.context = context_dev; gp.style = style_dev; gp.ids = st->ids; gp.tokens = st->tokens; gp.err = st->err;
+    gp.nseq = st->nseq; gp.rows_per_seq = st->rps; gp.ctx_frames = ctx_frames; gp.rvq_depth = c.rvq_depth;
+    gp.enc_depth = enc_depth; gp.style_depth = style_depth; gp.frames = o->num_frames;
+    gp.tok_stride = c.max_frames * c.rvq_depth; gp.codebook_size = c.codebook_size; gp.codec_offset = c.codec_offset;
+    if (glue_roll_smem(gp) > kGlueMaxSmem) throw Error{MRTDF_ERR_RANGE, "context too long for the device roll"};
+    CUDA_OK(cudaSetDevice(E->device));
+    // seeds of every chunk: seeds[chunk * nseq + i], or opts->seed + chunk for
+    // sequence 0 (the CLI's seed + chunk_index) and + i << 32 for sequence i
+    const size_t n = (size_t)num_chunks * st->nseq;
+    std::vector<uint64_t> h(n);
+    for (int k = 0; k < num_chunks; ++k)
+      for (int i = 0; i < st->nseq; ++i)
+        h[(size_t)k * st->nseq + i] = seeds ? seeds[(size_t)k * st->nseq + i] : o->seed + k + ((uint64_t)i << 32);
+    if (n > st->seed_table_cap) {
+      CUDA_OK(cudaStreamSynchronize(st->s));
+      if (st->seed_table) cudaFree(st->seed_table);
+      st->seed_table = nullptr;
+      CUDA_OK(cudaMalloc(&st->seed_table, n * 8));
+      st->seed_table_cap = n;
+    }
+    CUDA_OK(cudaMemcpyAsync(st->seed_table, h.data(), n * 8, cudaMemcpyHostToDevice, st->s));
+    CUDA_OK(cudaStreamSynchronize(st->s));  // h is a local
+    st->S = S;
+    for (int k = 0; k < num_chunks; ++k) {
+      CUDA_OK(cudaMemcpyAsync(st->seeds, st->seed_table + (size_t)k * st->nseq, (size_t)st->nseq * 8,
+                              cudaMemcpyDeviceToDevice, st->s));
+      check_cuda(launch_stream_encoder_ids(gp, st->s), "encoder ids");
+      run_chunk(st, S, *o);
+      gp.rvq_out = rvq_out_dev + (size_t)k * st->nseq * o->num_frames * c.rvq_depth;
+      check_cuda(launch_stream_roll(gp, st->s), "context roll");
+    }
+    st->encoded = true;
+    st->t_len = o->num_frames;
+    st->d_len = c.rvq_depth;
+    st->have_temporal = true;
+  });
+}
+
 int mrtdf_generate_tokens(mrtdf_stream* st, const int32_t* enc_ids, int seq_len, const mrtdf_gen_opts* o,
                           const uint64_t* seeds, int32_t* out_ids) {
   return guarded([&] {
@@ -1154,6 +1226,158 @@ int mrtdf_bench_gemv(mrtdf_stream* st, const mrtdf_gen_opts* o, int reps, float*
     *ms_per_rep = ms / reps;
     *launches_per_rep = st->gemv_launches;
     *bytes_per_rep = st->gemv_bytes;
+    check_device_err(st);
+  });
+}
+
+
+int mrtdf_bench_encoder(mrtdf_engine* E, int rows, int seq_len, int reps, float* ms_per_rep, double* flops_per_rep) {
+  return guarded([&] {
+    if (!E || rows <= 0 || reps <= 0 || !ms_per_rep || !flops_per_rep) throw Error{MRTDF_ERR_INVALID, "bad argument"};
+    if (!E->loaded) throw Error{MRTDF_ERR_STATE, "weights not loaded"};
+    const mrtdf_config& c = E->c;
+    if (seq_len <= 0 || seq_len > c.max_encoder_length) throw Error{MRTDF_ERR_RANGE, "seq_len out of range"};
+    CUDA_OK(cudaSetDevice(E->device));
+    // encoder-only workspace for `rows` sequences (no decode state)
+    mrtdf_stream st;
+    st.eng = E;
+    st.nseq = rows;
+    st.rps = 1;
+    st.B = rows;
+    CUDA_OK(cudaStreamCreateWithFlags(&st.s, cudaStreamNonBlocking));
+    const size_t B = rows, d = c.d_model, in = E->inner(), ff = c.d_ff, H = c.num_heads, es = E->esize;
+    const size_t M = B * seq_len;
+    const size_t cross = (size_t)c.num_temporal_layers * B * H * c.max_encoder_length * 64 * es;
+    std::vector<std::pair<void**, size_t>> plan = {
+        {&st.ex, M * d * es}, {&st.en, M * d * es}, {&st.eqkv, M * 3 * in * es}, {&st.eo, M * in * es},
+        {&st.eh, M * ff * es}, {(void**)&st.ids, M * 4}, {&st.ck, cross}, {&st.cv, cross}, {(void**)&st.err, 64}};
+    size_t total = 0;
+    for (auto& q : plan) total += (q.second + 255) & ~(size_t)255;
+    st.mem.reserve(total);
+    for (auto& q : plan) *q.first = st.mem.take(q.second);
+    // uniform-random ids in [0, vocab), seed 2
+    std::vector<int32_t> ids(M);
+    uint64_t x = 2;
+    for (auto& v : ids) {
+      x += 0x9E3779B97F4A7C15ull;  // splitmix64
+      uint64_t z = x;
+      z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+      z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+      z ^= z >> 31;
+      v = (int32_t)(z % (uint64_t)c.vocab_size);
+    }
+    CUDA_OK(cudaMemcpyAsync(st.ids, ids.data(), M * 4, cudaMemcpyHostToDevice, st.s));
+    CUDA_OK(cudaMemsetAsync(st.err, 0, 64, st.s));
+    st.S = seq_len;
+    cudaGraph_t g = nullptr;
+    CUDA_OK(cudaStreamBeginCapture(st.s, cudaStreamCaptureModeThreadLocal));
+    try {
+      enqueue_encode(&st, seq_len);
+    } catch (...) {
+      cudaStreamEndCapture(st.s, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    CUDA_OK(cudaStreamEndCapture(st.s, &g));
+    cudaGraphExec_t ex = nullptr;
+    const cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    check_cuda(e, "cudaGraphInstantiate");
+    cudaEvent_t a, b;
+    CUDA_OK(cudaEventCreate(&a));
+    CUDA_OK(cudaEventCreate(&b));
+    CUDA_OK(cudaGraphLaunch(ex, st.s));  // warm-up
+    CUDA_OK(cudaEventRecord(a, st.s));
+    for (int r = 0; r < reps; ++r) CUDA_OK(cudaGraphLaunch(ex, st.s));
+    CUDA_OK(cudaEventRecord(b, st.s));
+    CUDA_OK(cudaEventSynchronize(b));
+    float ms = 0.f;
+    CUDA_OK(cudaEventElapsedTime(&ms, a, b));
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    cudaGraphExecDestroy(ex);
+    *ms_per_rep = ms / reps;
+    // 2 flops per multiply-add: encoder linears, attention (QK^T and PV),
+    // and the cross-K/V projection of every temporal layer
+    const double Md = (double)M, S = seq_len;
+    const double lin = 2.0 * Md * ((double)d * 3 * in + (double)in * d + (double)d * 2 * ff + (double)ff * d);
+    const double att = 4.0 * (double)B * H * S * S * 64.0;
+    *flops_per_rep = c.num_encoder_layers * (lin + att) + 2.0 * Md * d * (2.0 * c.num_temporal_layers * in);
+    check_device_err(&st);
+  });
+}
+
+int mrtdf_bench_depth(mrtdf_stream* st, const mrtdf_gen_opts* o, int frames, int reps, float* us_per_step,
+                      double* bytes_per_step, long long* launches_per_step) {
+  return guarded([&] {
+    if (!st || !o || frames <= 0 || reps <= 0 || !us_per_step || !bytes_per_step || !launches_per_step)
+      throw Error{MRTDF_ERR_INVALID, "bad argument"};
+    mrtdf_engine* E = st->eng;
+    const mrtdf_config& c = E->c;
+    if (frames > c.max_frames) throw Error{MRTDF_ERR_RANGE, "frames must be <= max_frames"};
+    if (o->rvq_depth != c.rvq_depth) throw Error{MRTDF_ERR_INVALID, "rvq_depth must equal the model's rvq_depth"};
+    if (o->uniforms) throw Error{MRTDF_ERR_INVALID, "the depth microbenchmark draws with Philox"};
+    CUDA_OK(cudaSetDevice(E->device));
+    // one N(0, 1) temporal hidden state per frame and row (seed 3), in the compute dtype
+    const size_t per_frame = (size_t)st->B * c.d_model;
+    std::vector<float> xs(per_frame * frames);
+    fill_random_tensor(3, 0, 1.0f, false, false, xs.data(), (int64_t)xs.size());
+    const std::vector<uint8_t> xb = to_dtype(xs.data(), xs.size(), c.dtype);
+    uint8_t* xd = nullptr;
+    CUDA_OK(cudaMalloc(&xd, xb.size()));
+    struct Free {
+      uint8_t* p;
+      ~Free() { cudaFree(p); }
+    } free_xd{xd};
+    CUDA_OK(cudaMemcpyAsync(xd, xb.data(), xb.size(), cudaMemcpyHostToDevice, st->s));
+    upload_seeds(st, o, nullptr);
+    const bool masked = o->use_vocab_masks != 0;
+    st->gemv_launches = 0;
+    st->gemv_bytes = 0.0;
+    cudaGraph_t g = nullptr;
+    CUDA_OK(cudaStreamBeginCapture(st->s, cudaStreamCaptureModeThreadLocal));
+    try {
+      for (int f = 0; f < frames; ++f)
+        for (int l = 0; l < c.rvq_depth; ++l) {
+          int lo, hi;
+          level_range(c, masked, l, lo, hi);
+          enqueue_depth(st, l, l == 0 ? (const void*)(xd + act_bytes(E, per_frame * f)) : st->din, lo, hi);
+          enqueue_sample(st, f, l, *o, masked, lo, hi, false);
+        }
+    } catch (...) {
+      cudaStreamEndCapture(st->s, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    CUDA_OK(cudaStreamEndCapture(st->s, &g));
+    cudaGraphExec_t ex = nullptr;
+    const cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    check_cuda(e, "cudaGraphInstantiate");
+    cudaEvent_t a, b;
+    CUDA_OK(cudaEventCreate(&a));
+    CUDA_OK(cudaEventCreate(&b));
+    CUDA_OK(cudaGraphLaunch(ex, st->s));  // warm-up
+    CUDA_OK(cudaEventRecord(a, st->s));
+    for (int r = 0; r < reps; ++r) CUDA_OK(cudaGraphLaunch(ex, st->s));
+    CUDA_OK(cudaEventRecord(b, st->s));
+    CUDA_OK(cudaEventSynchronize(b));
+    float ms = 0.f;
+    CUDA_OK(cudaEventElapsedTime(&ms, a, b));
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    cudaGraphExecDestroy(ex);
+    const double steps = (double)frames * c.rvq_depth;
+    *us_per_step = (float)(ms * 1e3 / (reps * steps));
+    // GEMV phases (weights, inputs, outputs) + the self-attention K/V reads
+    double kv = 0.0;
+    for (int l = 0; l < c.rvq_depth; ++l)
+      kv += 2.0 * c.num_depth_layers * st->B * c.num_heads * (l + 1) * 64.0 * E->esize;
+    *bytes_per_step = (st->gemv_bytes + kv * frames) / steps;
+    // per level: layers x (QKV, attention, o_proj, FFN-up, FFN-down) + lm_head + sampler;
+    // the attention runs inside the QKV launch when fused
+    const bool fused = E->fuse_attn && c.dtype == MRTDF_DTYPE_BF16;
+    *launches_per_step = (long long)c.num_depth_layers * (fused ? 4 : 5) + 2;
     check_device_err(st);
   });
 }

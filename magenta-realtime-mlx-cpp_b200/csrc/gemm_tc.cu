@@ -10,8 +10,10 @@
 //                  frees the stage (`empty` mbarrier) once the MMAs that read
 //                  it retire, and signals `done` after the last k-tile;
 //   all 4 warps    epilogue: tcgen05.ld (32 lanes x 16 columns per load)
-//                  from the warp's TMEM lane quarter, then the fused epilogue
-//                  (store / residual add / GEGLU / cross-K/V scatter).
+//                  from the warp's TMEM lane quarter into a bf16 tile in the
+//                  freed pipeline shared memory (GEGLU applied here), then
+//                  16-byte stores along output rows with the fused epilogue
+//                  (store / residual add / cross-K/V scatter).
 // No cluster, no multicast. Every mbarrier wait is bounded and reports a
 // timeout in the stream's error word; TMEM is always released.
 //
@@ -29,7 +31,6 @@
 
 #include "common.cuh"
 #include "encoder_kernels.cuh"
-#include "gemm_epilogue.cuh"
 
 namespace mrtdf {
 
@@ -41,6 +42,9 @@ constexpr int B_BYTES = BN * BK * 2;  // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /* 1024-byte alignment slack */ + 256 /* barriers */;
 constexpr uint32_t TMEM_COLS = 128;
+// Epilogue tile in shared memory: 128 rows x (128 + 8) bf16 (16-byte row pad).
+constexpr int kTileLd = BN + 8;
+static_assert(BM * kTileLd * 2 <= STAGES * STAGE_BYTES, "epilogue tile must fit the pipeline buffers");
 
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu)  // start address
@@ -170,16 +174,81 @@ __global__ void __launch_bounds__(128, 1)
   const bool ok = __syncthreads_and(mbar_wait_bounded(done, 0, err) ? 1 : 0) && !abort_flag;
   tc_fence_after();
   if (ok) {
-    const int row = bm + warp * 32 + lane;
+    // Phase 1: TMEM -> registers -> a bf16 tile in the (now idle) pipeline
+    // shared memory; thread = tile row. GEGLU pairs (a, g) become one column.
+    typedef __nv_bfloat16 T;
+    T* stile = reinterpret_cast<T*>(smem);
+    const int r_local = warp * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
 #pragma unroll 1
     for (int c = 0; c < BN; c += 16) {
       uint32_t r[16];
       tmem_ld16(lane_base + (uint32_t)c, r);
       tmem_wait_ld();
+      if (EPI == kEpiGeglu) {
+        uint32_t o[4];
 #pragma unroll
-      for (int i = 0; i < 16; i += 2)
-        epi_pair<__nv_bfloat16, EPI>(p, row, bn + c + i, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+        for (int i = 0; i < 4; ++i) {
+          const float a0 = rnd<T>(__uint_as_float(r[4 * i])), g0 = rnd<T>(__uint_as_float(r[4 * i + 1]));
+          const float a1 = rnd<T>(__uint_as_float(r[4 * i + 2])), g1 = rnd<T>(__uint_as_float(r[4 * i + 3]));
+          const __nv_bfloat162 pr =
+              __floats2bfloat162_rn(__fmul_rn(gelu_approx<T>(a0), g0), __fmul_rn(gelu_approx<T>(a1), g1));
+          o[i] = *reinterpret_cast<const uint32_t*>(&pr);
+        }
+        *reinterpret_cast<uint4*>(stile + (size_t)r_local * kTileLd + (c >> 1)) = make_uint4(o[0], o[1], o[2], o[3]);
+      } else {
+        uint32_t o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const __nv_bfloat162 pr = __floats2bfloat162_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+          o[i] = *reinterpret_cast<const uint32_t*>(&pr);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(stile + (size_t)r_local * kTileLd + c);
+        dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+      }
+    }
+  }
+  __syncthreads();
+  if (ok) {
+    // Phase 2: 16-byte stores along output rows (8 columns per chunk).
+    typedef __nv_bfloat16 T;
+    const T* stile = reinterpret_cast<const T*>(smem);
+    constexpr int OC = (EPI == kEpiGeglu) ? BN / 2 : BN;  // output columns of the tile
+    constexpr int CPR = OC / 8;                          // 16-byte chunks per row
+    const int oc0 = (EPI == kEpiGeglu) ? bn / 2 : bn;
+    const int ncols = (EPI == kEpiGeglu) ? p.N / 2 : p.N;
+#pragma unroll 4
+    for (int idx = tid; idx < BM * CPR; idx += 128) {
+      const int r = idx / CPR, ch = idx - r * CPR;
+      const int m = bm + r, n = oc0 + ch * 8;
+      if (m >= p.M || n >= ncols) continue;
+      uint4 v = *reinterpret_cast<const uint4*>(stile + (size_t)r * kTileLd + ch * 8);
+      if (EPI == kEpiCrossKV) {
+        const int two_inner = 2 * p.inner;
+        const int layer = n / two_inner, within = n - layer * two_inner;
+        const int kv = within / p.inner, rr = within - kv * p.inner;
+        const int h = rr >> 6, cc = rr & 63;
+        const int b = m / p.S, s = m - b * p.S;
+        T* cache = reinterpret_cast<T*>(kv == 0 ? p.ck : p.cv);
+        *reinterpret_cast<uint4*>(cache + ((((size_t)layer * p.B + b) * p.H + h) * p.Smax + s) * 64 + cc) = v;
+      } else {
+        T* o = reinterpret_cast<T*>(p.out) + (size_t)m * p.ldo + n;
+        if (EPI == kEpiResid) {
+          const uint4 rv = *reinterpret_cast<const uint4*>(o);
+          const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&rv);
+          const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 fa = __bfloat1622float2(a2[i]), fb = __bfloat1622float2(b2[i]);
+            const __nv_bfloat162 pr = __floats2bfloat162_rn(__fadd_rn(fa.x, fb.x), __fadd_rn(fa.y, fb.y));
+            w[i] = *reinterpret_cast<const uint32_t*>(&pr);
+          }
+          v = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        *reinterpret_cast<uint4*>(o) = v;
+      }
     }
   }
   tc_fence_before();
@@ -251,7 +320,12 @@ cudaError_t gemm_tc_set_smem_limits() {
 
 cudaError_t launch_gemm_tc(int epi, const GemmParams& p, int* err, cudaStream_t s, bool pdl) {
   if (p.M <= 0 || p.N <= 0) return cudaSuccess;
-  if (p.N % 2 != 0 || p.K % 8 != 0 || p.lda % 8 != 0) return cudaErrorInvalidValue;
+  // 16-byte epilogue chunks: 8 output columns (16 GEMM columns for GEGLU)
+  if (p.N % (epi == kEpiGeglu ? 16 : 8) != 0 || p.K % 8 != 0 || p.lda % 8 != 0) return cudaErrorInvalidValue;
+  if (epi != kEpiCrossKV && (p.ldo % 8 != 0 || (reinterpret_cast<uintptr_t>(p.out) & 15))) return cudaErrorInvalidValue;
+  if (epi == kEpiCrossKV && (p.inner % 64 != 0 || (reinterpret_cast<uintptr_t>(p.ck) & 15) ||
+                             (reinterpret_cast<uintptr_t>(p.cv) & 15)))
+    return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(p.A) & 15) || (reinterpret_cast<uintptr_t>(p.W) & 15)) return cudaErrorInvalidValue;
   CUtensorMap a, b;
   if (!tc::make_map(&a, p.A, p.M, p.K, p.lda) || !tc::make_map(&b, p.W, p.N, p.K, p.K)) return cudaErrorInvalidValue;

@@ -37,8 +37,9 @@ EXPORTS = [
     "mrtdf_destroy", "mrtdf_load_safetensors", "mrtdf_load_random", "mrtdf_stream_create", "mrtdf_stream_destroy",
     "mrtdf_stream_rows", "mrtdf_encode", "mrtdf_temporal_step", "mrtdf_depth_step", "mrtdf_token_embedding",
     "mrtdf_sample", "mrtdf_sample_noalloc", "mrtdf_generate_tokens", "mrtdf_generate_tokens_dev",
-    "mrtdf_teacher_forced_logits", "mrtdf_stream_sync", "mrtdf_stream_cuda", "mrtdf_bench_gemv", "mrtdf_build_encoder_inputs", "mrtdf_context_roll",
-    "mrtdf_llm_to_rvq", "mrtdf_rvq_to_llm",
+    "mrtdf_teacher_forced_logits", "mrtdf_stream_sync", "mrtdf_stream_cuda", "mrtdf_bench_gemv",
+    "mrtdf_bench_encoder", "mrtdf_bench_depth", "mrtdf_generate_stream_dev", "mrtdf_build_encoder_inputs",
+    "mrtdf_context_roll", "mrtdf_llm_to_rvq", "mrtdf_rvq_to_llm",
 ]
 
 
@@ -194,6 +195,14 @@ class Engine:
                                           ctypes.byref(opts), ctypes.c_void_p(uniforms_dev_ptr or None),
                                           ctypes.c_void_p(token_dev_ptr), ctypes.c_void_p(stream or None)))
 
+    def bench_encoder(self, rows: int, seq_len: int, reps: int):
+        """(ms per encoder pass, algorithmic FLOPs per pass) for `rows`
+        sequences of `seq_len` random ids, replayed as one CUDA graph."""
+        ms = ctypes.c_float()
+        fl = ctypes.c_double()
+        _check(lib().mrtdf_bench_encoder(self.h, rows, seq_len, reps, ctypes.byref(ms), ctypes.byref(fl)))
+        return ms.value, fl.value
+
     def close(self):
         if self.h:
             lib().mrtdf_destroy(self.h)
@@ -255,6 +264,18 @@ class Stream:
         _check(lib().mrtdf_generate_tokens_dev(self.h, ctypes.c_void_p(ids_dev_ptr), seq_len, ctypes.byref(opts), sd,
                                                ctypes.c_void_p(out_dev_ptr)))
 
+    def generate_stream_dev(self, context_dev_ptr: int, ctx_frames: int, enc_depth: int, style_dev_ptr: int,
+                            style_depth: int, num_chunks: int, opts: GenOpts, out_dev_ptr: int,
+                            seeds: Optional[Sequence[int]] = None) -> None:
+        """num_chunks streaming chunks on the device (context rolled in place);
+        returns once queued."""
+        sd = None
+        if seeds is not None:
+            sd = (ctypes.c_uint64 * (num_chunks * self.num_sequences))(*seeds)
+        _check(lib().mrtdf_generate_stream_dev(self.h, ctypes.c_void_p(context_dev_ptr), ctx_frames, enc_depth,
+                                               ctypes.c_void_p(style_dev_ptr), style_depth, num_chunks,
+                                               ctypes.byref(opts), sd, ctypes.c_void_p(out_dev_ptr)))
+
     def teacher_forced_logits(self, ids: np.ndarray, tokens: np.ndarray, num_frames: int) -> np.ndarray:
         ids = np.ascontiguousarray(ids, dtype=np.int32)
         toks = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
@@ -264,6 +285,16 @@ class Stream:
 
     def sync(self) -> None:
         _check(lib().mrtdf_stream_sync(self.h))
+
+    def bench_depth(self, opts: GenOpts, frames: int, reps: int):
+        """(us per depth step, algorithmic bytes per step, launches per step)
+        of frames x rvq_depth depth steps from N(0, 1) hidden states."""
+        us = ctypes.c_float()
+        b = ctypes.c_double()
+        n = ctypes.c_longlong()
+        _check(lib().mrtdf_bench_depth(self.h, ctypes.byref(opts), frames, reps, ctypes.byref(us), ctypes.byref(b),
+                                       ctypes.byref(n)))
+        return us.value, b.value, n.value
 
     def bench_gemv(self, opts: GenOpts, reps: int):
         """(ms per chunk replay, GEMV launches, algorithmic bytes) of the

@@ -291,3 +291,92 @@ def test_tcgen05_encoder_gemm(mrtdf, oracle, tiny_weights, hybrid_weights, name,
     if name == "tiny":
         want = oracle.Oracle(path, cfg.as_ints()).encode(ids)
         assert np.abs(a - want).max() <= 4 * BF16_TOL
+
+
+# ---------------------------------------------------------------------------
+# bf16 self-attention fused into the q/k/v kernel vs the separate kernel
+# ---------------------------------------------------------------------------
+def _engine_env(mrtdf, var, value, make):
+    old = os.environ.get(var)
+    os.environ[var] = value
+    try:
+        return make()
+    finally:
+        if old is None:
+            del os.environ[var]
+        else:
+            os.environ[var] = old
+
+
+@pytest.mark.parametrize("name", ["tiny", "hybrid"])
+def test_fused_self_attention_matches_separate_kernel(mrtdf, tiny_weights, name):
+    """Same arithmetic in both places: bit-identical logits and tokens."""
+    cfg = mrtdf.preset(name, 1)
+    frames = cfg.max_frames if name == "tiny" else 3
+    seq = cfg.max_encoder_length if name == "tiny" else 256
+
+    def make():
+        e = mrtdf.Engine(cfg)
+        return e.load_safetensors(tiny_weights) if name == "tiny" else e.load_random(0)
+
+    outs = []
+    for fuse in ("1", "0"):
+        eng = _engine_env(mrtdf, "MRTDF_FUSE_ATTN", fuse, make)
+        st = mrtdf.Stream(eng, 1, True)
+        ids = random_ids(cfg, 2, seq, seed=21)
+        lg = st.teacher_forced_logits(ids, _forced_tokens(cfg, frames, 5), frames)
+        gen = st.generate_tokens(ids, mrtdf.gen_opts(cfg, frames, seed=4))
+        outs.append((lg, gen))
+        st.close()
+        eng.close()
+    np.testing.assert_array_equal(outs[0][0], outs[1][0])
+    np.testing.assert_array_equal(outs[0][1], outs[1][1])
+
+
+def test_measurement_hooks(mrtdf, tiny_weights):
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", 1)
+    ms, flops = eng.bench_encoder(3, cfg.max_encoder_length, 2)
+    S, M, d, inn, ff = cfg.max_encoder_length, 3 * cfg.max_encoder_length, cfg.d_model, cfg.inner, cfg.d_ff
+    lin = 2 * M * (d * 3 * inn + inn * d + d * 2 * ff + ff * d)
+    att = 4 * 3 * cfg.num_heads * S * S * 64
+    assert ms > 0 and flops == pytest.approx(cfg.num_encoder_layers * (lin + att)
+                                             + 2 * M * d * 2 * cfg.num_temporal_layers * inn)
+    st = mrtdf.Stream(eng, 1, True)
+    o = mrtdf.gen_opts(cfg, cfg.max_frames, seed=3)
+    us, b, n = st.bench_depth(o, cfg.max_frames, 2)
+    assert us > 0 and b > 0 and n == cfg.num_depth_layers * 5 + 2
+    st.sync()
+
+
+def test_device_streaming_equals_host_loop(mrtdf, tiny_weights):
+    """mrtdf_generate_stream_dev == the host System loop (encoder ids ->
+    generate_tokens -> llm_to_rvq -> context roll), chunk by chunk."""
+    torch = pytest.importorskip("torch")
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", 1)
+    nseq, K, F, enc_depth, style_depth = 2, 3, cfg.max_frames, 4, 6
+    ctx_frames = (cfg.max_encoder_length - style_depth) // enc_depth
+    rng = np.random.default_rng(31)
+    ctx = -np.ones((nseq, ctx_frames, cfg.rvq_depth), np.int32)
+    ctx[0, -5:] = rng.integers(0, cfg.codebook_size, (5, cfg.rvq_depth))  # a partly filled context
+    style = rng.integers(cfg.codec_offset, cfg.codec_offset + cfg.rvq_depth * cfg.codebook_size,
+                         (nseq, style_depth)).astype(np.int32)
+    seeds = [100 + 10 * k + i for k in range(K) for i in range(nseq)]
+    o = mrtdf.gen_opts(cfg, F)
+    ctx_dev = torch.from_numpy(ctx.copy()).cuda()
+    style_dev = torch.from_numpy(style).cuda()
+    out_dev = torch.full((K, nseq, F, cfg.rvq_depth), -1, dtype=torch.int32, device="cuda")
+    st_dev = mrtdf.Stream(eng, nseq, True)
+    st_dev.generate_stream_dev(ctx_dev.data_ptr(), ctx_frames, enc_depth, style_dev.data_ptr(), style_depth, K, o,
+                               out_dev.data_ptr(), seeds=seeds)
+    st_dev.sync()
+    st = mrtdf.Stream(eng, nseq, True)
+    want = []
+    for k in range(K):
+        ids = np.concatenate([mrtdf.build_encoder_inputs(ctx[i], style[i], enc_depth, cfg.codebook_size,
+                                                         cfg.codec_offset) for i in range(nseq)], axis=0)
+        toks = st.generate_tokens(ids, o, seeds=seeds[k * nseq:(k + 1) * nseq])
+        rvq = np.stack([mrtdf.llm_to_rvq(toks[i], cfg.codebook_size, cfg.codec_offset) for i in range(nseq)])
+        ctx = np.stack([mrtdf.context_roll(ctx[i], rvq[i]) for i in range(nseq)])
+        want.append(rvq)
+    np.testing.assert_array_equal(out_dev.cpu().numpy(), np.stack(want))
+    np.testing.assert_array_equal(ctx_dev.cpu().numpy(), ctx)
