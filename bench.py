@@ -377,6 +377,13 @@ def e2e_leg(mrtdf, torch, cfg, st, ext, ids, K: int, rank: int, dist, device) ->
             "ms_per_chunk": ms_e2e, "rtf": CHUNK_SECONDS * 1e3 / ms_e2e}
 
 
+# DRAM bytes / algorithmic bytes of the decode GEMV launches, from one ncu
+# --set full capture of three consecutive temporal-step launches (FFN-up,
+# FFN-down, q/k/v): dram__bytes_read.sum + dram__bytes_write.sum = 23.705 MB
+# against 23.648 MB of weights, inputs and outputs.
+GEMV_TRAFFIC_OVER_ALGORITHMIC = 1.0025
+
+
 def roofline_leg(mrtdf, cfg, st, peaks: dict) -> dict:
     """Dominant kernel = the decode GEMV phases (gemv_mma_kernel): algorithmic bytes per
     launch / average launch time, replaying exactly the chunk's GEMV launches
@@ -387,7 +394,9 @@ def roofline_leg(mrtdf, cfg, st, peaks: dict) -> dict:
     achieved = g_bytes / g_launches / per_launch_s / 1e9
     peak = peaks.get("hbm_gbs", 6650.0)
     return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-            "traffic": None, "kernel": "gemv_mma_kernel (decode GEMV phases)",
+            "traffic": g_bytes / g_launches * GEMV_TRAFFIC_OVER_ALGORITHMIC, "traffic_unit": "bytes per launch",
+            "traffic_source": "ncu capture of 3 launches, DRAM/algorithmic ratio applied to the average launch",
+            "kernel": "gemv_mma_kernel (decode GEMV phases)",
             "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "launches_per_chunk": g_launches,
             "bytes_per_launch": g_bytes / g_launches, "us_per_launch": per_launch_s * 1e6, "gemv_ms_per_chunk": g_ms}
 

@@ -186,12 +186,12 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_phase_kernel(const GemvPara
             const float a = rnd<T>(acc[0][b]);
             const float g = rnd<T>(acc[1][b]);
             reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + u] = from_f<T>(__fmul_rn(gelu_approx<T>(a), g));
-          } else {  // kGemvQKV
-            const int sect = u / p.inner, rr = u - sect * p.inner;
+          } else {  // kGemvQKV: head-major rows (h, q|k|v, 64)
+            const int h = u / kQkvRowsPerHead, rr = u - h * kQkvRowsPerHead;
+            const int sect = rr >> 6, cc = rr & 63;
             if (sect == 0) {
-              reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + rr] = from_f<T>(acc[0][b]);
+              reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + h * 64 + cc] = from_f<T>(acc[0][b]);
             } else {
-              const int h = rr >> 6, cc = rr & 63;
               T* cache = reinterpret_cast<T*>(sect == 1 ? p.kc : p.vc);
               cache[(((size_t)b * p.H + h) * p.cap + p.pos) * 64 + cc] = from_f<T>(acc[0][b]);
             }
@@ -347,6 +347,42 @@ __device__ __forceinline__ void attn_warp_bf16(const __nv_bfloat16* q, const __n
   out[2 * lane + 1] = __float2bfloat16_rn(o1 / l);
 }
 
+// ---- thread-block cluster helpers (kGemvQKVCluster) ----------------------
+constexpr int kClusterRows = kQkvRowsPerHead / kQkvCluster;  // q/k/v rows per CTA
+// Shared memory appended to the GEMV layout: the new q, k, v of the (row,
+// head) this CTA attends (192 floats, written by every CTA of the cluster),
+// the attention weights (kSelfAttnMaxT floats) and the head's cached keys /
+// values before this position (2 x (kSelfAttnMaxT - 1) x 64 bf16).
+constexpr int kClusterOffAttF = 0;
+constexpr int kClusterOffP = kClusterOffAttF + 192 * 4;
+constexpr int kClusterOffKVStart = kClusterOffP + kSelfAttnMaxT * 4;
+constexpr int kClusterOffKV = (kClusterOffKVStart + 127) & ~127;
+constexpr int kClusterKVStride = 64 * 2 + 16;  // padded row: conflict-free per-lane key rows
+constexpr int kClusterKVBytes = (kSelfAttnMaxT - 1) * kClusterKVStride;
+constexpr int kClusterExtra = kClusterOffKV + 2 * kClusterKVBytes;
+
+__host__ __device__ inline int cluster_ext_offset(int total) { return (total + 127) & ~127; }
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// All threads of all CTAs of the cluster; release / acquire order the
+// shared-memory writes before it against the remote reads after it.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Store to the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ void st_cluster_f32(float* local, uint32_t rank, float v) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
 template <int BMAX, int NT, bool NORM, int MODE>
 __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, const int max_rows) {
   typedef __nv_bfloat16 T;
@@ -357,6 +393,8 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
   uint8_t* xsm = smem + L.w_bytes;
   float* red = reinterpret_cast<float*>(smem + L.w_bytes + L.x_bytes);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.w_bytes + L.x_bytes + L.red_bytes);
+  uint8_t* cl_ext = smem + cluster_ext_offset(L.total);  // kGemvQKVCluster only
+  float* cl_recv = reinterpret_cast<float*>(cl_ext + kClusterOffAttF);
   __shared__ float wred[8][BMAX];
   __shared__ float rstd[BMAX];
   __shared__ int ok_flag;
@@ -393,6 +431,16 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
     for (int r = lane; r < R; r += 32) bulk_g2s_hint(wsm + (size_t)r * L.rstride, src + (size_t)r * row_bytes,
                                                     (uint32_t)row_bytes, bar, pol);
   }
+  // kGemvQKVCluster: the relative-position bias of this query (a table
+  // written at weight load) is read ahead of the dependency wait
+  float cl_bias0 = 0.f, cl_bias1 = 0.f;
+  if constexpr (MODE == kGemvQKVCluster) {
+    if (warp == 0 && p.bias) {
+      const float* bias = p.bias + (size_t)(c / kQkvCluster) * p.bias_stride;
+      if (lane < p.pos + 1) cl_bias0 = bias[lane];
+      if (32 + lane < p.pos + 1) cl_bias1 = bias[32 + lane];
+    }
+  }
   pdl_wait();
 
   // ---- every global load of this phase, issued back to back -------------
@@ -419,6 +467,25 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
         resv[i] = to_f(reinterpret_cast<const T*>(p.resid)[(size_t)b * p.resid_stride + u0 + uu]);
       }
     }
+  }
+
+  // kGemvQKVCluster: CTA rank b < B of head h's cluster attends row b; its
+  // cached keys / values (positions < pos, written by earlier launches)
+  // stream into shared memory while the product runs.
+  if constexpr (MODE == kGemvQKVCluster) {
+    const int crank = (int)cluster_ctarank(), h = c / kQkvCluster;
+    if (crank < p.B) {
+      const size_t base = (((size_t)crank * p.H + h) * p.cap) * 64;
+      const uint8_t* Kc = reinterpret_cast<const uint8_t*>(reinterpret_cast<const T*>(p.kc) + base);
+      const uint8_t* Vc = reinterpret_cast<const uint8_t*>(reinterpret_cast<const T*>(p.vc) + base);
+      const int n16 = p.pos * 8;  // 16-byte chunks of pos rows of 64 bf16
+      for (int i = tid; i < 2 * n16; i += 256) {
+        const int k = i < n16 ? i : i - n16, row = k >> 3, part = k & 7;
+        uint8_t* dst = cl_ext + kClusterOffKV + (i < n16 ? 0 : kClusterKVBytes) + row * kClusterKVStride + part * 16;
+        cp_async16(dst, (i < n16 ? Kc : Vc) + (size_t)k * 16);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
   }
 
   // ---- inputs -> shared memory as bf16 (RMS-normalised when NORM) --------
@@ -502,7 +569,10 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
   const uint32_t xrow = smem_u32(xsm) + (uint32_t)(g * L.rstride) + (uint32_t)(4 * t);
   if (tid == 0 && R > 0) ok_flag = mbar_wait_bounded(bar, 0, p.err);
   __syncthreads();
-  if (!ok_flag || R == 0) return;
+  // (a timed-out weight copy is already reported in the error word; the
+  // cluster variant carries on with whatever shared memory holds so that
+  // every CTA reaches the cluster barriers; it always has rows)
+  if (MODE != kGemvQKVCluster && (!ok_flag || R == 0)) return;
   float acc[NT][4];
 #pragma unroll
   for (int i = 0; i < NT; ++i)
@@ -599,15 +669,101 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
       const float a = rnd<T>(v[0]);
       const float gg = rnd<T>(v[RPU - 1]);
       reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + u] = from_f<T>(__fmul_rn(gelu_approx<T>(a), gg));
-    } else {  // kGemvQKV
-      const int sect = u / p.inner, rr = u - sect * p.inner;
+    } else {  // kGemvQKV / QKVAttn / QKVCluster: head-major rows (h, q|k|v, 64)
+      const int h = u / kQkvRowsPerHead, rr = u - h * kQkvRowsPerHead;
+      const int sect = rr >> 6, cc = rr & 63;
+      const T val = from_f<T>(v[0]);
       if (sect == 0) {
-        reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + rr] = from_f<T>(v[0]);
+        reinterpret_cast<T*>(p.out)[(size_t)b * p.out_stride + h * 64 + cc] = val;
       } else {
-        const int h = rr >> 6, cc = rr & 63;
         T* cache = reinterpret_cast<T*>(sect == 1 ? p.kc : p.vc);
-        cache[(((size_t)b * p.H + h) * p.cap + p.pos) * 64 + cc] = from_f<T>(v[0]);
+        cache[(((size_t)b * p.H + h) * p.cap + p.pos) * 64 + cc] = val;
       }
+      // the head's q/k/v of row b go to CTA rank b of the cluster, which attends (b, h)
+      if (MODE == kGemvQKVCluster) st_cluster_f32(cl_recv + rr, (uint32_t)b, to_f(val));
+    }
+  }
+  if constexpr (MODE == kGemvQKVCluster) {
+    // Every CTA of the head's cluster has stored its q/k/v rows of batch row
+    // b into CTA rank b (distributed shared memory); after the barrier, CTA
+    // b < B runs attn_self_kernel's arithmetic for (b, h) with its cached
+    // keys / values. No CTA reads another's shared memory after the barrier,
+    // so the others may exit.
+    cluster_sync();
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    const int crank = (int)cluster_ctarank(), h = c / kQkvCluster;
+    if (crank < p.B && warp == 0) {
+      const int b = crank, nkeys = p.pos + 1;
+      const float* qn = cl_recv;
+      const float* kn = cl_recv + 64;
+      const float* vn = cl_recv + 128;
+      float* pk = reinterpret_cast<float*>(cl_ext + kClusterOffP);
+      const T* Kold = reinterpret_cast<const T*>(cl_ext + kClusterOffKV);
+      const T* Vold = reinterpret_cast<const T*>(cl_ext + kClusterOffKV + kClusterKVBytes);
+      const bool has_bias = p.bias != nullptr;
+      float sc[2];
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int j = cc * 32 + lane;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        if (j < nkeys) {
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            float kf[8];
+            if (j == nkeys - 1) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) kf[e] = kn[ch * 8 + e];
+            } else {
+              Vec16<T>::unpack(
+                  reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(Kold) + (size_t)j * kClusterKVStride)[ch],
+                  kf);
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e & 3] = fmaf(qn[ch * 8 + e], kf[e], acc[e & 3]);
+          }
+        }
+        float a = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+        if (has_bias) a += (cc == 0 ? cl_bias0 : cl_bias1);
+        sc[cc] = j < nkeys ? a : -INFINITY;
+      }
+      const float m = warp_max(fmaxf(sc[0], sc[1]));
+      const float p0 = lane < nkeys ? expf(sc[0] - m) : 0.f;
+      const float p1 = 32 + lane < nkeys ? expf(sc[1] - m) : 0.f;
+      const float l = warp_sum(p0 + p1);
+      pk[lane] = p0;
+      pk[32 + lane] = p1;
+      __syncwarp();
+      // o = sum_j p_j v_j in key order (the order of attn_self_kernel)
+      float o0 = 0.f, o1 = 0.f;
+      const uint32_t* vrow = reinterpret_cast<const uint32_t*>(Vold) + lane;
+      constexpr int kVw = kClusterKVStride / 4;  // 32-bit words per padded row
+      int jv = 0;
+      for (; jv + 4 <= nkeys - 1; jv += 4) {
+        uint32_t bits[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) bits[q] = vrow[(size_t)(jv + q) * kVw];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float pw = pk[jv + q];
+          o0 = fmaf(pw, __uint_as_float(bits[q] << 16), o0);
+          o1 = fmaf(pw, __uint_as_float(bits[q] & 0xffff0000u), o1);
+        }
+      }
+      for (; jv < nkeys - 1; ++jv) {
+        const uint32_t bits = vrow[(size_t)jv * kVw];
+        const float pw = pk[jv];
+        o0 = fmaf(pw, __uint_as_float(bits << 16), o0);
+        o1 = fmaf(pw, __uint_as_float(bits & 0xffff0000u), o1);
+      }
+      {  // the newest key
+        const float pw = pk[nkeys - 1];
+        o0 = fmaf(pw, vn[2 * lane], o0);
+        o1 = fmaf(pw, vn[2 * lane + 1], o1);
+      }
+      T* out = reinterpret_cast<T*>(p.attn_out) + (size_t)b * p.inner + h * 64;
+      out[2 * lane] = from_f<T>(o0 / l);
+      out[2 * lane + 1] = from_f<T>(o1 / l);
     }
   }
   if constexpr (MODE == kGemvQKVAttn) {
@@ -620,7 +776,7 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
     if (tid == 0) {
       int hs[4], cnt[4], nh = 0;
       for (int u = u0; u < u1; ++u) {
-        const int h = (u % p.inner) >> 6;
+        const int h = u / kQkvRowsPerHead;
         int k = 0;
         while (k < nh && hs[k] != h) ++k;
         if (k == nh) {
@@ -686,6 +842,29 @@ static cudaError_t launch_mma_nt(const GemvParams& p, int grid, int max_rows, cu
   return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<BMAX, NT, NORM, MODE>, p, max_rows);
 }
 
+// kGemvQKVCluster: one cluster of kQkvCluster CTAs per head, kClusterRows
+// q/k/v rows each (three 8-row n-tiles).
+template <int BMAX>
+static cudaError_t launch_mma_cluster(const GemvParams& p, cudaStream_t s, bool pdl) {
+  if (p.units != p.H * kQkvRowsPerHead || p.pos + 1 > kSelfAttnMaxT || !p.attn_out || p.B > kQkvCluster)
+    return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.H * kQkvCluster);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = cluster_ext_offset(mma_layout(p.cols, kClusterRows).total) + kClusterExtra;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kQkvCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<BMAX, 3, true, kGemvQKVCluster>, p, kClusterRows);
+}
+
 template <int BMAX, bool NORM, int MODE>
 static cudaError_t launch_mma_t(const GemvParams& p, int num_sms, cudaStream_t s, bool pdl) {
   int grid, max_rows;
@@ -713,6 +892,8 @@ static cudaError_t launch_gemv_mma_b(int mode, bool norm, const GemvParams& p, i
     case kGemvQKVAttn:
       if (p.pos + 1 > kSelfAttnMaxT || !p.counters || !p.attn_out || p.inner % 64 != 0) return cudaErrorInvalidValue;
       return launch_mma_t<BMAX, true, kGemvQKVAttn>(p, num_sms, s, pdl);
+    case kGemvQKVCluster:
+      return launch_mma_cluster<BMAX>(p, s, pdl);
     case kGemvGeglu:
       return launch_mma_t<BMAX, true, kGemvGeglu>(p, num_sms, s, pdl);
     case kGemvLogits:
@@ -741,6 +922,7 @@ static cudaError_t set_mma_limits_bn() {
   set((const void*)gemv_mma_kernel<BMAX, NT, false, kGemvResid>);
   set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvQKV>);
   set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvQKVAttn>);
+  if (NT == 3) set((const void*)gemv_mma_kernel<BMAX, 3, true, kGemvQKVCluster>);
   set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvGeglu>);
   set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvLogits>);
   return e;

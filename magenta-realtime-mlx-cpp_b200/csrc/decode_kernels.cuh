@@ -17,7 +17,13 @@ enum GemvMode : int {
   kGemvLogits = 4,  // float out[b, off + u] = R(acc)
   kGemvQKVAttn = 5, // kGemvQKV + the self-attention of each head, run by the
                     // CTA whose q/k/v rows complete that head (bf16 only)
+  kGemvQKVCluster = 6,  // kGemvQKV on one thread-block cluster per head; the
+                        // head's attention runs inside the cluster (bf16 only)
 };
+// q/k/v weight rows of a decoder layer are head-major: row h * 192 + s * 64
+// + c is output c of head h in section s (0 = q, 1 = k, 2 = v).
+constexpr int kQkvRowsPerHead = 192;
+constexpr int kQkvCluster = 8;  // CTAs per head in kGemvQKVCluster (24 rows each)
 
 struct GemvParams {
   const void* W;       // weight rows, (units * rows_per_unit, cols), row-major

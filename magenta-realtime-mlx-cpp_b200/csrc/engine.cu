@@ -92,6 +92,9 @@ struct mrtdf_engine {
   // add ~4 dependent L2 round trips to the q/k/v kernel, which measured
   // slower than the separate attention launch.
   bool fuse_attn = false;
+  // bf16 decode self-attention inside a thread-block cluster per head that
+  // also computes the head's q/k/v rows (MRTDF_CLUSTER_ATTN=0: separate kernel)
+  bool cluster_attn = true;
   Arena weights;
   void* emb = nullptr;
   void* enc_norm = nullptr;
@@ -254,6 +257,20 @@ static void upload_weights(mrtdf_engine* E, const WeightSource& src) {
     put(dst, tmp.data(), rows * cols);
     return dst;
   };
+  // decoder q/k/v rows head-major: row h * 192 + s * 64 + c = row h * 64 + c
+  // of q_proj (s = 0), k_proj (1) or v_proj (2), so each head's rows are one
+  // contiguous block (one thread-block cluster per head in the bf16 decode)
+  auto head_qkv = [&](const std::string& p) {
+    const float* w[3] = {fetch(p + "self_attn.q_proj.weight", in * d), fetch(p + "self_attn.k_proj.weight", in * d),
+                         fetch(p + "self_attn.v_proj.weight", in * d)};
+    tmp.resize((size_t)(3 * in * d));
+    for (int64_t h = 0; h < c.num_heads; ++h)
+      for (int sct = 0; sct < 3; ++sct)
+        std::memcpy(&tmp[(size_t)((h * 192 + sct * 64) * d)], w[sct] + h * 64 * d, (size_t)(64 * d) * 4);
+    void* dst = E->weights.take((size_t)(3 * in * d) * es);
+    put(dst, tmp.data(), 3 * in * d);
+    return dst;
+  };
   // interleave wi_0 / wi_1 rows: row 2j = wi_0[j], row 2j+1 = wi_1[j]
   auto geglu = [&](const std::string& p) {
     const float* a = fetch(p + "ffn.wi_0.weight", ff * d);
@@ -287,9 +304,7 @@ static void upload_weights(mrtdf_engine* E, const WeightSource& src) {
   for (int i = 0; i < c.num_temporal_layers; ++i) {
     const std::string p = "temporal_layers." + std::to_string(i) + ".";
     DecLayerDev& L = E->tl[i];
-    L.wqkv = concat({{p + "self_attn.q_proj.weight", in}, {p + "self_attn.k_proj.weight", in},
-                     {p + "self_attn.v_proj.weight", in}},
-                    d);
+    L.wqkv = head_qkv(p);
     L.wo = single(p + "self_attn.o_proj.weight", d * in);
     L.n_self = single(p + "pre_self_attn_norm.weight", d);
     L.wcq = single(p + "cross_attn.q_proj.weight", in * d);
@@ -312,9 +327,7 @@ static void upload_weights(mrtdf_engine* E, const WeightSource& src) {
   for (int i = 0; i < c.num_depth_layers; ++i) {
     const std::string p = "depth_layers." + std::to_string(i) + ".";
     DecLayerDev& L = E->dl[i];
-    L.wqkv = concat({{p + "self_attn.q_proj.weight", in}, {p + "self_attn.k_proj.weight", in},
-                     {p + "self_attn.v_proj.weight", in}},
-                    d);
+    L.wqkv = head_qkv(p);
     L.wo = single(p + "self_attn.o_proj.weight", d * in);
     L.n_self = single(p + "pre_self_attn_norm.weight", d);
     L.wcq = L.wco = L.n_cross = nullptr;
@@ -372,7 +385,8 @@ void gemv(mrtdf_stream* st, int mode, bool norm, GemvParams p) {
   double bytes = (double)p.units * rpu * p.cols * es + (double)p.B * p.cols * es;
   bytes += (double)p.B * p.units * (mode == kGemvLogits ? 4.0 : es) * (mode == kGemvResid ? 2.0 : 1.0);
   if (norm) bytes += (double)p.cols * es;
-  if (mode == kGemvQKVAttn) bytes += 2.0 * p.B * p.H * (p.pos + 1) * 64.0 * es;  // fused attention's K/V reads
+  if (mode == kGemvQKVAttn || mode == kGemvQKVCluster)
+    bytes += 2.0 * p.B * p.H * (p.pos + 1) * 64.0 * es;  // fused attention's K/V reads
   st->gemv_launches += 1;
   st->gemv_bytes += bytes;
   check_cuda(launch_gemv(E->c.dtype, mode, norm, p, E->num_sms, st->s, E->pdl), "gemv launch");
@@ -395,7 +409,10 @@ void enqueue_decoder_layer(mrtdf_stream* st, const DecLayerDev& L, const void* x
   p.cap = cap; p.pos = pos; p.l2_keep = l2_keep;
   // 2. self attention with relative-position bias (scale 1.0): in bf16 fused
   // into the q/k/v kernel (the CTA completing a head attends it)
-  if (E->fuse_attn && c.dtype == MRTDF_DTYPE_BF16) {
+  if (E->cluster_attn && c.dtype == MRTDF_DTYPE_BF16 && st->B <= kQkvCluster) {
+    p.bias = bias; p.bias_stride = bias_stride; p.attn_out = st->ao;
+    gemv(st, kGemvQKVCluster, true, p);
+  } else if (E->fuse_attn && c.dtype == MRTDF_DTYPE_BF16) {
     p.bias = bias; p.bias_stride = bias_stride; p.attn_out = st->ao; p.counters = st->head_cnt;
     gemv(st, kGemvQKVAttn, true, p);
   } else {
@@ -712,6 +729,7 @@ int mrtdf_create(const mrtdf_config* cfg, int device, mrtdf_engine** out) {
     E->pdl = env_flag("MRTDF_PDL", true);
     E->tc_gemm = env_flag("MRTDF_TC_GEMM", true);
     E->fuse_attn = env_flag("MRTDF_FUSE_ATTN", false);
+    E->cluster_attn = env_flag("MRTDF_CLUSTER_ATTN", true);
     CUDA_OK(gemv_set_smem_limits());
     CUDA_OK(gemm_set_smem_limits());
     CUDA_OK(gemm_tc_set_smem_limits());
@@ -1376,7 +1394,8 @@ int mrtdf_bench_depth(mrtdf_stream* st, const mrtdf_gen_opts* o, int frames, int
     *bytes_per_step = (st->gemv_bytes + kv * frames) / steps;
     // per level: layers x (QKV, attention, o_proj, FFN-up, FFN-down) + lm_head + sampler;
     // the attention runs inside the QKV launch when fused
-    const bool fused = E->fuse_attn && c.dtype == MRTDF_DTYPE_BF16;
+    const bool fused =
+        c.dtype == MRTDF_DTYPE_BF16 && (E->fuse_attn || (E->cluster_attn && st->B <= kQkvCluster));
     *launches_per_step = (long long)c.num_depth_layers * (fused ? 4 : 5) + 2;
     check_device_err(st);
   });
