@@ -427,12 +427,13 @@ def depth_microbench(mrtdf, cfg, st) -> dict:
 
 
 def multi_stream(mrtdf, torch, eng, cfg, device, rank: int, world: int, dist, n_streams: int = 64,
-                 per_group: int = 4, rounds: int = 2) -> dict:
+                 per_group: int = 64, rounds: int = 2) -> dict:
     """64 independent CFG streams per GPU (bf16, top-k 40,
-    T 1.1), seeds 100 + global stream index, as 16 engine streams of 4 CFG
-    pairs (8 rows each) whose chunk graphs run concurrently on 16 CUDA
-    streams. Aggregate tokens/s over all ranks; a stream holds real time when
-    its chunk (2 s of audio) takes <= 2 s."""
+    T 1.1), seeds 100 + global stream index, batched as one engine stream of
+    64 CFG pairs (128 rows: RMSNorm + tcgen05 GEMM projections; with
+    per_group < 64, several engine streams run concurrently on their own
+    CUDA streams). Aggregate tokens/s over all ranks; a stream holds real
+    time when its chunk (2 s of audio) takes <= 2 s."""
     groups = n_streams // per_group
     sts = [mrtdf.Stream(eng, per_group, True) for _ in range(groups)]
     exts = [torch.cuda.ExternalStream(s.cuda_stream(), device=device) for s in sts]

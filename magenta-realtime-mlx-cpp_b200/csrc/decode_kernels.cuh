@@ -55,6 +55,9 @@ constexpr int kGemvStageBytes = 24576;
 constexpr int kGemvStages = 3;
 constexpr int kGemvThreads = 256;
 constexpr int kGemvMaxB = 8;
+// Rows per step of a bf16 stream; above kGemvMaxB the projections run as
+// RMSNorm + tcgen05 GEMM with the batch rows as M (one 128-row tile).
+constexpr int kWideMaxRows = 128;
 
 size_t gemv_smem_bytes(int B, int cols);
 // Launch the GEMV phase. dtype 1 (bf16) runs the tensor-core kernel over

@@ -12,6 +12,10 @@ enum GemmEpi : int {
   kEpiResid = 1,    // out[m, n] = R(out[m, n] + R(acc))
   kEpiGeglu = 2,    // columns (2j, 2j+1) = (wi_0, wi_1): out[m, j] = R(gelu(R(a)) * R(b))
   kEpiCrossKV = 3,  // column n of the all-layer K/V projection -> cross cache
+  // decode projections for more rows than the GEMV kernel takes (tcgen05 only)
+  kEpiDecResid = 4,  // out[m, n] = R(resid[m, n] + R(acc))   (resid may alias out)
+  kEpiDecQKV = 5,    // head-major q/k/v rows: q -> out (m, h*64+c), k/v -> cache at `pos`
+  kEpiLogits = 6,    // float out[m, out_offset + n] = R(acc)
 };
 
 struct GemmParams {
@@ -24,6 +28,12 @@ struct GemmParams {
   void* ck;
   void* cv;
   int S, B, H, Smax, inner;
+  // decode epilogues: residual rows (kEpiDecResid), self K/V caches (rows, H,
+  // cap, 64) written at position pos (kEpiDecQKV), column offset (kEpiLogits)
+  const void* resid;
+  int ldr;
+  int cap, pos;
+  int out_offset;
 };
 
 cudaError_t launch_gemm(int dtype, int epi, const GemmParams& p, cudaStream_t s, bool pdl);

@@ -130,6 +130,7 @@ struct mrtdf_stream {
   void *tk, *tv, *ck, *cv, *dk, *dv;
   // encoder scratch
   void *ex, *en, *eqkv, *eo, *eh;
+  void* xn;  // (B, d) normalised rows of the wide decode path
   int32_t* ids;
   int32_t* tokens;  // (nseq, Tmax, depth)
   uint64_t* seeds;  // (nseq)
@@ -375,6 +376,34 @@ static void upload_weights(mrtdf_engine* E, const WeightSource& src) {
 // ---------------------------------------------------------------------------
 namespace {
 
+// A decode projection for more rows than the GEMV kernel takes (up to 128,
+// bf16): RMSNorm rows (when the phase normalises) then the tcgen05 GEMM with
+// the phase's epilogue; the batch rows are the MMA's M.
+void wide_gemv(mrtdf_stream* st, int mode, bool norm, const GemvParams& p) {
+  mrtdf_engine* E = st->eng;
+  const mrtdf_config& c = E->c;
+  const void* A = p.x;
+  if (norm) {
+    check_cuda(launch_rmsnorm_rows(c.dtype, p.x, p.norm_w, st->B, p.cols, st->xn, st->s, E->pdl), "rmsnorm");
+    A = st->xn;
+  }
+  const int rpu = mode == kGemvGeglu ? 2 : 1;
+  GemmParams g{};
+  g.A = A; g.W = p.W; g.out = p.out; g.M = st->B; g.N = p.units * rpu; g.K = p.cols; g.lda = p.x_stride;
+  g.ldo = p.out_stride;
+  int epi = kEpiStore;
+  switch (mode) {
+    case kGemvStore: epi = kEpiStore; break;
+    case kGemvResid: epi = kEpiDecResid; g.resid = p.resid; g.ldr = p.resid_stride; break;
+    case kGemvGeglu: epi = kEpiGeglu; break;
+    case kGemvLogits: epi = kEpiLogits; g.out_offset = p.out_offset; break;
+    case kGemvQKV: epi = kEpiDecQKV; g.ck = p.kc; g.cv = p.vc; g.H = p.H; g.cap = p.cap; g.pos = p.pos; break;
+    default: throw Error{MRTDF_ERR_INVALID, "wide decode path: unsupported projection"};
+  }
+  if (mode == kGemvStore && p.out_offset != 0) throw Error{MRTDF_ERR_INVALID, "wide decode path: column offset"};
+  check_cuda(launch_gemm_tc(epi, g, st->err, st->s, E->pdl), "wide decode gemm");
+}
+
 void gemv(mrtdf_stream* st, int mode, bool norm, GemvParams p) {
   mrtdf_engine* E = st->eng;
   p.err = st->err;
@@ -389,6 +418,10 @@ void gemv(mrtdf_stream* st, int mode, bool norm, GemvParams p) {
     bytes += 2.0 * p.B * p.H * (p.pos + 1) * 64.0 * es;  // fused attention's K/V reads
   st->gemv_launches += 1;
   st->gemv_bytes += bytes;
+  if (st->B > kGemvMaxB) {
+    wide_gemv(st, mode, norm, p);
+    return;
+  }
   check_cuda(launch_gemv(E->c.dtype, mode, norm, p, E->num_sms, st->s, E->pdl), "gemv launch");
 }
 
@@ -412,7 +445,7 @@ void enqueue_decoder_layer(mrtdf_stream* st, const DecLayerDev& L, const void* x
   if (E->cluster_attn && c.dtype == MRTDF_DTYPE_BF16 && st->B <= kQkvCluster) {
     p.bias = bias; p.bias_stride = bias_stride; p.attn_out = st->ao;
     gemv(st, kGemvQKVCluster, true, p);
-  } else if (E->fuse_attn && c.dtype == MRTDF_DTYPE_BF16) {
+  } else if (E->fuse_attn && c.dtype == MRTDF_DTYPE_BF16 && st->B <= kGemvMaxB) {
     p.bias = bias; p.bias_stride = bias_stride; p.attn_out = st->ao; p.counters = st->head_cnt;
     gemv(st, kGemvQKVAttn, true, p);
   } else {
@@ -793,8 +826,10 @@ int mrtdf_stream_create(mrtdf_engine* E, int num_sequences, int cfg, mrtdf_strea
     if (!E->loaded) throw Error{MRTDF_ERR_STATE, "load weights before creating a stream"};
     if (num_sequences <= 0) throw Error{MRTDF_ERR_INVALID, "num_sequences must be positive"};
     const int rps = cfg ? 2 : 1;
-    if (num_sequences * rps > kGemvMaxB)
-      throw Error{MRTDF_ERR_INVALID, "rows per step (num_sequences * (cfg ? 2 : 1)) must be <= 8"};
+    const int max_rows = E->c.dtype == MRTDF_DTYPE_BF16 ? kWideMaxRows : kGemvMaxB;
+    if (num_sequences * rps > max_rows)
+      throw Error{MRTDF_ERR_INVALID, "rows per step (num_sequences * (cfg ? 2 : 1)) must be <= " +
+                                         std::to_string(max_rows) + " (8 in fp32, 128 in bf16)"};
     CUDA_OK(cudaSetDevice(E->device));
     const mrtdf_config& c = E->c;
     auto st = std::make_unique<mrtdf_stream>();
@@ -817,7 +852,7 @@ int mrtdf_stream_create(mrtdf_engine* E, int num_sequences, int cfg, mrtdf_strea
         {&st->dk, c.num_depth_layers * B * H * c.rvq_depth * 64 * es},
         {&st->dv, c.num_depth_layers * B * H * c.rvq_depth * 64 * es},
         {&st->ex, Mx * d * es}, {&st->en, Mx * d * es}, {&st->eqkv, Mx * 3 * in * es}, {&st->eo, Mx * in * es},
-        {&st->eh, Mx * ff * es}, {(void**)&st->ids, Mx * 4},
+        {&st->eh, Mx * ff * es}, {(void**)&st->ids, Mx * 4}, {&st->xn, B * d * es},
         {(void**)&st->tokens, (size_t)num_sequences * c.max_frames * c.rvq_depth * 4},
         {(void**)&st->seeds, (size_t)num_sequences * 8}, {(void**)&st->forced, (size_t)num_sequences * 4},
         {(void**)&st->part, B * H * kCrossSplit * 66 * 4}, {(void**)&st->counters, B * H * 4},
@@ -1394,8 +1429,7 @@ int mrtdf_bench_depth(mrtdf_stream* st, const mrtdf_gen_opts* o, int frames, int
     *bytes_per_step = (st->gemv_bytes + kv * frames) / steps;
     // per level: layers x (QKV, attention, o_proj, FFN-up, FFN-down) + lm_head + sampler;
     // the attention runs inside the QKV launch when fused
-    const bool fused =
-        c.dtype == MRTDF_DTYPE_BF16 && (E->fuse_attn || (E->cluster_attn && st->B <= kQkvCluster));
+    const bool fused = c.dtype == MRTDF_DTYPE_BF16 && st->B <= kQkvCluster && (E->fuse_attn || E->cluster_attn);
     *launches_per_step = (long long)c.num_depth_layers * (fused ? 4 : 5) + 2;
     check_device_err(st);
   });

@@ -224,7 +224,21 @@ __global__ void __launch_bounds__(128, 1)
       const int m = bm + r, n = oc0 + ch * 8;
       if (m >= p.M || n >= ncols) continue;
       uint4 v = *reinterpret_cast<const uint4*>(stile + (size_t)r * kTileLd + ch * 8);
-      if (EPI == kEpiCrossKV) {
+      if (EPI == kEpiLogits) {
+        // bf16-rounded values as float; 8-byte stores (the level's column
+        // offset is only even)
+        float* o = reinterpret_cast<float*>(p.out) + (size_t)m * p.ldo + p.out_offset + n;
+        const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (n + 2 * i < ncols) reinterpret_cast<float2*>(o)[i] = __bfloat1622float2(v2[i]);  // N is only even
+      } else if (EPI == kEpiDecQKV) {
+        const int h = n / 192, rr = n - h * 192, sect = rr >> 6, cc = rr & 63;
+        T* dst = sect == 0 ? reinterpret_cast<T*>(p.out) + (size_t)m * p.ldo + h * 64 + cc
+                           : reinterpret_cast<T*>(sect == 1 ? p.ck : p.cv) +
+                                 (((size_t)m * p.H + h) * p.cap + p.pos) * 64 + cc;
+        *reinterpret_cast<uint4*>(dst) = v;
+      } else if (EPI == kEpiCrossKV) {
         const int two_inner = 2 * p.inner;
         const int layer = n / two_inner, within = n - layer * two_inner;
         const int kv = within / p.inner, rr = within - kv * p.inner;
@@ -234,8 +248,9 @@ __global__ void __launch_bounds__(128, 1)
         *reinterpret_cast<uint4*>(cache + ((((size_t)layer * p.B + b) * p.H + h) * p.Smax + s) * 64 + cc) = v;
       } else {
         T* o = reinterpret_cast<T*>(p.out) + (size_t)m * p.ldo + n;
-        if (EPI == kEpiResid) {
-          const uint4 rv = *reinterpret_cast<const uint4*>(o);
+        if (EPI == kEpiResid || EPI == kEpiDecResid) {
+          const T* rsrc = EPI == kEpiResid ? o : reinterpret_cast<const T*>(p.resid) + (size_t)m * p.ldr + n;
+          const uint4 rv = *reinterpret_cast<const uint4*>(rsrc);
           const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&rv);
           const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&v);
           uint32_t w[4];
@@ -315,14 +330,26 @@ cudaError_t gemm_tc_set_smem_limits() {
   set((const void*)tc::gemm_tc_kernel<kEpiResid>);
   set((const void*)tc::gemm_tc_kernel<kEpiGeglu>);
   set((const void*)tc::gemm_tc_kernel<kEpiCrossKV>);
+  set((const void*)tc::gemm_tc_kernel<kEpiDecResid>);
+  set((const void*)tc::gemm_tc_kernel<kEpiDecQKV>);
+  set((const void*)tc::gemm_tc_kernel<kEpiLogits>);
   return e;
 }
 
 cudaError_t launch_gemm_tc(int epi, const GemmParams& p, int* err, cudaStream_t s, bool pdl) {
   if (p.M <= 0 || p.N <= 0) return cudaSuccess;
   // 16-byte epilogue chunks: 8 output columns (16 GEMM columns for GEGLU)
-  if (p.N % (epi == kEpiGeglu ? 16 : 8) != 0 || p.K % 8 != 0 || p.lda % 8 != 0) return cudaErrorInvalidValue;
-  if (epi != kEpiCrossKV && (p.ldo % 8 != 0 || (reinterpret_cast<uintptr_t>(p.out) & 15))) return cudaErrorInvalidValue;
+  if (p.N % (epi == kEpiGeglu ? 16 : epi == kEpiLogits ? 2 : 8) != 0 || p.K % 8 != 0 || p.lda % 8 != 0)
+    return cudaErrorInvalidValue;
+  if (epi == kEpiLogits) {
+    if (p.ldo % 2 || p.out_offset % 2 || (reinterpret_cast<uintptr_t>(p.out) & 7)) return cudaErrorInvalidValue;
+  } else if (epi != kEpiCrossKV && (p.ldo % 8 != 0 || (reinterpret_cast<uintptr_t>(p.out) & 15))) {
+    return cudaErrorInvalidValue;
+  }
+  if (epi == kEpiDecResid && (p.ldr % 8 || (reinterpret_cast<uintptr_t>(p.resid) & 15))) return cudaErrorInvalidValue;
+  if (epi == kEpiDecQKV && (p.N % 192 || (reinterpret_cast<uintptr_t>(p.ck) & 15) ||
+                            (reinterpret_cast<uintptr_t>(p.cv) & 15)))
+    return cudaErrorInvalidValue;
   if (epi == kEpiCrossKV && (p.inner % 64 != 0 || (reinterpret_cast<uintptr_t>(p.ck) & 15) ||
                              (reinterpret_cast<uintptr_t>(p.cv) & 15)))
     return cudaErrorInvalidValue;
@@ -334,6 +361,9 @@ cudaError_t launch_gemm_tc(int epi, const GemmParams& p, int* err, cudaStream_t 
     case kEpiResid: return tc::launch_t<kEpiResid>(a, b, p, err, s, pdl);
     case kEpiGeglu: return tc::launch_t<kEpiGeglu>(a, b, p, err, s, pdl);
     case kEpiCrossKV: return tc::launch_t<kEpiCrossKV>(a, b, p, err, s, pdl);
+    case kEpiDecResid: return tc::launch_t<kEpiDecResid>(a, b, p, err, s, pdl);
+    case kEpiDecQKV: return tc::launch_t<kEpiDecQKV>(a, b, p, err, s, pdl);
+    case kEpiLogits: return tc::launch_t<kEpiLogits>(a, b, p, err, s, pdl);
   }
   return cudaErrorInvalidValue;
 }

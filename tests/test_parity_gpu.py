@@ -383,3 +383,49 @@ def test_device_streaming_equals_host_loop(mrtdf, tiny_weights):
         want.append(rvq)
     np.testing.assert_array_equal(out_dev.cpu().numpy(), np.stack(want))
     np.testing.assert_array_equal(ctx_dev.cpu().numpy(), ctx)
+
+
+# ---------------------------------------------------------------------------
+# wide bf16 streams (> 8 rows): RMSNorm + tcgen05 GEMM projections
+# ---------------------------------------------------------------------------
+def test_wide_stream_step_api_matches_oracle(mrtdf, oracle, tiny_weights):
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", 1)
+    nseq = 8  # 16 rows
+    ids = np.concatenate([random_ids(cfg, 2, 60, seed=50 + i) for i in range(nseq)])
+    st = mrtdf.Stream(eng, nseq, True)
+    assert st.rows == 16
+    orc = oracle.Oracle(tiny_weights, cfg.as_ints())
+    st.encode(ids)
+    orc.encode(ids)
+    rng = np.random.default_rng(5)
+    x = None
+    for f in range(3):
+        a = st.temporal_step(x, f)
+        b = orc.temporal_step(x, f)
+        assert np.abs(a - b).max() <= BF16_TOL * 4, f
+        d = None
+        for l in range(4):
+            la = st.depth_step(d, l)
+            lb = orc.depth_step(d, l)
+            assert np.abs(la - lb).max() <= BF16_TOL, (f, l)
+            d = rng.standard_normal((16, cfg.d_model)).astype(np.float32) * 0.5
+        x = rng.standard_normal((16, cfg.d_model)).astype(np.float32) * 0.5
+
+
+def test_wide_stream_generation(mrtdf, tiny_weights):
+    """64 CFG pairs in one stream: tokens in their level ranges, graph replay
+    equal to stream launches, sequence i independent of its neighbours."""
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", 1)
+    nseq = 64
+    ids = np.concatenate([random_ids(cfg, 2, cfg.max_encoder_length, seed=60 + i % 4) for i in range(nseq)])
+    st = mrtdf.Stream(eng, nseq, True)
+    o = mrtdf.gen_opts(cfg, cfg.max_frames, seed=7)
+    seeds = [100 + (i % 4) for i in range(nseq)]
+    a = st.generate_tokens(ids, o, seeds=seeds)
+    b = st.generate_tokens(ids, o, seeds=seeds)  # graph replay
+    np.testing.assert_array_equal(a, b)
+    lo = cfg.codec_offset + np.arange(cfg.rvq_depth) * cfg.codebook_size
+    assert ((a >= lo) & (a < lo + cfg.codebook_size)).all()
+    # sequences with the same ids and seed decode the same tokens
+    for i in range(4, nseq):
+        np.testing.assert_array_equal(a[i], a[i % 4])
