@@ -34,6 +34,9 @@ struct GemmParams {
   int ldr;
   int cap, pos;
   int out_offset;
+  // tcgen05 only: largest split-K cluster (1, 2, 4 or 8) the launcher may
+  // choose when the output tiles cannot fill the GPU (0 or 1: no split)
+  int max_ksplit;
 };
 
 cudaError_t launch_gemm(int dtype, int epi, const GemmParams& p, cudaStream_t s, bool pdl);

@@ -95,6 +95,9 @@ struct mrtdf_engine {
   // bf16 decode self-attention inside a thread-block cluster per head that
   // also computes the head's q/k/v rows (MRTDF_CLUSTER_ATTN=0: separate kernel)
   bool cluster_attn = true;
+  // wide streams: largest split-K cluster of the tcgen05 decode GEMMs
+  // (MRTDF_WIDE_KSPLIT, default 1 = off: measured slower)
+  int wide_ksplit = 1;
   Arena weights;
   void* emb = nullptr;
   void* enc_norm = nullptr;
@@ -401,6 +404,7 @@ void wide_gemv(mrtdf_stream* st, int mode, bool norm, const GemvParams& p) {
     default: throw Error{MRTDF_ERR_INVALID, "wide decode path: unsupported projection"};
   }
   if (mode == kGemvStore && p.out_offset != 0) throw Error{MRTDF_ERR_INVALID, "wide decode path: column offset"};
+  g.max_ksplit = E->wide_ksplit;
   check_cuda(launch_gemm_tc(epi, g, st->err, st->s, E->pdl), "wide decode gemm");
 }
 
@@ -763,6 +767,7 @@ int mrtdf_create(const mrtdf_config* cfg, int device, mrtdf_engine** out) {
     E->tc_gemm = env_flag("MRTDF_TC_GEMM", true);
     E->fuse_attn = env_flag("MRTDF_FUSE_ATTN", false);
     E->cluster_attn = env_flag("MRTDF_CLUSTER_ATTN", true);
+    if (const char* v = std::getenv("MRTDF_WIDE_KSPLIT")) E->wide_ksplit = std::max(1, std::min(8, std::atoi(v)));
     CUDA_OK(gemv_set_smem_limits());
     CUDA_OK(gemm_set_smem_limits());
     CUDA_OK(gemm_tc_set_smem_limits());

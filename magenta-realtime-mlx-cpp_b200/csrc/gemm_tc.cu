@@ -95,7 +95,60 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+// ---- split-K over a thread-block cluster (few output tiles, long K) -------
+// CTA z of a cluster (z = blockIdx.z, cluster dims (1, 1, KSPLIT)) runs k-tiles
+// [z KT / KSPLIT, (z + 1) KT / KSPLIT) into its own TMEM accumulator, parks the
+// fp32 partial tile in its shared memory and, after a cluster barrier, sums
+// rows [z * 128 / KSPLIT, ...) of all KSPLIT partials in rank order through
+// distributed shared memory before running the epilogue on those rows.
+constexpr int kPartLd = BN + 4;                      // floats per partial-tile row
+constexpr int kPartBytes = BM * kPartLd * 4;         // 66 KB
+static_assert(kPartBytes + (BM / 2) * kTileLd * 2 <= STAGES * STAGE_BYTES,
+              "split-K partial tile + epilogue rows must fit the pipeline buffers");
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float4 ld_cluster_f32x4(const float* local, uint32_t rank) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(ra)
+               : "memory");
+  return v;
+}
+
+// 16 fp32 accumulator columns [c, c + 16) of one tile row -> bf16 tile row
+// (GEGLU: 8 output columns at c / 2).
 template <int EPI>
+__device__ __forceinline__ void tile_row_store(__nv_bfloat16* srow, int c, const float* f) {
+  typedef __nv_bfloat16 T;
+  if (EPI == kEpiGeglu) {
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a0 = rnd<T>(f[4 * i]), g0 = rnd<T>(f[4 * i + 1]);
+      const float a1 = rnd<T>(f[4 * i + 2]), g1 = rnd<T>(f[4 * i + 3]);
+      const __nv_bfloat162 pr =
+          __floats2bfloat162_rn(__fmul_rn(gelu_approx<T>(a0), g0), __fmul_rn(gelu_approx<T>(a1), g1));
+      o[i] = *reinterpret_cast<const uint32_t*>(&pr);
+    }
+    *reinterpret_cast<uint4*>(srow + (c >> 1)) = make_uint4(o[0], o[1], o[2], o[3]);
+  } else {
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const __nv_bfloat162 pr = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+      o[i] = *reinterpret_cast<const uint32_t*>(&pr);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(srow + c);
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+template <int EPI, int KSPLIT>
 __global__ void __launch_bounds__(128, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmParams p, int* err) {
@@ -110,7 +163,10 @@ __global__ void __launch_bounds__(128, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bm = blockIdx.y * BM, bn = blockIdx.x * BN;
-  const int KT = (p.K + BK - 1) / BK;
+  const int KT_all = (p.K + BK - 1) / BK;
+  const int kz = KSPLIT > 1 ? (int)blockIdx.z : 0;
+  const int kt0 = kz * KT_all / KSPLIT, kt1 = (kz + 1) * KT_all / KSPLIT;
+  const int KT = kt1 - kt0;
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -145,8 +201,8 @@ __global__ void __launch_bounds__(128, 1)
       }
       uint8_t* sa = smem + s * STAGE_BYTES;
       mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-      tma_load_2d(sa, &tmA, kt * BK, bm, &full[s]);
-      tma_load_2d(sa + A_BYTES, &tmB, kt * BK, bn, &full[s]);
+      tma_load_2d(sa, &tmA, (kt0 + kt) * BK, bm, &full[s]);
+      tma_load_2d(sa + A_BYTES, &tmB, (kt0 + kt) * BK, bn, &full[s]);
     }
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer ----
@@ -173,57 +229,88 @@ __global__ void __launch_bounds__(128, 1)
   // the TMEM loads below are .sync.aligned: decide CTA-uniformly
   const bool ok = __syncthreads_and(mbar_wait_bounded(done, 0, err) ? 1 : 0) && !abort_flag;
   tc_fence_after();
-  if (ok) {
-    // Phase 1: TMEM -> registers -> a bf16 tile in the (now idle) pipeline
-    // shared memory; thread = tile row. GEGLU pairs (a, g) become one column.
-    typedef __nv_bfloat16 T;
-    T* stile = reinterpret_cast<T*>(smem);
-    const int r_local = warp * 32 + lane;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+  // Rows [r0, r1) of the tile get the epilogue in this CTA; their bf16 values
+  // sit at stile (row r at (r - r0) * kTileLd).
+  typedef __nv_bfloat16 T;
+  int r0 = 0, r1 = BM;
+  T* stile = reinterpret_cast<T*>(smem);
+  if constexpr (KSPLIT == 1) {
+    if (ok) {
+      // Phase 1: TMEM -> registers -> a bf16 tile in the (now idle) pipeline
+      // shared memory; thread = tile row. GEGLU pairs (a, g) become one column.
+      const int r_local = warp * 32 + lane;
+      const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      uint32_t r[16];
-      tmem_ld16(lane_base + (uint32_t)c, r);
-      tmem_wait_ld();
-      if (EPI == kEpiGeglu) {
-        uint32_t o[4];
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(lane_base + (uint32_t)c, r);
+        tmem_wait_ld();
+        float f[16];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float a0 = rnd<T>(__uint_as_float(r[4 * i])), g0 = rnd<T>(__uint_as_float(r[4 * i + 1]));
-          const float a1 = rnd<T>(__uint_as_float(r[4 * i + 2])), g1 = rnd<T>(__uint_as_float(r[4 * i + 3]));
-          const __nv_bfloat162 pr =
-              __floats2bfloat162_rn(__fmul_rn(gelu_approx<T>(a0), g0), __fmul_rn(gelu_approx<T>(a1), g1));
-          o[i] = *reinterpret_cast<const uint32_t*>(&pr);
-        }
-        *reinterpret_cast<uint4*>(stile + (size_t)r_local * kTileLd + (c >> 1)) = make_uint4(o[0], o[1], o[2], o[3]);
-      } else {
-        uint32_t o[8];
+        for (int q = 0; q < 16; ++q) f[q] = __uint_as_float(r[q]);
+        tile_row_store<EPI>(stile + (size_t)r_local * kTileLd, c, f);
+      }
+    }
+  } else {
+    // Split-K: park this CTA's fp32 partial tile, then reduce a row slice
+    // over the cluster in rank order.
+    float* part = reinterpret_cast<float*>(smem);
+    if (ok) {
+      const int r_local = warp * 32 + lane;
+      const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(lane_base + (uint32_t)c, r);
+        tmem_wait_ld();
+        float4* dst = reinterpret_cast<float4*>(part + (size_t)r_local * kPartLd + c);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const __nv_bfloat162 pr = __floats2bfloat162_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-          o[i] = *reinterpret_cast<const uint32_t*>(&pr);
+        for (int q = 0; q < 4; ++q)
+          dst[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
+                               __uint_as_float(r[4 * q + 3]));
+      }
+    }
+    cluster_sync_all();  // every partial is in place (every CTA arrives, ok or not)
+    constexpr int RS = BM / KSPLIT;  // rows reduced by this CTA
+    r0 = kz * RS;
+    r1 = r0 + RS;
+    stile = reinterpret_cast<T*>(smem + kPartBytes);
+    if (ok) {
+      // thread -> (row, 16-column group): RS rows x 8 groups over 128 threads
+      for (int item = tid; item < RS * (BN / 16); item += 128) {
+        const int rr = item / (BN / 16), c = (item - rr * (BN / 16)) * 16;
+        const float* src = part + (size_t)(r0 + rr) * kPartLd + c;
+        float f[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 v = ld_cluster_f32x4(src + 4 * q, 0);
+          f[4 * q] = v.x; f[4 * q + 1] = v.y; f[4 * q + 2] = v.z; f[4 * q + 3] = v.w;
         }
-        uint4* dst = reinterpret_cast<uint4*>(stile + (size_t)r_local * kTileLd + c);
-        dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-        dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+#pragma unroll 1
+        for (int z = 1; z < KSPLIT; ++z) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 v = ld_cluster_f32x4(src + 4 * q, (uint32_t)z);
+            f[4 * q] += v.x; f[4 * q + 1] += v.y; f[4 * q + 2] += v.z; f[4 * q + 3] += v.w;
+          }
+        }
+        tile_row_store<EPI>(stile + (size_t)rr * kTileLd, c, f);
       }
     }
   }
   __syncthreads();
   if (ok) {
     // Phase 2: 16-byte stores along output rows (8 columns per chunk).
-    typedef __nv_bfloat16 T;
-    const T* stile = reinterpret_cast<const T*>(smem);
     constexpr int OC = (EPI == kEpiGeglu) ? BN / 2 : BN;  // output columns of the tile
     constexpr int CPR = OC / 8;                          // 16-byte chunks per row
     const int oc0 = (EPI == kEpiGeglu) ? bn / 2 : bn;
     const int ncols = (EPI == kEpiGeglu) ? p.N / 2 : p.N;
 #pragma unroll 4
-    for (int idx = tid; idx < BM * CPR; idx += 128) {
-      const int r = idx / CPR, ch = idx - r * CPR;
-      const int m = bm + r, n = oc0 + ch * 8;
+    for (int idx = tid; idx < (r1 - r0) * CPR; idx += 128) {
+      const int rl = idx / CPR, ch = idx - rl * CPR;
+      const int m = bm + r0 + rl, n = oc0 + ch * 8;
       if (m >= p.M || n >= ncols) continue;
-      uint4 v = *reinterpret_cast<const uint4*>(stile + (size_t)r * kTileLd + ch * 8);
+      uint4 v = *reinterpret_cast<const uint4*>(stile + (size_t)rl * kTileLd + ch * 8);
       if (EPI == kEpiLogits) {
         // bf16-rounded values as float; 8-byte stores (the level's column
         // offset is only even)
@@ -266,6 +353,8 @@ __global__ void __launch_bounds__(128, 1)
       }
     }
   }
+  // split-K: no CTA leaves while others may still read its partial tile
+  if constexpr (KSPLIT > 1) cluster_sync_all();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -302,37 +391,79 @@ bool make_map(CUtensorMap* m, const void* base, int rows, int cols, int ld) {
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int EPI>
+template <int EPI, int KSPLIT>
 cudaError_t launch_t(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int* err, cudaStream_t s,
                      bool pdl) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((p.N + BN - 1) / BN, (p.M + BM - 1) / BM);
+  cfg.gridDim = dim3((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, KSPLIT);
   cfg.blockDim = dim3(128);
   cfg.dynamicSmemBytes = SMEM;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (KSPLIT > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = KSPLIT;
+    ++n;
+  }
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EPI>, a, b, p, err);
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EPI, KSPLIT>, a, b, p, err);
+}
+
+template <int EPI>
+cudaError_t launch_split(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int ksplit, int* err,
+                         cudaStream_t s, bool pdl) {
+  switch (ksplit) {
+    case 2: return launch_t<EPI, 2>(a, b, p, err, s, pdl);
+    case 4: return launch_t<EPI, 4>(a, b, p, err, s, pdl);
+    case 8: return launch_t<EPI, 8>(a, b, p, err, s, pdl);
+    default: return launch_t<EPI, 1>(a, b, p, err, s, pdl);
+  }
+}
+
+// Split-K factor: when the output tiles cannot fill the GPU (the decode
+// projections of a wide stream: 8-44 tiles), split K over a cluster of up
+// to max_ksplit CTAs while the grid stays within one wave and each CTA keeps
+// >= 2 k-tiles. (Measured on the 128-row decode: 655 ms per chunk with up
+// to 8-way splits against 608 ms without, so the engine leaves it off by
+// default; the rank-ordered DSMEM reduction is on the critical path.)
+int choose_ksplit(int tiles, int kt, int num_sms, int max_ksplit) {
+  int k = 1;
+  while (k < 8 && k < max_ksplit && tiles * k * 2 <= num_sms && kt >= 4 * k) k *= 2;
+  return k;
 }
 
 }  // namespace tc
 
-cudaError_t gemm_tc_set_smem_limits() {
-  cudaError_t e = cudaSuccess;
+template <int EPI>
+static void set_limits_epi(cudaError_t& e) {
   auto set = [&](const void* f) {
     cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM);
     if (r != cudaSuccess) e = r;
   };
-  set((const void*)tc::gemm_tc_kernel<kEpiStore>);
-  set((const void*)tc::gemm_tc_kernel<kEpiResid>);
-  set((const void*)tc::gemm_tc_kernel<kEpiGeglu>);
-  set((const void*)tc::gemm_tc_kernel<kEpiCrossKV>);
-  set((const void*)tc::gemm_tc_kernel<kEpiDecResid>);
-  set((const void*)tc::gemm_tc_kernel<kEpiDecQKV>);
-  set((const void*)tc::gemm_tc_kernel<kEpiLogits>);
+  set((const void*)tc::gemm_tc_kernel<EPI, 1>);
+  set((const void*)tc::gemm_tc_kernel<EPI, 2>);
+  set((const void*)tc::gemm_tc_kernel<EPI, 4>);
+  set((const void*)tc::gemm_tc_kernel<EPI, 8>);
+}
+
+cudaError_t gemm_tc_set_smem_limits() {
+  cudaError_t e = cudaSuccess;
+  set_limits_epi<kEpiStore>(e);
+  set_limits_epi<kEpiResid>(e);
+  set_limits_epi<kEpiGeglu>(e);
+  set_limits_epi<kEpiCrossKV>(e);
+  set_limits_epi<kEpiDecResid>(e);
+  set_limits_epi<kEpiDecQKV>(e);
+  set_limits_epi<kEpiLogits>(e);
   return e;
 }
 
@@ -356,14 +487,18 @@ cudaError_t launch_gemm_tc(int epi, const GemmParams& p, int* err, cudaStream_t 
   if ((reinterpret_cast<uintptr_t>(p.A) & 15) || (reinterpret_cast<uintptr_t>(p.W) & 15)) return cudaErrorInvalidValue;
   CUtensorMap a, b;
   if (!tc::make_map(&a, p.A, p.M, p.K, p.lda) || !tc::make_map(&b, p.W, p.N, p.K, p.K)) return cudaErrorInvalidValue;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int tiles = ((p.N + tc::BN - 1) / tc::BN) * ((p.M + tc::BM - 1) / tc::BM);
+  const int ks = tc::choose_ksplit(tiles, (p.K + tc::BK - 1) / tc::BK, sms, p.max_ksplit);
   switch (epi) {
-    case kEpiStore: return tc::launch_t<kEpiStore>(a, b, p, err, s, pdl);
-    case kEpiResid: return tc::launch_t<kEpiResid>(a, b, p, err, s, pdl);
-    case kEpiGeglu: return tc::launch_t<kEpiGeglu>(a, b, p, err, s, pdl);
-    case kEpiCrossKV: return tc::launch_t<kEpiCrossKV>(a, b, p, err, s, pdl);
-    case kEpiDecResid: return tc::launch_t<kEpiDecResid>(a, b, p, err, s, pdl);
-    case kEpiDecQKV: return tc::launch_t<kEpiDecQKV>(a, b, p, err, s, pdl);
-    case kEpiLogits: return tc::launch_t<kEpiLogits>(a, b, p, err, s, pdl);
+    case kEpiStore: return tc::launch_split<kEpiStore>(a, b, p, ks, err, s, pdl);
+    case kEpiResid: return tc::launch_split<kEpiResid>(a, b, p, ks, err, s, pdl);
+    case kEpiGeglu: return tc::launch_split<kEpiGeglu>(a, b, p, ks, err, s, pdl);
+    case kEpiCrossKV: return tc::launch_split<kEpiCrossKV>(a, b, p, ks, err, s, pdl);
+    case kEpiDecResid: return tc::launch_split<kEpiDecResid>(a, b, p, ks, err, s, pdl);
+    case kEpiDecQKV: return tc::launch_split<kEpiDecQKV>(a, b, p, ks, err, s, pdl);
+    case kEpiLogits: return tc::launch_split<kEpiLogits>(a, b, p, ks, err, s, pdl);
   }
   return cudaErrorInvalidValue;
 }
