@@ -24,6 +24,7 @@
 namespace mrtdf {
 
 constexpr int kSelfAttnMaxT = 64;  // keys of a decode self-attention (2 chunks of 32)
+constexpr int kFlagSpinLimit = 1 << 20;  // polls of a flag-carrying input (~1 s) before giving up
 
 // ---------------------------------------------------------------------------
 // GEMV phase kernel
@@ -401,8 +402,10 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, c = blockIdx.x;
-  const int u0 = (int)(((long long)c * p.units) / G);
-  const int u1 = (int)(((long long)(c + 1) * p.units) / G);
+  // flag-carrying output words hold unit pairs: split at even units
+  const int upair = p.out_flag ? 2 : 1;
+  const int u0 = upair * (int)(((long long)c * (p.units / upair)) / G);
+  const int u1 = upair * (int)(((long long)(c + 1) * (p.units / upair)) / G);
   const int R = (u1 - u0) * RPU;
   const int row_bytes = p.cols * 2;
   const int nchunk = p.cols >> 3;  // 16-byte chunks per row
@@ -441,19 +444,64 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
       if (32 + lane < p.pos + 1) cl_bias1 = bias[32 + lane];
     }
   }
-  pdl_wait();
-
   // ---- every global load of this phase, issued back to back -------------
   // inputs: thread owns 16-byte chunks ch = tid + 256 i (i < 2: cols <= 4096)
   uint4 xin[BMAX][2];
+  bool ll_in = false;
+  if constexpr (BMAX <= 4) ll_in = p.x_flag != 0;
+  if (!ll_in) {
+    pdl_wait();
 #pragma unroll
-  for (int b = 0; b < BMAX; ++b)
+    for (int b = 0; b < BMAX; ++b)
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int ch = tid + i * 256;
-      xin[b][i] = (b < p.B && ch < nchunk) ? *reinterpret_cast<const uint4*>(x_ptr + (size_t)b * p.x_stride + ch * 8)
-                                          : make_uint4(0, 0, 0, 0);
+      for (int i = 0; i < 2; ++i) {
+        const int ch = tid + i * 256;
+        xin[b][i] = (b < p.B && ch < nchunk) ? *reinterpret_cast<const uint4*>(x_ptr + (size_t)b * p.x_stride + ch * 8)
+                                            : make_uint4(0, 0, 0, 0);
+      }
+  } else if constexpr (BMAX <= 4) {
+    // Poll the previous launch's flag-carrying words: chunk ch (8 values) is
+    // four 8-byte words = two 16-byte loads; every load is retried until all
+    // its flags read x_flag (L1 bypassed: the words are written while this
+    // launch runs). No dependency wait: this launch only reads data of the
+    // previous launch through these words, and older data, which the previous
+    // launch had fully seen before it let this launch start.
+    const uint32_t f = p.x_flag;
+    const uint4* xw = reinterpret_cast<const uint4*>(p.x);
+    const int wrow = p.x_stride >> 2;  // 16-byte loads per row (2 values each half)
+    uint4 lw[BMAX][2][2];
+    bool gave_up = *reinterpret_cast<volatile const int*>(p.err) & kErrCounterTimeout;
+    for (int it = 0; !gave_up; ++it) {
+      bool ok = true;
+#pragma unroll
+      for (int b = 0; b < BMAX; ++b)
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int ch = tid + i * 256;
+          if (b < p.B && ch < nchunk) {
+            const uint4* src = xw + (size_t)b * wrow + 2 * ch;
+            lw[b][i][0] = __ldcv(src);
+            lw[b][i][1] = __ldcv(src + 1);
+            ok = ok && lw[b][i][0].y == f && lw[b][i][0].w == f && lw[b][i][1].y == f && lw[b][i][1].w == f;
+          }
+        }
+      if (ok) break;
+      if (it >= kFlagSpinLimit) {
+        atomicOr(p.err, kErrCounterTimeout);
+        gave_up = true;
+      }
+      __nanosleep(64);  // back off: the polls share L2 bandwidth with the producer
     }
+#pragma unroll
+    for (int b = 0; b < BMAX; ++b)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int ch = tid + i * 256;
+        xin[b][i] = (b < p.B && ch < nchunk)
+                        ? make_uint4(lw[b][i][0].x, lw[b][i][0].z, lw[b][i][1].x, lw[b][i][1].z)
+                        : make_uint4(0, 0, 0, 0);
+      }
+  }
   // residual values of the epilogue (same thread -> (unit, row) mapping)
   const int nunits = u1 - u0;
   float resv[2];
@@ -464,7 +512,8 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
       resv[i] = 0.f;
       if (idx < nunits * p.B) {
         const int uu = idx / p.B, b = idx - uu * p.B;
-        resv[i] = to_f(reinterpret_cast<const T*>(p.resid)[(size_t)b * p.resid_stride + u0 + uu]);
+        const T* rp = reinterpret_cast<const T*>(p.resid) + (size_t)b * p.resid_stride + u0 + uu;
+        resv[i] = ll_in ? __bfloat162float(__ldcg(rp)) : to_f(*rp);
       }
     }
   }
@@ -643,6 +692,34 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
   __syncthreads();
 
   // ---- cross-warp reduction + fused epilogue: one thread per (unit, row b)
+  if (MODE == kGemvGeglu && p.out_flag) {
+    // flag-carrying output: one thread per (unit pair, row b) writes one
+    // 8-byte word (bf16 pair, flag)
+    for (int idx = tid; idx < (nunits >> 1) * p.B; idx += 256) {
+      const int pu = idx / p.B, b = idx - pu * p.B;
+      float val[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        float v2[2];
+#pragma unroll
+        for (int qq = 0; qq < 2; ++qq) {
+          const int rr = (2 * pu + q) * 2 + qq;
+          const int nt = rr >> 3, col = rr & 7;
+          float sacc = 0.f;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) sacc += red[((w * 8 + nt) * 8 + col) * BMAX + b];
+          v2[qq] = sacc;
+        }
+        val[q] = __fmul_rn(gelu_approx<T>(rnd<T>(v2[0])), rnd<T>(v2[1]));
+      }
+      const __nv_bfloat162 pr = __floats2bfloat162_rn(val[0], val[1]);
+      uint32_t* dst = reinterpret_cast<uint32_t*>(p.out) + 2 * ((size_t)b * (p.out_stride >> 1) + ((u0 >> 1) + pu));
+      asm volatile("st.global.v2.u32 [%0], {%1, %2};" ::"l"(dst), "r"(*reinterpret_cast<const uint32_t*>(&pr)),
+                   "r"(p.out_flag)
+                   : "memory");
+    }
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const int idx = tid + i * 256;
@@ -815,16 +892,17 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
 
 // Grid for the tensor-core GEMV: at least one CTA per SM when there are
 // enough units, and no CTA with more rows than fit its shared memory.
-static void mma_plan(int units, int rpu, int cols, int num_sms, int* grid, int* max_rows) {
+static void mma_plan(int units, int rpu, int cols, int num_sms, int* grid, int* max_rows, int upair = 1) {
   const int rstride = cols * 2 + 16;
   int cap_rows = (190 * 1024) / rstride;
   cap_rows = min(cap_rows, kMmaMaxRows);
-  cap_rows -= cap_rows % rpu;
-  int G = min(units, num_sms);
+  cap_rows -= cap_rows % (rpu * upair);
+  const int groups = units / upair;  // units are split in groups of upair
+  int G = min(groups, num_sms);
   const int need = (units * rpu + cap_rows - 1) / cap_rows;
   if (need > G) G = need;
   *grid = G;
-  *max_rows = ((units + G - 1) / G) * rpu;
+  *max_rows = ((groups + G - 1) / G) * upair * rpu;
 }
 
 template <int BMAX, int NT, bool NORM, int MODE>
@@ -868,7 +946,9 @@ static cudaError_t launch_mma_cluster(const GemvParams& p, cudaStream_t s, bool 
 template <int BMAX, bool NORM, int MODE>
 static cudaError_t launch_mma_t(const GemvParams& p, int num_sms, cudaStream_t s, bool pdl) {
   int grid, max_rows;
-  mma_plan(p.units, MODE == kGemvGeglu ? 2 : 1, p.cols, num_sms, &grid, &max_rows);
+  if (p.out_flag && (MODE != kGemvGeglu || BMAX > 4 || p.units % 2)) return cudaErrorInvalidValue;
+  if (p.x_flag && (BMAX > 4 || p.x_stride % 8)) return cudaErrorInvalidValue;
+  mma_plan(p.units, MODE == kGemvGeglu ? 2 : 1, p.cols, num_sms, &grid, &max_rows, p.out_flag ? 2 : 1);
   if (max_rows > kMmaMaxRows || grid <= 0) return cudaErrorInvalidValue;
   switch ((max_rows + 7) / 8) {
     case 1: return launch_mma_nt<BMAX, 1, NORM, MODE>(p, grid, max_rows, s, pdl);

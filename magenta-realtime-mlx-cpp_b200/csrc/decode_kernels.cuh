@@ -48,6 +48,12 @@ struct GemvParams {
   int bias_stride;
   void* attn_out;
   int* counters;
+  // Flag-carrying activations (B <= 4, bf16): x_flag != 0 -> x is stored as
+  // 8-byte words (bf16 pair, 32-bit flag) written by the previous launch,
+  // which this launch polls for x_flag instead of waiting for that launch to
+  // complete; out_flag != 0 -> the GEGLU output is written that way.
+  uint32_t x_flag;
+  uint32_t out_flag;
 };
 
 // Bytes of one TMA stage of the GEMV kernel and the number of stages.

@@ -96,8 +96,10 @@ struct mrtdf_engine {
   // also computes the head's q/k/v rows (MRTDF_CLUSTER_ATTN=0: separate kernel)
   bool cluster_attn = true;
   // wide streams: largest split-K cluster of the tcgen05 decode GEMMs
-  // (MRTDF_WIDE_KSPLIT, default 1 = off: measured slower)
-  int wide_ksplit = 1;
+  // (MRTDF_WIDE_KSPLIT; 64 CFG pairs: 607 ms per chunk unsplit, 504 ms at 8)
+  int wide_ksplit = 8;
+  // flag-carrying activations on the FFN-up -> FFN-down edge (MRTDF_LL)
+  bool flag_acts = false;
   Arena weights;
   void* emb = nullptr;
   void* enc_norm = nullptr;
@@ -141,6 +143,10 @@ struct mrtdf_stream {
   float* part;
   int* counters;
   int* head_cnt;  // (H) arrival counters of the fused q/k/v + attention kernel
+  // flag-carrying FFN hidden rows (hb as (bf16 pair, flag) words): the
+  // FFN-down launch polls them instead of waiting for the FFN-up launch
+  bool ll = false;
+  uint32_t ll_ctr = 0;
   int* err;
   float* uniforms = nullptr;
   size_t uniforms_cap = 0;
@@ -486,11 +492,18 @@ void enqueue_decoder_layer(mrtdf_stream* st, const DecLayerDev& L, const void* x
   p = GemvParams{};
   p.W = L.wi; p.x = xr; p.norm_w = L.n_ffn; p.out = st->hb; p.units = ff; p.cols = d; p.x_stride = d;
   p.out_stride = ff; p.l2_keep = l2_keep;
+  uint32_t hb_flag = 0;
+  if (st->ll) {
+    if (++st->ll_ctr == 0) st->ll_ctr = 1;  // 0 means "plain rows"
+    hb_flag = st->ll_ctr;
+  }
+  p.out_flag = hb_flag;
   gemv(st, kGemvGeglu, true, p);
   // 8. wo + residual
   p = GemvParams{};
   p.W = L.wout; p.x = st->hb; p.out = xr; p.resid = xr; p.units = d; p.cols = ff; p.x_stride = ff;
   p.out_stride = d; p.resid_stride = d; p.l2_keep = l2_keep;
+  p.x_flag = hb_flag;
   gemv(st, kGemvResid, false, p);
 }
 
@@ -767,6 +780,7 @@ int mrtdf_create(const mrtdf_config* cfg, int device, mrtdf_engine** out) {
     E->tc_gemm = env_flag("MRTDF_TC_GEMM", true);
     E->fuse_attn = env_flag("MRTDF_FUSE_ATTN", false);
     E->cluster_attn = env_flag("MRTDF_CLUSTER_ATTN", true);
+    E->flag_acts = env_flag("MRTDF_LL", false);
     if (const char* v = std::getenv("MRTDF_WIDE_KSPLIT")) E->wide_ksplit = std::max(1, std::min(8, std::atoi(v)));
     CUDA_OK(gemv_set_smem_limits());
     CUDA_OK(gemm_set_smem_limits());
@@ -842,13 +856,14 @@ int mrtdf_stream_create(mrtdf_engine* E, int num_sequences, int cfg, mrtdf_strea
     st->nseq = num_sequences;
     st->rps = rps;
     st->B = num_sequences * rps;
+    st->ll = E->flag_acts && E->c.dtype == MRTDF_DTYPE_BF16 && st->B <= 4;
     CUDA_OK(cudaStreamCreateWithFlags(&st->s, cudaStreamNonBlocking));
     const size_t B = st->B, d = c.d_model, in = E->inner(), ff = c.d_ff, V = c.vocab_size, H = c.num_heads;
     const size_t es = E->esize;
     const size_t Mx = B * c.max_encoder_length;
     std::vector<std::pair<void**, size_t>> plan = {
         {&st->tx, B * d * es}, {&st->dx, B * d * es}, {&st->tin, B * d * es}, {&st->din, B * d * es},
-        {&st->fsum, B * d * es}, {&st->qb, B * in * es}, {&st->ao, B * in * es}, {&st->hb, B * ff * es},
+        {&st->fsum, B * d * es}, {&st->qb, B * in * es}, {&st->ao, B * in * es}, {&st->hb, B * ff * 4},
         {(void**)&st->logits, B * V * 4}, {(void**)&st->stage_f32, B * std::max(d, V) * 4},
         {&st->tk, c.num_temporal_layers * B * H * c.max_frames * 64 * es},
         {&st->tv, c.num_temporal_layers * B * H * c.max_frames * 64 * es},

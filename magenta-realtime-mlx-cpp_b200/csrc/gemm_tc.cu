@@ -40,7 +40,8 @@ constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3;
 constexpr int A_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_BYTES = BN * BK * 2;  // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /* 1024-byte alignment slack */ + 256 /* barriers */;
+constexpr int SMEM_PIPE = STAGES * STAGE_BYTES;  // pipeline buffers (then the epilogue tile)
+constexpr int SMEM = SMEM_PIPE + 1024 /* 1024-byte alignment slack */ + 256 /* barriers */;
 constexpr uint32_t TMEM_COLS = 128;
 // Epilogue tile in shared memory: 128 rows x (128 + 8) bf16 (16-byte row pad).
 constexpr int kTileLd = BN + 8;
@@ -97,16 +98,23 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 
 // ---- split-K over a thread-block cluster (few output tiles, long K) -------
 // CTA z of a cluster (z = blockIdx.z, cluster dims (1, 1, KSPLIT)) runs k-tiles
-// [z KT / KSPLIT, (z + 1) KT / KSPLIT) into its own TMEM accumulator, parks the
-// fp32 partial tile in its shared memory and, after a cluster barrier, sums
-// rows [z * 128 / KSPLIT, ...) of all KSPLIT partials in rank order through
-// distributed shared memory before running the epilogue on those rows.
+// [z KT / KSPLIT, (z + 1) KT / KSPLIT) into its own TMEM accumulator, pushes
+// each row of its fp32 partial tile into the receive region of the CTA that
+// owns that row (rows [z' * 128 / KSPLIT, ...) belong to CTA z') through
+// distributed shared memory and, after one cluster barrier, sums its rows
+// over the KSPLIT slots in rank order before running the epilogue on them.
 constexpr int kPartLd = BN + 4;                      // floats per partial-tile row
-constexpr int kPartBytes = BM * kPartLd * 4;         // 66 KB
-static_assert(kPartBytes + (BM / 2) * kTileLd * 2 <= STAGES * STAGE_BYTES,
-              "split-K partial tile + epilogue rows must fit the pipeline buffers");
+constexpr int kPartBytes = BM * kPartLd * 4;         // 66 KB receive region (split-K launches only)
+constexpr int SMEM_SPLIT = SMEM + kPartBytes;
+static_assert(BM * kTileLd * 2 <= SMEM_PIPE, "epilogue tile must fit the pipeline buffers");
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void st_cluster_f32x4(float* local, uint32_t rank, float a, float b, float c, float d) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(ra), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
 }
 __device__ __forceinline__ float4 ld_cluster_f32x4(const float* local, uint32_t rank) {
   uint32_t ra;
@@ -252,47 +260,45 @@ __global__ void __launch_bounds__(128, 1)
       }
     }
   } else {
-    // Split-K: park this CTA's fp32 partial tile, then reduce a row slice
-    // over the cluster in rank order.
-    float* part = reinterpret_cast<float*>(smem);
+    // Split-K: row r of this CTA's fp32 partial goes to CTA r / RS of the
+    // cluster (st.shared::cluster into slot [this rank] of its receive
+    // region, which the mainloop never touches, so no CTA waits for another
+    // to finish its k-tiles before pushing); after one cluster barrier each
+    // CTA sums its RS rows over the slots in rank order with local reads.
+    constexpr int RS = BM / KSPLIT;  // rows reduced by this CTA
+    float* recv = reinterpret_cast<float*>(smem + SMEM_PIPE + 256);  // after the barrier words
     if (ok) {
       const int r_local = warp * 32 + lane;
+      const uint32_t owner = (uint32_t)(r_local / RS);
+      float* slot_row = recv + ((size_t)kz * RS + (r_local % RS)) * kPartLd;  // same offset in the owner
       const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
         uint32_t r[16];
         tmem_ld16(lane_base + (uint32_t)c, r);
         tmem_wait_ld();
-        float4* dst = reinterpret_cast<float4*>(part + (size_t)r_local * kPartLd + c);
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-          dst[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
-                               __uint_as_float(r[4 * q + 3]));
+          st_cluster_f32x4(slot_row + c + 4 * q, owner, __uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                           __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
       }
     }
-    cluster_sync_all();  // every partial is in place (every CTA arrives, ok or not)
-    constexpr int RS = BM / KSPLIT;  // rows reduced by this CTA
+    cluster_sync_all();  // every pushed partial has landed (every CTA arrives, ok or not)
     r0 = kz * RS;
     r1 = r0 + RS;
-    stile = reinterpret_cast<T*>(smem + kPartBytes);
+    stile = reinterpret_cast<T*>(smem);  // this CTA's pipeline buffers are idle now
     if (ok) {
       // thread -> (row, 16-column group): RS rows x 8 groups over 128 threads
       for (int item = tid; item < RS * (BN / 16); item += 128) {
         const int rr = item / (BN / 16), c = (item - rr * (BN / 16)) * 16;
-        const float* src = part + (size_t)(r0 + rr) * kPartLd + c;
         float f[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 v = ld_cluster_f32x4(src + 4 * q, 0);
-          f[4 * q] = v.x; f[4 * q + 1] = v.y; f[4 * q + 2] = v.z; f[4 * q + 3] = v.w;
-        }
+        for (int q = 0; q < 16; ++q) f[q] = recv[(size_t)rr * kPartLd + c + q];
 #pragma unroll 1
         for (int z = 1; z < KSPLIT; ++z) {
+          const float* src = recv + ((size_t)z * RS + rr) * kPartLd + c;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float4 v = ld_cluster_f32x4(src + 4 * q, (uint32_t)z);
-            f[4 * q] += v.x; f[4 * q + 1] += v.y; f[4 * q + 2] += v.z; f[4 * q + 3] += v.w;
-          }
+          for (int q = 0; q < 16; ++q) f[q] += src[q];
         }
         tile_row_store<EPI>(stile + (size_t)rr * kTileLd, c, f);
       }
@@ -353,8 +359,6 @@ __global__ void __launch_bounds__(128, 1)
       }
     }
   }
-  // split-K: no CTA leaves while others may still read its partial tile
-  if constexpr (KSPLIT > 1) cluster_sync_all();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -397,7 +401,7 @@ cudaError_t launch_t(const CUtensorMap& a, const CUtensorMap& b, const GemmParam
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, KSPLIT);
   cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = SMEM;
+  cfg.dynamicSmemBytes = KSPLIT > 1 ? SMEM_SPLIT : SMEM;
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   int n = 0;
@@ -432,9 +436,7 @@ cudaError_t launch_split(const CUtensorMap& a, const CUtensorMap& b, const GemmP
 // Split-K factor: when the output tiles cannot fill the GPU (the decode
 // projections of a wide stream: 8-44 tiles), split K over a cluster of up
 // to max_ksplit CTAs while the grid stays within one wave and each CTA keeps
-// >= 2 k-tiles. (Measured on the 128-row decode: 655 ms per chunk with up
-// to 8-way splits against 608 ms without, so the engine leaves it off by
-// default; the rank-ordered DSMEM reduction is on the critical path.)
+// >= 2 k-tiles.
 int choose_ksplit(int tiles, int kt, int num_sms, int max_ksplit) {
   int k = 1;
   while (k < 8 && k < max_ksplit && tiles * k * 2 <= num_sms && kt >= 4 * k) k *= 2;
@@ -445,14 +447,14 @@ int choose_ksplit(int tiles, int kt, int num_sms, int max_ksplit) {
 
 template <int EPI>
 static void set_limits_epi(cudaError_t& e) {
-  auto set = [&](const void* f) {
-    cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM);
+  auto set = [&](const void* f, int bytes) {
+    cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (r != cudaSuccess) e = r;
   };
-  set((const void*)tc::gemm_tc_kernel<EPI, 1>);
-  set((const void*)tc::gemm_tc_kernel<EPI, 2>);
-  set((const void*)tc::gemm_tc_kernel<EPI, 4>);
-  set((const void*)tc::gemm_tc_kernel<EPI, 8>);
+  set((const void*)tc::gemm_tc_kernel<EPI, 1>, tc::SMEM);
+  set((const void*)tc::gemm_tc_kernel<EPI, 2>, tc::SMEM_SPLIT);
+  set((const void*)tc::gemm_tc_kernel<EPI, 4>, tc::SMEM_SPLIT);
+  set((const void*)tc::gemm_tc_kernel<EPI, 8>, tc::SMEM_SPLIT);
 }
 
 cudaError_t gemm_tc_set_smem_limits() {

@@ -300,7 +300,8 @@ def test_tcgen05_encoder_gemm(mrtdf, oracle, tiny_weights, hybrid_weights, name,
 def test_fused_self_attention_matches_separate_kernel(mrtdf, tiny_weights, name):
     """bf16 self-attention inside the q/k/v launch - per head in a thread-block
     cluster (default) or behind arrival tickets - has the separate kernel's
-    arithmetic: bit-identical logits and tokens."""
+    arithmetic: bit-identical logits and tokens. The same holds with the
+    FFN hidden rows passed as flag-carrying words (MRTDF_LL=1)."""
     cfg = mrtdf.preset(name, 1)
     frames = cfg.max_frames if name == "tiny" else 3
     seq = cfg.max_encoder_length if name == "tiny" else 256
@@ -310,10 +311,11 @@ def test_fused_self_attention_matches_separate_kernel(mrtdf, tiny_weights, name)
         return e.load_safetensors(tiny_weights) if name == "tiny" else e.load_random(0)
 
     outs = []
-    for cluster, tickets in (("1", "0"), ("0", "1"), ("0", "0")):
-        old = {k: os.environ.get(k) for k in ("MRTDF_CLUSTER_ATTN", "MRTDF_FUSE_ATTN")}
+    for cluster, tickets, ll in (("1", "0", "0"), ("0", "1", "0"), ("0", "0", "0"), ("1", "0", "1")):
+        old = {k: os.environ.get(k) for k in ("MRTDF_CLUSTER_ATTN", "MRTDF_FUSE_ATTN", "MRTDF_LL")}
         os.environ["MRTDF_CLUSTER_ATTN"] = cluster
         os.environ["MRTDF_FUSE_ATTN"] = tickets
+        os.environ["MRTDF_LL"] = ll
         try:
             eng = make()
         finally:
