@@ -156,6 +156,66 @@ __device__ __forceinline__ void tile_row_store(__nv_bfloat16* srow, int c, const
   }
 }
 
+// Phase 2 of the epilogue: 16-byte stores along output rows (8 columns per
+// chunk) for tile rows [r0, r1); the bf16 values of row r sit at stile row
+// r - r0. Threads thread_id of nthreads share the chunks.
+template <int EPI>
+__device__ __forceinline__ void epi_store_rows(const GemmParams& p, const __nv_bfloat16* stile, int bm, int bn, int r0,
+                                             int r1, int thread_id, int nthreads) {
+  typedef __nv_bfloat16 T;
+  constexpr int OC = (EPI == kEpiGeglu) ? BN / 2 : BN;  // output columns of the tile
+  constexpr int CPR = OC / 8;                          // 16-byte chunks per row
+  const int oc0 = (EPI == kEpiGeglu) ? bn / 2 : bn;
+  const int ncols = (EPI == kEpiGeglu) ? p.N / 2 : p.N;
+#pragma unroll 4
+  for (int idx = thread_id; idx < (r1 - r0) * CPR; idx += nthreads) {
+    const int rl = idx / CPR, ch = idx - rl * CPR;
+    const int m = bm + r0 + rl, n = oc0 + ch * 8;
+    if (m >= p.M || n >= ncols) continue;
+    uint4 v = *reinterpret_cast<const uint4*>(stile + (size_t)rl * kTileLd + ch * 8);
+    if (EPI == kEpiLogits) {
+      // bf16-rounded values as float; 8-byte stores (the level's column
+      // offset is only even)
+      float* o = reinterpret_cast<float*>(p.out) + (size_t)m * p.ldo + p.out_offset + n;
+      const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (n + 2 * i < ncols) reinterpret_cast<float2*>(o)[i] = __bfloat1622float2(v2[i]);  // N is only even
+    } else if (EPI == kEpiDecQKV) {
+      const int h = n / 192, rr = n - h * 192, sect = rr >> 6, cc = rr & 63;
+      T* dst = sect == 0 ? reinterpret_cast<T*>(p.out) + (size_t)m * p.ldo + h * 64 + cc
+                         : reinterpret_cast<T*>(sect == 1 ? p.ck : p.cv) +
+                               (((size_t)m * p.H + h) * p.cap + p.pos) * 64 + cc;
+      *reinterpret_cast<uint4*>(dst) = v;
+    } else if (EPI == kEpiCrossKV) {
+      const int two_inner = 2 * p.inner;
+      const int layer = n / two_inner, within = n - layer * two_inner;
+      const int kv = within / p.inner, rr = within - kv * p.inner;
+      const int h = rr >> 6, cc = rr & 63;
+      const int b = m / p.S, s = m - b * p.S;
+      T* cache = reinterpret_cast<T*>(kv == 0 ? p.ck : p.cv);
+      *reinterpret_cast<uint4*>(cache + ((((size_t)layer * p.B + b) * p.H + h) * p.Smax + s) * 64 + cc) = v;
+    } else {
+      T* o = reinterpret_cast<T*>(p.out) + (size_t)m * p.ldo + n;
+      if (EPI == kEpiResid || EPI == kEpiDecResid) {
+        const T* rsrc = EPI == kEpiResid ? o : reinterpret_cast<const T*>(p.resid) + (size_t)m * p.ldr + n;
+        const uint4 rv = *reinterpret_cast<const uint4*>(rsrc);
+        const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&rv);
+        const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 fa = __bfloat1622float2(a2[i]), fb = __bfloat1622float2(b2[i]);
+          const __nv_bfloat162 pr = __floats2bfloat162_rn(__fadd_rn(fa.x, fb.x), __fadd_rn(fa.y, fb.y));
+          w[i] = *reinterpret_cast<const uint32_t*>(&pr);
+        }
+        v = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      *reinterpret_cast<uint4*>(o) = v;
+    }
+  }
+}
+
 template <int EPI, int KSPLIT>
 __global__ void __launch_bounds__(128, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -305,60 +365,7 @@ __global__ void __launch_bounds__(128, 1)
     }
   }
   __syncthreads();
-  if (ok) {
-    // Phase 2: 16-byte stores along output rows (8 columns per chunk).
-    constexpr int OC = (EPI == kEpiGeglu) ? BN / 2 : BN;  // output columns of the tile
-    constexpr int CPR = OC / 8;                          // 16-byte chunks per row
-    const int oc0 = (EPI == kEpiGeglu) ? bn / 2 : bn;
-    const int ncols = (EPI == kEpiGeglu) ? p.N / 2 : p.N;
-#pragma unroll 4
-    for (int idx = tid; idx < (r1 - r0) * CPR; idx += 128) {
-      const int rl = idx / CPR, ch = idx - rl * CPR;
-      const int m = bm + r0 + rl, n = oc0 + ch * 8;
-      if (m >= p.M || n >= ncols) continue;
-      uint4 v = *reinterpret_cast<const uint4*>(stile + (size_t)rl * kTileLd + ch * 8);
-      if (EPI == kEpiLogits) {
-        // bf16-rounded values as float; 8-byte stores (the level's column
-        // offset is only even)
-        float* o = reinterpret_cast<float*>(p.out) + (size_t)m * p.ldo + p.out_offset + n;
-        const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if (n + 2 * i < ncols) reinterpret_cast<float2*>(o)[i] = __bfloat1622float2(v2[i]);  // N is only even
-      } else if (EPI == kEpiDecQKV) {
-        const int h = n / 192, rr = n - h * 192, sect = rr >> 6, cc = rr & 63;
-        T* dst = sect == 0 ? reinterpret_cast<T*>(p.out) + (size_t)m * p.ldo + h * 64 + cc
-                           : reinterpret_cast<T*>(sect == 1 ? p.ck : p.cv) +
-                                 (((size_t)m * p.H + h) * p.cap + p.pos) * 64 + cc;
-        *reinterpret_cast<uint4*>(dst) = v;
-      } else if (EPI == kEpiCrossKV) {
-        const int two_inner = 2 * p.inner;
-        const int layer = n / two_inner, within = n - layer * two_inner;
-        const int kv = within / p.inner, rr = within - kv * p.inner;
-        const int h = rr >> 6, cc = rr & 63;
-        const int b = m / p.S, s = m - b * p.S;
-        T* cache = reinterpret_cast<T*>(kv == 0 ? p.ck : p.cv);
-        *reinterpret_cast<uint4*>(cache + ((((size_t)layer * p.B + b) * p.H + h) * p.Smax + s) * 64 + cc) = v;
-      } else {
-        T* o = reinterpret_cast<T*>(p.out) + (size_t)m * p.ldo + n;
-        if (EPI == kEpiResid || EPI == kEpiDecResid) {
-          const T* rsrc = EPI == kEpiResid ? o : reinterpret_cast<const T*>(p.resid) + (size_t)m * p.ldr + n;
-          const uint4 rv = *reinterpret_cast<const uint4*>(rsrc);
-          const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&rv);
-          const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&v);
-          uint32_t w[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 fa = __bfloat1622float2(a2[i]), fb = __bfloat1622float2(b2[i]);
-            const __nv_bfloat162 pr = __floats2bfloat162_rn(__fadd_rn(fa.x, fb.x), __fadd_rn(fa.y, fb.y));
-            w[i] = *reinterpret_cast<const uint32_t*>(&pr);
-          }
-          v = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-        *reinterpret_cast<uint4*>(o) = v;
-      }
-    }
-  }
+  if (ok) epi_store_rows<EPI>(p, stile, bm, bn, r0, r1, tid, 128);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
