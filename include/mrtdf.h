@@ -273,6 +273,13 @@ int mrtdf_bench_encoder(mrtdf_engine* eng, int rows, int seq_len, int reps, floa
 int mrtdf_bench_depth(mrtdf_stream* st, const mrtdf_gen_opts* opts, int frames, int reps, float* us_per_step,
                       double* bytes_per_step, long long* launches_per_step);
 
+/*
+ * Measurement hook (no counterpart in the reference): kernel nodes of the
+ * CUDA graph of the chunk this stream ran last (every one is a kernel of this
+ * library), or -1 when that chunk ran as stream launches (MRTDF_GRAPH=0).
+ */
+long long mrtdf_stream_chunk_kernels(const mrtdf_stream* st);
+
 /* ---- streaming glue (System, system.cpp) ---------------------------------- */
 
 /*

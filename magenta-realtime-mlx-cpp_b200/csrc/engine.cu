@@ -158,6 +158,8 @@ struct mrtdf_stream {
   int t_len = 0, d_len = 0;
   bool have_temporal = false;
   std::map<GraphKey, cudaGraphExec_t> graphs;
+  std::map<GraphKey, long long> graph_kernels;  // kernel nodes of each chunk graph
+  long long last_chunk_kernels = 0;              // of the chunk run last (graph or stream launches)
   // measurement hook: when set, only the GEMV phases are enqueued and their
   // launches / algorithmic bytes are counted
   bool gemv_only = false;
@@ -704,6 +706,7 @@ void run_chunk(mrtdf_stream* st, int S, const mrtdf_gen_opts& o) {
                o.guidance_weight};
   const bool use_graph = env_flag("MRTDF_GRAPH", true);
   if (!use_graph) {
+    st->last_chunk_kernels = -1;  // counted only for graphs
     enqueue_chunk(st, S, o);
     return;
   }
@@ -719,12 +722,24 @@ void run_chunk(mrtdf_stream* st, int S, const mrtdf_gen_opts& o) {
       throw;
     }
     CUDA_OK(cudaStreamEndCapture(st->s, &g));
+    size_t n = 0;
+    long long kernels = 0;
+    if (cudaGraphGetNodes(g, nullptr, &n) == cudaSuccess && n) {
+      std::vector<cudaGraphNode_t> nodes(n);
+      if (cudaGraphGetNodes(g, nodes.data(), &n) == cudaSuccess)
+        for (size_t i = 0; i < n; ++i) {
+          cudaGraphNodeType t;
+          if (cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+        }
+    }
     cudaGraphExec_t ex = nullptr;
     const cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
     cudaGraphDestroy(g);
     check_cuda(e, "cudaGraphInstantiate");
     it = st->graphs.emplace(key, ex).first;
+    st->graph_kernels[key] = kernels;
   }
+  st->last_chunk_kernels = st->graph_kernels[key];
   CUDA_OK(cudaGraphLaunch(it->second, st->s));
 }
 
@@ -1454,5 +1469,8 @@ int mrtdf_bench_depth(mrtdf_stream* st, const mrtdf_gen_opts* o, int frames, int
     check_device_err(st);
   });
 }
+
+
+long long mrtdf_stream_chunk_kernels(const mrtdf_stream* st) { return st ? st->last_chunk_kernels : -1; }
 
 }  // extern "C"

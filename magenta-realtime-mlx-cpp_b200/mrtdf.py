@@ -38,7 +38,8 @@ EXPORTS = [
     "mrtdf_stream_rows", "mrtdf_encode", "mrtdf_temporal_step", "mrtdf_depth_step", "mrtdf_token_embedding",
     "mrtdf_sample", "mrtdf_sample_noalloc", "mrtdf_generate_tokens", "mrtdf_generate_tokens_dev",
     "mrtdf_teacher_forced_logits", "mrtdf_stream_sync", "mrtdf_stream_cuda", "mrtdf_bench_gemv",
-    "mrtdf_bench_encoder", "mrtdf_bench_depth", "mrtdf_generate_stream_dev", "mrtdf_build_encoder_inputs",
+    "mrtdf_bench_encoder", "mrtdf_bench_depth", "mrtdf_stream_chunk_kernels", "mrtdf_generate_stream_dev",
+    "mrtdf_build_encoder_inputs",
     "mrtdf_context_roll", "mrtdf_llm_to_rvq", "mrtdf_rvq_to_llm",
 ]
 
@@ -108,6 +109,8 @@ def lib() -> ctypes.CDLL:
                      "mrtdf_generate_tokens_dev", "mrtdf_teacher_forced_logits", "mrtdf_token_embedding",
                      "mrtdf_sample"]:
             getattr(L, name).restype = ctypes.c_int
+        L.mrtdf_stream_chunk_kernels.restype = ctypes.c_longlong
+        L.mrtdf_stream_chunk_kernels.argtypes = [ctypes.c_void_p]
         L.mrtdf_sample_noalloc.restype = ctypes.c_int
         L.mrtdf_sample_noalloc.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                            ctypes.POINTER(GenOpts), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
@@ -285,6 +288,10 @@ class Stream:
 
     def sync(self) -> None:
         _check(lib().mrtdf_stream_sync(self.h))
+
+    def chunk_kernels(self) -> int:
+        """Kernel nodes of the last chunk's CUDA graph (-1: no graph)."""
+        return int(lib().mrtdf_stream_chunk_kernels(self.h))
 
     def bench_depth(self, opts: GenOpts, frames: int, reps: int):
         """(us per depth step, algorithmic bytes per step, launches per step)

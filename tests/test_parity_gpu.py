@@ -470,3 +470,18 @@ def test_wide_stream_hybrid_matches_narrow(mrtdf):
         msg = (k, ew.mean(), en.mean(), ew.max(), en.max(), np.abs(w - n).max())
         assert ew.mean() <= 1.25 * en.mean() + 1e-3, msg
         assert ew.max() <= 1.25 * en.max() + 2e-2, msg
+
+
+def test_chunk_graph_kernel_count(mrtdf, tiny_weights):
+    """The chunk graph holds exactly the kernels the structure implies (the
+    bench's gpu_launches claim): encoder, PAD embedding, then per frame the
+    temporal layers and 16 x (depth layers + lm_head + sampler)."""
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+
+    cfg, eng = _engine(mrtdf, tiny_weights, "tiny", 1)
+    st = mrtdf.Stream(eng, 1, True)
+    ids = random_ids(cfg, 2, cfg.max_encoder_length, seed=80)
+    st.generate_tokens(ids, mrtdf.gen_opts(cfg, cfg.max_frames, seed=1))
+    assert st.chunk_kernels() == bench.st_launch_count(cfg, cfg.max_frames)
