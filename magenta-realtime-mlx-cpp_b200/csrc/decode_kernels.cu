@@ -1228,16 +1228,15 @@ __global__ void __launch_bounds__(128) attn_self_kernel(const AttnParams p) {
 
 // ---------------------------------------------------------------------------
 // Cross-attention for one new query over the cached encoder K/V: grid
-// (B*H, nsplit), 4 warps per CTA. Each CTA reduces its key slice to a
-// partial (max, sum, o[64]) in global scratch; the last CTA of a (row, head)
-// to arrive (atomic ticket) combines all slices and resets the ticket.
+// (B*H, nsplit), 4 warps per CTA, the nsplit CTAs of a (row, head) one
+// thread-block cluster. Each CTA reduces its key slice to a partial (max,
+// sum, o[64]) and stores it into rank 0's shared memory; rank 0 combines.
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(128) attn_cross_kernel(const AttnParams p) {
   pdl_wait();
   __shared__ float qs[4][64];
   __shared__ float wm[4], wl[4], wo[4][64];
-  __shared__ int is_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int bh = blockIdx.x, sp = blockIdx.y;
   const int b = bh / p.H, h = bh - b * p.H;
@@ -1301,7 +1300,7 @@ __global__ void __launch_bounds__(128) attn_cross_kernel(const AttnParams p) {
   wo[warp][2 * lane] = o0;
   wo[warp][2 * lane + 1] = o1;
   __syncthreads();
-  float* part = p.part + ((size_t)bh * p.nsplit + sp) * 66;
+  float part_m = -INFINITY, part_l = 0.f, part_o = 0.f;
   if (threadIdx.x < 64) {
     float M = -INFINITY;
     for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w]);
@@ -1312,33 +1311,34 @@ __global__ void __launch_bounds__(128) attn_cross_kernel(const AttnParams p) {
       L += wl[w] * f;
       O += wo[w][threadIdx.x] * f;
     }
-    part[2 + threadIdx.x] = O;
-    if (threadIdx.x == 0) {
-      part[0] = M;
-      part[1] = L;
-    }
+    part_m = M;
+    part_l = L;
+    part_o = O;
   }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) is_last = (atomicAdd(&p.counters[bh], 1) == p.nsplit - 1);
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
+  // The nsplit CTAs of this (row, head) are one thread-block cluster: each
+  // pushes its partial (max, sum, o[64]) into slot `sp` of rank 0, which
+  // combines the slots in split order after one cluster barrier.
+  __shared__ float slots[kCrossSplit][66];
   if (threadIdx.x < 64) {
-    const float* pb = p.part + (size_t)bh * p.nsplit * 66;
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < p.nsplit; ++s2) M = fmaxf(M, __ldcg(pb + (size_t)s2 * 66));
-    float L = 0.f, O = 0.f;
-    for (int s2 = 0; s2 < p.nsplit; ++s2) {
-      const float ms = __ldcg(pb + (size_t)s2 * 66);
-      if (ms == -INFINITY) continue;
-      const float f = expf(ms - M);
-      L += __ldcg(pb + (size_t)s2 * 66 + 1) * f;
-      O += __ldcg(pb + (size_t)s2 * 66 + 2 + threadIdx.x) * f;
+    st_cluster_f32(&slots[sp][2 + threadIdx.x], 0, part_o);
+    if (threadIdx.x == 0) {
+      st_cluster_f32(&slots[sp][0], 0, part_m);
+      st_cluster_f32(&slots[sp][1], 0, part_l);
     }
-    reinterpret_cast<T*>(p.out)[(size_t)b * p.inner + h * 64 + threadIdx.x] = from_f<T>(O / L);
   }
-  if (threadIdx.x == 0) p.counters[bh] = 0;
+  cluster_sync();
+  if (cluster_ctarank() != 0 || threadIdx.x >= 64) return;
+  float M = -INFINITY;
+  for (int s2 = 0; s2 < p.nsplit; ++s2) M = fmaxf(M, slots[s2][0]);
+  float L = 0.f, O = 0.f;
+  for (int s2 = 0; s2 < p.nsplit; ++s2) {
+    const float ms = slots[s2][0];
+    if (ms == -INFINITY) continue;
+    const float f = expf(ms - M);
+    L += slots[s2][1] * f;
+    O += slots[s2][2 + threadIdx.x] * f;
+  }
+  reinterpret_cast<T*>(p.out)[(size_t)b * p.inner + h * 64 + threadIdx.x] = from_f<T>(O / L);
 }
 
 template <typename P>
@@ -1365,9 +1365,22 @@ cudaError_t launch_attn_self(int dtype, const AttnParams& p, cudaStream_t s, boo
 }
 
 cudaError_t launch_attn_cross(int dtype, const AttnParams& p, cudaStream_t s, bool pdl) {
-  const dim3 grid(p.B * p.H, p.nsplit);
-  return dtype == 1 ? launch_k(attn_cross_kernel<__nv_bfloat16>, grid, dim3(128), 0, s, pdl, p)
-                    : launch_k(attn_cross_kernel<float>, grid, dim3(128), 0, s, pdl, p);
+  if (p.nsplit != kCrossSplit) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.B * p.H, p.nsplit);
+  cfg.blockDim = dim3(128);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = kCrossSplit;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return dtype == 1 ? cudaLaunchKernelEx(&cfg, attn_cross_kernel<__nv_bfloat16>, p)
+                    : cudaLaunchKernelEx(&cfg, attn_cross_kernel<float>, p);
 }
 
 // ---------------------------------------------------------------------------
