@@ -1419,16 +1419,51 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
   const int n = p.hi - p.lo;
   const int r0 = seq * p.rows_per_seq;
 
+  // The frame's running embedding sum does not depend on the token: its
+  // loads go out first, next to the logits loads (one round trip for both).
+  constexpr int EPC = Vec16<T>::N;
+  const int nchunk = p.d / EPC;
+  constexpr int kFsumRegs = 2;  // chunks per thread held in registers (d <= 2 x 256 x EPC)
+  uint4 fs_pre[2][kFsumRegs];
+  const bool fs_in_regs = !p.is_first && p.rows_per_seq <= 2 && nchunk <= kFsumRegs * kSampleThreads;
+  if (fs_in_regs) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int q = 0; q < kFsumRegs; ++q) {
+        const int ch = tid + q * kSampleThreads;
+        fs_pre[r][q] = (r < p.rows_per_seq && ch < nchunk)
+                           ? reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.fsum) +
+                                                            (size_t)(r0 + r) * p.d)[ch]
+                           : make_uint4(0, 0, 0, 0);
+      }
+  }
+
   int token;
   if (p.forced) {
     token = p.forced[seq];
   } else {
     const float* l0 = p.logits + (size_t)r0 * p.logits_stride + (p.lo - p.col_offset);
     const float* l1 = l0 + p.logits_stride;
-    for (int i = tid; i < n; i += kSampleThreads) {
-      float g = (p.rows_per_seq == 2) ? cfg_mix(l0[i], l1[i], p.w) : l0[i];
-      if (p.temperature != 0.0f) g = __fdiv_rn(g, p.temperature);
-      vals[i] = g;
+    // four strides of candidates per pass: all eight loads in flight at once
+    constexpr int U = 4;
+    for (int i0 = 0; i0 < n; i0 += U * kSampleThreads) {
+      float a[U], b[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * kSampleThreads + tid;
+        a[u] = i < n ? l0[i] : 0.f;
+        b[u] = (i < n && p.rows_per_seq == 2) ? l1[i] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * kSampleThreads + tid;
+        if (i < n) {
+          float g = (p.rows_per_seq == 2) ? cfg_mix(a[u], b[u], p.w) : a[u];
+          if (p.temperature != 0.0f) g = __fdiv_rn(g, p.temperature);
+          vals[i] = g;
+        }
+      }
     }
     if (tid == 0) {
       sel_prefix = 0u;
@@ -1532,10 +1567,8 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
   if (tid == 0 && p.tokens) p.tokens[(size_t)seq * p.tok_stride + p.tok_index] = token;
 
   // embedding feedback, 16 bytes per thread per row
-  constexpr int EPC = Vec16<T>::N;
   const uint4* e = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.emb) + (size_t)token * p.d);
-  const int nchunk = p.d / EPC;
-  for (int ch = tid; ch < nchunk; ch += kSampleThreads) {
+  for (int ch = tid, q_reg = 0; ch < nchunk; ch += kSampleThreads, ++q_reg) {
     const uint4 ev = e[ch];
     float ef[EPC];
     Vec16<T>::unpack(ev, ef);
@@ -1544,12 +1577,30 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
       *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.din) + off) = ev;
       T* fs = reinterpret_cast<T*>(p.fsum) + off;
       T* tin = reinterpret_cast<T*>(p.tin) + off;
+      float prev[EPC];
+      if (!p.is_first) {
+        if (fs_in_regs) {
+          uint4 pv = make_uint4(0, 0, 0, 0);
+#pragma unroll
+          for (int qq = 0; qq < kFsumRegs; ++qq)
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr)
+              if (qq == q_reg && rr == r) pv = fs_pre[rr][qq];
+          Vec16<T>::unpack(pv, prev);
+        } else {
+#pragma unroll
+          for (int q = 0; q < EPC; ++q) prev[q] = to_f(fs[q]);
+        }
+      }
+      T outv[EPC];
 #pragma unroll
       for (int q = 0; q < EPC; ++q) {
-        const float sum = p.is_first ? ef[q] : rnd<T>(__fadd_rn(to_f(fs[q]), ef[q]));
-        fs[q] = from_f<T>(sum);
+        const float sum = p.is_first ? ef[q] : rnd<T>(__fadd_rn(prev[q], ef[q]));
+        outv[q] = from_f<T>(sum);
         if (p.is_last) tin[q] = from_f<T>(__fdiv_rn(sum, (float)p.depth));
       }
+#pragma unroll
+      for (int q = 0; q < EPC; ++q) fs[q] = outv[q];
     }
   }
 }

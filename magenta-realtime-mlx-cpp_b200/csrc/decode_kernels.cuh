@@ -80,12 +80,10 @@ struct AttnParams {
   const float* bias;  // (H, bias_stride) for this query position, or null
   int bias_stride;
   void* out;        // (B, inner)
-  float* part;      // split-K partials (B*H, nsplit, 66), cross attention only
-  int* counters;    // (B*H), zero between launches
   int* err;
   int B, H, cap, T;  // T = number of valid keys
   int inner;
-  int nsplit;
+  int nsplit;  // cross attention: key slices = CTAs of one cluster (kCrossSplit)
 };
 cudaError_t launch_attn_self(int dtype, const AttnParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_attn_cross(int dtype, const AttnParams& p, cudaStream_t s, bool pdl);

@@ -140,8 +140,6 @@ struct mrtdf_stream {
   int32_t* tokens;  // (nseq, Tmax, depth)
   uint64_t* seeds;  // (nseq)
   int32_t* forced;  // (nseq)
-  float* part;
-  int* counters;
   int* head_cnt;  // (H) arrival counters of the fused q/k/v + attention kernel
   // flag-carrying FFN hidden rows (hb as (bf16 pair, flag) words): the
   // FFN-down launch polls them instead of waiting for the FFN-up launch
@@ -480,8 +478,8 @@ void enqueue_decoder_layer(mrtdf_stream* st, const DecLayerDev& L, const void* x
     gemv(st, kGemvStore, true, p);
     // 5. cross attention over the cached encoder K/V
     AttnParams ca{};
-    ca.q = st->qb; ca.K = ck; ca.V = cv; ca.bias = nullptr; ca.out = st->ao; ca.part = st->part;
-    ca.counters = st->counters; ca.err = st->err; ca.B = st->B; ca.H = c.num_heads; ca.cap = c.max_encoder_length;
+    ca.q = st->qb; ca.K = ck; ca.V = cv; ca.bias = nullptr; ca.out = st->ao;
+    ca.err = st->err; ca.B = st->B; ca.H = c.num_heads; ca.cap = c.max_encoder_length;
     ca.T = st->S; ca.inner = in; ca.nsplit = kCrossSplit;
     if (!st->gemv_only) check_cuda(launch_attn_cross(c.dtype, ca, st->s, E->pdl), "attn_cross launch");
     // 6. cross o_proj + residual
@@ -890,7 +888,6 @@ int mrtdf_stream_create(mrtdf_engine* E, int num_sequences, int cfg, mrtdf_strea
         {&st->eh, Mx * ff * es}, {(void**)&st->ids, Mx * 4}, {&st->xn, B * d * es},
         {(void**)&st->tokens, (size_t)num_sequences * c.max_frames * c.rvq_depth * 4},
         {(void**)&st->seeds, (size_t)num_sequences * 8}, {(void**)&st->forced, (size_t)num_sequences * 4},
-        {(void**)&st->part, B * H * kCrossSplit * 66 * 4}, {(void**)&st->counters, B * H * 4},
         {(void**)&st->head_cnt, H * 4},
         {(void**)&st->err, 64}};
     size_t total = 0;
