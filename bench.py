@@ -119,6 +119,13 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU baseline (oracle port of the reference's eager path)
 # ---------------------------------------------------------------------------
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
 def cpu_sample(frames: int = 2):
     """Time the oracle on the encoder + `frames` frames of the same workload;
     returns (tokens/s extrapolated to a 50-frame chunk, ms per chunk, threads)."""
@@ -126,6 +133,7 @@ def cpu_sample(frames: int = 2):
     import mrtdf
     import oracle_py
 
+    oracle_py.set_num_threads(host_cores())
     cfg = mrtdf.preset("hybrid", mrtdf.DTYPE_BF16)
     with tempfile.TemporaryDirectory() as td:
         path = os.path.join(td, "w.safetensors")
@@ -213,6 +221,8 @@ def run_reference(args):
     import mrtdf
     import oracle_py
 
+    # every host core (torchrun sets OMP_NUM_THREADS=1 per rank; rank 0 runs alone)
+    oracle_py.set_num_threads(host_cores())
     cfg = mrtdf.preset("hybrid", mrtdf.DTYPE_BF16)
     with tempfile.TemporaryDirectory() as td:
         path = os.path.join(td, "w.safetensors")
