@@ -14,8 +14,10 @@
 //                  freed pipeline shared memory (GEGLU applied here), then
 //                  16-byte stores along output rows with the fused epilogue
 //                  (store / residual add / cross-K/V scatter).
-// No cluster, no multicast. Every mbarrier wait is bounded and reports a
-// timeout in the stream's error word; TMEM is always released.
+// No multicast anywhere. Launches with few output tiles may split K over a
+// thread-block cluster (see the split-K section below: partial tiles move
+// through st.shared::cluster stores only). Every mbarrier wait is bounded and
+// reports a timeout in the stream's error word; TMEM is always released.
 //
 // Descriptor formats follow the sm_100 UMMA definitions (CUTLASS
 // cute/arch/mma_sm100_desc.hpp): shared-memory descriptor = start >> 4,
@@ -115,16 +117,6 @@ __device__ __forceinline__ void st_cluster_f32x4(float* local, uint32_t rank, fl
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
   asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(ra), "f"(a), "f"(b), "f"(c), "f"(d)
                : "memory");
-}
-__device__ __forceinline__ float4 ld_cluster_f32x4(const float* local, uint32_t rank) {
-  uint32_t ra;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(ra)
-               : "memory");
-  return v;
 }
 
 // 16 fp32 accumulator columns [c, c + 16) of one tile row -> bf16 tile row
