@@ -398,7 +398,6 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
   float* cl_recv = reinterpret_cast<float*>(cl_ext + kClusterOffAttF);
   __shared__ float wred[8][BMAX];
   __shared__ float rstd[BMAX];
-  __shared__ int ok_flag;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, c = blockIdx.x;
@@ -423,7 +422,6 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
   if (tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
-    ok_flag = 1;
   }
   __syncthreads();
   if (warp == 0 && R > 0) {
@@ -616,12 +614,12 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
   const int g = lane >> 2, t = lane & 3;
   const bool gval = g < p.B;
   const uint32_t xrow = smem_u32(xsm) + (uint32_t)(g * L.rstride) + (uint32_t)(4 * t);
-  if (tid == 0 && R > 0) ok_flag = mbar_wait_bounded(bar, 0, p.err);
-  __syncthreads();
-  // (a timed-out weight copy is already reported in the error word; the
-  // cluster variant carries on with whatever shared memory holds so that
-  // every CTA reaches the cluster barriers; it always has rows)
-  if (MODE != kGemvQKVCluster && (!ok_flag || R == 0)) return;
+  // Every thread waits for the weight rows itself, so no CTA barrier follows.
+  // A timed-out copy is reported in the error word and the CTA carries on
+  // with whatever shared memory holds (control flow stays uniform; the
+  // cluster variant must reach its cluster barrier anyway).
+  if (R > 0) mbar_wait_bounded(bar, 0, p.err);
+  if (MODE != kGemvQKVCluster && R == 0) return;
   float acc[NT][4];
 #pragma unroll
   for (int i = 0; i < NT; ++i)
