@@ -764,9 +764,11 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
     // b < B runs attn_self_kernel's arithmetic for (b, h) with its cached
     // keys / values. No CTA reads another's shared memory after the barrier,
     // so the others may exit.
-    cluster_sync();
+    // each thread's cached-key copies have landed; the cluster barrier
+    // (release / acquire, all threads of all CTAs) then publishes them and
+    // the pushed q/k/v rows to the attending warp
     asm volatile("cp.async.wait_all;" ::: "memory");
-    __syncthreads();
+    cluster_sync();
     const int crank = (int)cluster_ctarank(), h = c / kQkvCluster;
     if (crank < p.B && warp == 0) {
       const int b = crank, nkeys = p.pos + 1;
