@@ -447,6 +447,13 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
   uint4 xin[BMAX][2];
   bool ll_in = false;
   if constexpr (BMAX <= 4) ll_in = p.x_flag != 0;
+  // RMSNorm without a CTA-wide reduction (B <= 2, cols <= 1024, a multiple
+  // of 256): every warp also loads the whole rows (L1 hits after the first
+  // warp) and reduces the sum of squares with shuffles alone.
+  constexpr int kWJ = 4;  // row chunks per lane
+  constexpr int kWB = (NORM && BMAX <= 2) ? BMAX : 1;
+  uint4 wx[kWB][kWJ];
+  const bool wnorm = NORM && BMAX <= 2 && !ll_in && (nchunk & 31) == 0 && nchunk <= 32 * kWJ;
   if (!ll_in) {
     pdl_wait();
 #pragma unroll
@@ -457,6 +464,19 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
         xin[b][i] = (b < p.B && ch < nchunk) ? *reinterpret_cast<const uint4*>(x_ptr + (size_t)b * p.x_stride + ch * 8)
                                             : make_uint4(0, 0, 0, 0);
       }
+    if constexpr (NORM && BMAX <= 2) {
+      if (wnorm) {
+#pragma unroll
+        for (int b = 0; b < kWB; ++b)
+#pragma unroll
+          for (int j = 0; j < kWJ; ++j) {
+            const int ch = lane + 32 * j;
+            wx[b][j] = (b < p.B && ch < nchunk)
+                           ? *reinterpret_cast<const uint4*>(x_ptr + (size_t)b * p.x_stride + ch * 8)
+                           : make_uint4(0, 0, 0, 0);
+          }
+      }
+    }
   } else if constexpr (BMAX <= 4) {
     // Poll the previous launch's flag-carrying words: chunk ch (8 values) is
     // four 8-byte words = two 16-byte loads; every load is retried until all
@@ -536,7 +556,43 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
   }
 
   // ---- inputs -> shared memory as bf16 (RMS-normalised when NORM) --------
-  if (NORM) {
+  bool staged = false;
+  if constexpr (NORM && BMAX <= 2) {
+    if (wnorm) {
+#pragma unroll
+      for (int b = 0; b < kWB; ++b) {
+        if (b < p.B) {
+          float ssw = 0.f;
+#pragma unroll
+          for (int j = 0; j < kWJ; ++j) {
+            float f[8];
+            Vec16<T>::unpack(wx[b][j], f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ssw = fmaf(f[e], f[e], ssw);
+          }
+          ssw = warp_sum(ssw);
+          const float r = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(ssw, (float)p.cols), 1e-6f)));
+          const int ch = tid;  // nchunk <= 128: one chunk per thread, xin[b][0]
+          if (ch < nchunk) {
+            float f[8], w[8];
+            Vec16<T>::unpack(xin[b][0], f);
+            Vec16<T>::unpack(nw_reg[0], w);
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float a0 = rnd<T>(__fmul_rn(w[2 * e], rnd<T>(__fmul_rn(f[2 * e], r))));
+              const float a1 = rnd<T>(__fmul_rn(w[2 * e + 1], rnd<T>(__fmul_rn(f[2 * e + 1], r))));
+              const __nv_bfloat162 pr = __floats2bfloat162_rn(a0, a1);
+              o[e] = *reinterpret_cast<const uint32_t*>(&pr);
+            }
+            *reinterpret_cast<uint4*>(xsm + (size_t)b * L.rstride + ch * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        }
+      }
+      staged = true;
+    }
+  }
+  if (NORM && !staged) {
     float ss[BMAX];
 #pragma unroll
     for (int b = 0; b < BMAX; ++b) {
@@ -584,7 +640,7 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
         }
       }
     }
-  } else {
+  } else if (!NORM) {
 #pragma unroll
     for (int b = 0; b < BMAX; ++b)
 #pragma unroll
