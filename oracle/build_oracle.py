@@ -1,6 +1,7 @@
 """Build recipe for the CPU oracle (test infrastructure only).
 
-Compiles oracle/*.cpp into oracle/_build/liboracle.so with g++. The
+Compiles the Depthformer and SpectroStream oracles (oracle/*.cpp) into
+oracle/_build/liboracle.so with g++. The
 exact-arithmetic translation unit (bf16 rounding, Philox, Gumbel, CFG mix)
 is built with -ffp-contract=off so no multiply-add is fused; the model code
 may fuse. -march=x86-64-v3 keeps the binary runnable on any AVX2 host, so it
@@ -19,8 +20,8 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(BUILD, "liboracle.so")
-SOURCES = ["depthformer_oracle.cpp", "oracle_exact.cpp"]
-HEADERS = ["oracle.h"]
+SOURCES = ["depthformer_oracle.cpp", "oracle_exact.cpp", "spectrostream_oracle.cpp"]
+HEADERS = ["oracle.h", "safetensors_reader.h"]
 
 
 def _stale() -> bool:

@@ -56,6 +56,19 @@ def lib() -> ctypes.CDLL:
         L.orc_gelu.restype = ctypes.c_float
         L.orc_gelu.argtypes = [ctypes.c_float, ctypes.c_int]
         L.orc_set_num_threads.argtypes = [ctypes.c_int]
+        # SpectroStream decode phase (spectrostream_oracle.cpp)
+        P, I = ctypes.c_void_p, ctypes.c_int
+        L.orc_ss_last_error.restype = ctypes.c_char_p
+        L.orc_ss_create.restype = P
+        L.orc_ss_create.argtypes = [ctypes.c_char_p, ctypes.c_char_p]
+        L.orc_ss_destroy.argtypes = [P]
+        L.orc_ss_dequantize.argtypes = [P, P, I, I, P]
+        L.orc_ss_decode.argtypes = [P, P, I, I, P]
+        L.orc_ss_istft.argtypes = [P, I, I, I, P]
+        L.orc_ss_decode_tokens.argtypes = [P, P, I, I, P]
+        L.orc_ss_conv2d.argtypes = [P, I, I, I, I, P, P, I, I, I, I, I, I, P]
+        L.orc_ss_conv_transpose2d.argtypes = [P, I, I, I, I, P, P, I, I, I, I, I, P]
+        L.orc_ss_set_num_threads.argtypes = [I]
         _lib = L
     return _lib
 
@@ -193,3 +206,95 @@ def set_num_threads(n: int):
 
 def num_threads() -> int:
     return lib().orc_num_threads()
+
+
+# ---------------------------------------------------------------------------
+# SpectroStream decode phase (oracle/spectrostream_oracle.cpp)
+# ---------------------------------------------------------------------------
+def _ss_check(rc: int):
+    if rc != 0:
+        raise RuntimeError("oracle: " + lib().orc_ss_last_error().decode())
+
+
+class CodecOracle:
+    """CPU restatement (float32) of rvq_dequantization, SpectroStreamDecoder
+    and istft_postprocess."""
+
+    def __init__(self, decoder_path: str, codebooks_path: str):
+        h = lib().orc_ss_create(decoder_path.encode(), codebooks_path.encode())
+        if not h:
+            raise RuntimeError("oracle: " + lib().orc_ss_last_error().decode())
+        self.h = h
+
+    def rvq_dequantize(self, codes: np.ndarray) -> np.ndarray:
+        codes = np.ascontiguousarray(codes, dtype=np.int32)
+        out = np.empty((codes.shape[0], 256), np.float32)
+        _ss_check(lib().orc_ss_dequantize(self.h, codes.ctypes.data, codes.shape[0], codes.shape[1], out.ctypes.data))
+        return out
+
+    def decode(self, emb: np.ndarray) -> np.ndarray:
+        emb = np.ascontiguousarray(emb, dtype=np.float32)
+        B, S, _ = emb.shape
+        out = np.empty((B, 4 * S, 480, 4), np.float32)
+        _ss_check(lib().orc_ss_decode(self.h, emb.ctypes.data, B, S, out.ctypes.data))
+        return out
+
+    def decode_tokens(self, codes: np.ndarray) -> np.ndarray:
+        codes = np.ascontiguousarray(codes, dtype=np.int32)
+        S, levels = codes.shape
+        out = np.empty((S * 1920, 2), np.float32)
+        _ss_check(lib().orc_ss_decode_tokens(self.h, codes.ctypes.data, S, levels, out.ctypes.data))
+        return out
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().orc_ss_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def istft(spec: np.ndarray, target_length: int) -> np.ndarray:
+    spec = np.ascontiguousarray(spec, dtype=np.float32)
+    B, frames = spec.shape[:2]
+    out = np.empty((B, target_length, 2), np.float32)
+    _ss_check(lib().orc_ss_istft(spec.ctypes.data, B, frames, target_length, out.ctypes.data))
+    return out
+
+
+def conv2d(x: np.ndarray, w: np.ndarray, b: np.ndarray, stride=(1, 1), causal_pad: bool = False) -> np.ndarray:
+    """NHWC x, canonical weight (O, I, kh, kw)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    N, H, W, C = x.shape
+    O, I, kh, kw = w.shape
+    sh, sw = stride
+    if causal_pad:
+        ow = -(-W // sw)
+        tot = max((ow - 1) * sw + kw - W, 0)
+        Hp, Wp = H + kh - sh, W + tot
+    else:
+        Hp, Wp = H, W
+    out = np.empty((N, (Hp - kh) // sh + 1, (Wp - kw) // sw + 1, O), np.float32)
+    _ss_check(lib().orc_ss_conv2d(x.ctypes.data, N, H, W, C, w.ctypes.data, b.ctypes.data, O, kh, kw, sh, sw,
+                                  int(causal_pad), out.ctypes.data))
+    return out
+
+
+def conv_transpose2d(x: np.ndarray, w: np.ndarray, b: np.ndarray, stride=(1, 1)) -> np.ndarray:
+    """NHWC x, canonical weight (I, O, kh, kw)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    N, H, W, C = x.shape
+    I, O, kh, kw = w.shape
+    sh, sw = stride
+    out = np.empty((N, (H - 1) * sh + kh, (W - 1) * sw + kw, O), np.float32)
+    _ss_check(lib().orc_ss_conv_transpose2d(x.ctypes.data, N, H, W, C, w.ctypes.data, b.ctypes.data, O, kh, kw, sh,
+                                            sw, out.ctypes.data))
+    return out

@@ -13,18 +13,27 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def _declared_symbols():
-    text = open(os.path.join(ROOT, "include", "mrtdf.h")).read()
-    return sorted(set(re.findall(r"\b(mrtdf_[a-z0-9_]+)\s*\(", text)))
+def _declared_symbols(header="mrtdf.h", prefix="mrtdf_"):
+    text = open(os.path.join(ROOT, "include", header)).read()
+    return sorted(set(re.findall(r"\b(" + prefix + r"[a-z0-9_]+)\s*\(", text)))
 
 
 def test_library_exports_every_declared_symbol(mrtdf):
+    import mrtss
+
     lib = mrtdf.lib()
     declared = _declared_symbols()
     assert len(declared) >= 20
     missing = [s for s in declared if not hasattr(lib, s)]
     assert not missing, missing
     assert sorted(mrtdf.EXPORTS) == sorted(declared)
+    # the SpectroStream decode phase (include/mrtss.h) lives in the same library
+    codec = _declared_symbols("mrtss.h", "mrtss_")
+    assert len(codec) >= 10
+    missing = [s for s in codec if not hasattr(lib, s)]
+    assert not missing, missing
+    assert sorted(mrtss.EXPORTS) == sorted(codec)
+    assert sorted(os.listdir(os.path.join(ROOT, "include"))) == ["mrtdf.h", "mrtss.h"]
 
 
 def test_version(mrtdf):
