@@ -23,6 +23,10 @@ and 16 depth steps + sampling per frame = 800 RVQ tokens.
   Depthformer, all host threads) on a bounded sample: the encoder pass and
   two frames, extrapolated to a 50-frame chunk.
 
+* codec_decode (rank 0): the next stage of a chunk, the SpectroStream decode
+  phase (RVQ codes -> decoder -> iSTFT -> 48 kHz stereo) on the tensor cores;
+  `--codec-only` prints just this leg.
+
 Multi-GPU (torchrun, one process per GPU): independent replicas, one stream
 per GPU with seed offset by rank, no collective on the data path
 (scaling = weak); the barrier and the max-over-ranks reduction use
@@ -349,6 +353,8 @@ def run_ours(args):
             line["encoder_microbench"] = encoder_microbench(eng, peaks)
             line["depth_microbench"] = depth_microbench(mrtdf, cfg, st)
         line["multi_stream"] = multi_stream(mrtdf, torch, eng, cfg, device, rank, world, dist)
+        if rank == 0:
+            line["codec_decode"] = codec_decode(torch, peaks, device, local, cpu=world == 1 and not args.no_cpu_baseline)
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.timed_only:
         tps, ms_cpu, cores, t_enc, t_frame = cpu_sample(2)
         line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port",
@@ -440,6 +446,96 @@ def depth_microbench(mrtdf, cfg, st) -> dict:
             "launches_per_step": n, "us_per_launch": us / n}
 
 
+# SpectroStream decoder blocks (spectrostream.cpp:328-338): in, out, stride, transposed kernel
+CODEC_BLOCKS = [(512, 1024, (2, 1), (4, 3)), (512, 256, (2, 2), (4, 4)), (256, 256, (1, 2), (3, 4)),
+                (256, 256, (1, 2), (3, 4)), (256, 128, (1, 3), (3, 6)), (128, 128, (1, 2), (3, 4)),
+                (128, 64, (1, 2), (3, 4))]
+
+
+def codec_flops(S: int, B: int = 1):
+    """Multiply-adds x 2 of the decoder's tensor-core convolutions at (B, S)
+    (every tap of every kept output, padding taps included, as the GEMMs
+    compute them) and of the SIMT 7x7 output convolution."""
+    Hs = S + 1
+    tc = 2 * B * Hs * (256 * 2560 * 2 + 2560 * 2560)          # input_proj 1x1 convs
+    tc += 2 * 2 * B * Hs * 5 * 9 * 512 * 512                   # input_conv
+    n, h, w = B, Hs, 5
+    for cin, cout, (sh, sw), (kh, kw) in CODEC_BLOCKS:
+        if cin != cout:
+            tc += 2 * n * h * w * cin * cout                   # shortcut at the input resolution
+        cws = (kw - sw) // 2
+        for ry in range(sh):
+            for rx in range(sw):
+                taps = -(-(kh - ry) // sh) * -(-(kw - rx) // sw)
+                q0 = -((rx - cws) // sw)
+                wq = (w * sw - 1 + cws - rx) // sw - q0 + 1
+                tc += 2 * n * h * wq * taps * cin * cout       # transposed-conv phase
+        h, w = h * sh, w * sw
+        tc += 2 * n * h * w * 9 * cout * cout                  # post conv
+        if cout == 1024:
+            n *= 2                                             # stereo split
+    simt = 2 * n * (h - 4) * w * 49 * 64 * 2
+    return tc, simt
+
+
+def codec_decode(torch, peaks: dict, device, local: int, cpu: bool, S: int = 51, reps: int = 20) -> dict:
+    """Codec decode phase of one chunk (system.cpp:372-390): 51 codec frames
+    (50 + 1 crossfade) x 16 RVQ levels -> 97,920 stereo samples at 48 kHz.
+    Random-init decoder and codebooks (seed 11), codes uniform (seed 12).
+    Device-resident codes, one CUDA graph per call, CUDA events on the
+    codec's stream (ms); e2e through the host API (codes in, audio out);
+    tensor-core roofline against the measured bf16 peak / 2 (dense tf32
+    runs at half the bf16 rate). The CPU baseline is the float32 oracle
+    (all host threads) on the same chunk."""
+    import mrtss
+
+    codec = mrtss.Codec(max_batch=1, max_frames=S, device=local).load_random(11, 16)
+    codes = np.random.default_rng(12).integers(0, 1024, size=(1, S, 16), dtype=np.int32)
+    dcodes = torch.from_numpy(codes).to(device)
+    daudio = torch.empty((1, S * 1920, 2), dtype=torch.float32, device=device)
+    ext = torch.cuda.ExternalStream(codec.cuda_stream(), device=device)
+    for _ in range(3):
+        codec.decode_tokens_dev(dcodes.data_ptr(), 1, S, 16, daudio.data_ptr())
+    codec.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    for _ in range(reps):
+        codec.decode_tokens_dev(dcodes.data_ptr(), 1, S, 16, daudio.data_ptr())
+    e1.record(ext)
+    codec.sync()
+    ms = e0.elapsed_time(e1) / reps
+    t0 = time.perf_counter()
+    for _ in range(5):
+        codec.decode_tokens(codes[0])
+    ms_e2e = (time.perf_counter() - t0) * 1e3 / 5
+    tc, simt = codec_flops(S)
+    bf16 = peaks.get("bf16_tflops")
+    peak = (bf16 if bf16 else 1590.0) / 2
+    seconds = S * 1920 / 48000.0
+    out = {"frames": S, "levels": 16, "ms": ms, "rtf": seconds * 1e3 / ms, "samples_per_s": S * 1920 / (ms / 1e3),
+           "e2e_ms": ms_e2e, "kernels": codec.decode_kernels(1, S),
+           "roofline": {"bound": "tensor", "achieved": tc / (ms / 1e3) / 1e12, "peak": peak, "unit": "TFLOP/s",
+                        "frac": tc / (ms / 1e3) / 1e12 / peak, "tensor_gflop": tc / 1e9, "simt_gflop": simt / 1e9,
+                        "peak_source": ("measured" if bf16 else "fallback") + " bf16 / 2 (tf32)"}}
+    codec.close()
+    if cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle_py
+
+        oracle_py.set_num_threads(host_cores())
+        with tempfile.TemporaryDirectory() as td:
+            dec, cb = os.path.join(td, "d.safetensors"), os.path.join(td, "c.safetensors")
+            mrtss.write_random_safetensors(11, 16, dec, cb)
+            orc = oracle_py.CodecOracle(dec, cb)
+        t0 = time.perf_counter()
+        orc.decode_tokens(codes[0])
+        ms_cpu = (time.perf_counter() - t0) * 1e3
+        orc.close()
+        out["cpu_baseline"] = {"ms": ms_cpu, "cores": oracle_py.num_threads(), "kind": "port",
+                               "sample": f"one full chunk ({S} frames) through the float32 oracle"}
+    return out
+
+
 def multi_stream(mrtdf, torch, eng, cfg, device, rank: int, world: int, dist, n_streams: int = 64,
                  per_group: int = 64, rounds: int = 2) -> dict:
     """64 independent CFG streams per GPU (bf16, top-k 40,
@@ -506,6 +602,23 @@ def st_launch_count(cfg, frames: int = 50) -> int:
     return enc + 1 + frames * (temporal + cfg.rvq_depth * depth)
 
 
+def run_codec_only(args) -> int:
+    import torch
+
+    _, _, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    peaks = {}
+    if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")):
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    out = codec_decode(torch, peaks, device, local, cpu=not args.no_cpu_baseline)
+    print(json.dumps({"metric": "SpectroStream decode phase, ms per 2.04 s chunk (51 frames x 16 levels)",
+                      "value": out["ms"], "unit": "ms", "higher_is_better": False, "n_gpus": 1, "dtype": "f32/tf32",
+                      "data": "synthetic (random-init decoder and codebooks seed 11, codes seed 12)",
+                      "codec_decode": out}), flush=True)
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -516,7 +629,11 @@ def main(argv=None):
     ap.add_argument("--no-suite", action="store_true", help="skip the config 3-5 measurements")
     ap.add_argument("--timed-only", action="store_true",
                     help="only the timed chunks (for an ncu launch list): no e2e, roofline, suite or CPU legs")
+    ap.add_argument("--codec-only", action="store_true",
+                    help="only the SpectroStream decode-phase leg (one GPU), as its own JSON line")
     args = ap.parse_args(argv)
+    if args.codec_only:
+        return run_codec_only(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

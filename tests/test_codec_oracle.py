@@ -6,7 +6,6 @@ stft_preprocess), RVQ dequantisation, and the whole decoder at a small
 number of frames. No GPU needed."""
 from __future__ import annotations
 
-
 import numpy as np
 import pytest
 
