@@ -156,6 +156,7 @@ struct Plan {
   bool pdl = true;
   long long kernels = 0;
   size_t need_act = 0;
+  int nseq = 1;  // sequences in the call: the split-K choice uses one sequence's tiles
 
   void fail(cudaError_t e, const char* what) {
     if (e != cudaSuccess) throw Error{MRTDF_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e)};
@@ -189,6 +190,7 @@ struct Plan {
     p.resid = resid; p.rh = 1; p.rw = npx; p.rsy = 1; p.rsx = 1;
     p.osy = 1; p.osx = 1; p.ory = 0; p.orx = 0; p.ho = 1; p.wo = npx; p.split = 0;
     p.out_raw = out_raw; p.out_elu = out_elu;
+    p.split_tiles = (npx / nseq + 127) / 128;
     run(p);
   }
 
@@ -208,6 +210,7 @@ struct Plan {
     p.resid = resid; p.rh = rh; p.rw = rw; p.rsy = rsy; p.rsx = rsx;
     p.osy = 1; p.osx = 1; p.ory = 0; p.orx = 0; p.ho = in.h; p.wo = in.w; p.split = split;
     p.out_raw = out_raw; p.out_elu = out_elu;
+    p.split_tiles = p.tiles_x * p.tiles_y * (in.n / nseq);
     run(p);
   }
 
@@ -230,11 +233,13 @@ struct Plan {
     p.resid = nullptr; p.rh = 0; p.rw = 0; p.rsy = 1; p.rsx = 1;
     p.osy = s.sh; p.osx = s.sw; p.ory = ry; p.orx = rx - cws; p.ho = in.h * s.sh; p.wo = in.w * s.sw; p.split = 0;
     p.out_raw = out; p.out_elu = nullptr;
+    p.split_tiles = p.tiles_x * p.tiles_y * (in.n / nseq);
     run(p);
   }
 
   // decoder from x0 (B, S + 1, 1, 256) to spec (B, 4 S, 480, 4)
   void decoder(int B, int S) {
+    nseq = B;
     const int Hs = S + 1, M0 = B * Hs;
     // input_proj: Res1x1Block 256 -> 2560 -> 2560, no pre-ELU (spectrostream.cpp:174-181)
     conv1x1(c->x0, M0, c->ip_sc, nullptr, 0, c->r, nullptr);
@@ -290,9 +295,10 @@ struct Plan {
   }
 
   void istft(int B, int frames, int target, const float* spec, float* audio) {
-    ++kernels;
+    kernels += 2;
+    need_act = std::max(need_act, (size_t)B * 2 * frames * kFft);  // windowed frames in the y buffer
     if (launch) {
-      IstftParams q{spec, c->synth, c->cosv, audio, B, frames, target};
+      IstftParams q{spec, c->synth, c->cosv, audio, c->y, B, frames, target};
       fail(launch_istft(q, c->s, pdl), "istft");
     }
   }
@@ -645,7 +651,8 @@ int mrtss_istft(mrtss_codec* c, const float* spec, int B, int frames, int target
     if (!c || !spec || !audio) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
     if (B <= 0 || frames <= 0 || target <= 0 || target > (frames + 1) * kHop)
       throw Error{MRTDF_ERR_INVALID, "need B, frames > 0 and 0 < target <= (frames + 1) * 480"};
-    if ((size_t)B * frames * MRTSS_STFT_BINS * 4 > c->spec_floats || (size_t)B * target * 2 > c->audio_floats)
+    if ((size_t)B * frames * MRTSS_STFT_BINS * 4 > c->spec_floats || (size_t)B * target * 2 > c->audio_floats ||
+        (size_t)B * 2 * frames * kFft > c->act_floats)
       throw Error{MRTDF_ERR_RANGE, "spectrogram or audio exceeds the codec's capacity"};
     if (!c->synth) throw Error{MRTDF_ERR_STATE, "load the codec's weights first"};
     SS_CUDA(cudaSetDevice(c->device));

@@ -25,6 +25,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "codec_kernels.cuh"
@@ -101,7 +102,86 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 // elu with alpha 1 (nn_ops.h:31-39)
 __device__ __forceinline__ float elu1(float v) { return v > 0.f ? v : expf(v) - 1.0f; }
 
+// ---- split-K over a thread-block cluster --------------------------------------
+// Layers with few output tiles and long K (the decoder's first layers: 12-140
+// CTAs, up to 144 k-tiles) split K over a cluster of KSPLIT CTAs (grid z,
+// cluster dims (1, 1, KSPLIT)): CTA z runs k-tiles [z KT / KSPLIT, (z + 1) KT /
+// KSPLIT) into its own TMEM accumulator, pushes every row of its fp32 partial
+// tile into the receive region of the CTA that owns the row (rows
+// [z' 128 / KSPLIT, ...) belong to CTA z') with st.shared::cluster, and after
+// one cluster barrier each CTA sums its rows over the slots in rank order
+// (deterministic) and runs the epilogue on them. The receive region lies past
+// the pipeline buffers, so no CTA waits for another's mainloop to push.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void st_cluster_f32x4(float* local, uint32_t rank, float a, float b, float c, float d) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(ra), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
 template <int BN>
+constexpr int part_ld() { return BN + 4; }  // floats per partial-tile row in the receive region
+template <int BN>
+constexpr int smem_split() { return Cfg<BN>::SMEM + BM * part_ld<BN>() * 4; }
+
+// Epilogue of one accumulator row r, output channels [n, n + 16): the row's
+// output position, then bias, ELU, residual, stores (raw and / or ELU'd,
+// the stereo split folded into the address). Rows outside the tile's valid
+// positions or the output image are skipped.
+__device__ __forceinline__ void epi16(const ConvParams& p, int img, int qy0, int qx0, int r, int n, float* f) {
+  const int ly = r / p.wt, lx = r - ly * p.wt;
+  const int qy = qy0 + ly, qx = qx0 + lx;
+  const int oy = qy * p.osy + p.ory, ox = qx * p.osx + p.orx;
+  if (!(r < p.wt * p.ht && qy < p.q0y + p.hq && qx < p.q0x + p.wq && oy >= 0 && oy < p.ho && ox >= 0 &&
+        ox < p.wo))
+    return;
+#pragma unroll
+  for (int q = 0; q < 16; q += 4) {
+    const float4 b4 = *reinterpret_cast<const float4*>(p.bias + n + q);
+    f[q] += b4.x;
+    f[q + 1] += b4.y;
+    f[q + 2] += b4.z;
+    f[q + 3] += b4.w;
+  }
+  if (p.elu_acc) {
+#pragma unroll
+    for (int q = 0; q < 16; ++q) f[q] = elu1(f[q]);
+  }
+  if (p.resid) {
+    const float* rp = p.resid + (((size_t)img * p.rh + oy / p.rsy) * p.rw + ox / p.rsx) * p.cout + n;
+#pragma unroll
+    for (int q = 0; q < 16; q += 4) {
+      const float4 r4 = *reinterpret_cast<const float4*>(rp + q);
+      f[q] += r4.x;
+      f[q + 1] += r4.y;
+      f[q + 2] += r4.z;
+      f[q + 3] += r4.w;
+    }
+  }
+  int oimg = img, oc = p.cout, nn = n;
+  if (p.split > 0) {
+    oimg = (n / p.split) * p.n_img + img;
+    nn = n - (n / p.split) * p.split;
+    oc = p.split;
+  }
+  const size_t off = (((size_t)oimg * p.ho + oy) * p.wo + ox) * oc + nn;
+  if (p.out_raw) {
+    float4* dst = reinterpret_cast<float4*>(p.out_raw + off);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) dst[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+  }
+  if (p.out_elu) {
+    float4* dst = reinterpret_cast<float4*>(p.out_elu + off);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      dst[q] = make_float4(elu1(f[4 * q]), elu1(f[4 * q + 1]), elu1(f[4 * q + 2]), elu1(f[4 * q + 3]));
+  }
+}
+
+template <int BN, int KSPLIT>
 __global__ void __launch_bounds__(128, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const ConvParams p, int* err) {
@@ -123,7 +203,10 @@ __global__ void __launch_bounds__(128, 1)
   const int qy0 = p.q0y + tile_y * p.ht, qx0 = p.q0x + tile_x * p.wt;
   const int bn = blockIdx.y * BN;
   const int kc = p.cin / BK;  // k-tiles per tap
-  const int KT = p.ntaps * kc;
+  const int KT_all = p.ntaps * kc;
+  const int kz = KSPLIT > 1 ? (int)blockIdx.z : 0;
+  const int kt0 = kz * KT_all / KSPLIT, kt1 = (kz + 1) * KT_all / KSPLIT;
+  const int KT = kt1 - kt0;
   const uint32_t tx_bytes = (uint32_t)(BK * 4 * p.wt * p.ht + C::B_BYTES);
 
   if (warp == 0) {
@@ -151,12 +234,13 @@ __global__ void __launch_bounds__(128, 1)
 
   if (warp == 0 && lane == 0) {
     // ---- TMA producer ----
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % STAGES, round = kt / STAGES;
+    for (int i = 0; i < KT; ++i) {
+      const int s = i % STAGES, round = i / STAGES;
       if (round > 0 && !mbar_wait_bounded(&empty[s], (uint32_t)((round - 1) & 1), err)) {
         abort_flag = 1;
         break;
       }
+      const int kt = kt0 + i;
       const int tap = kt / kc, c0 = (kt - tap * kc) * BK;
       const int ty = tap / p.ntx, tx = tap - ty * p.ntx;
       uint8_t* sa = smem + s * C::STAGE;
@@ -166,8 +250,8 @@ __global__ void __launch_bounds__(128, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer ----
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % STAGES, round = kt / STAGES;
+    for (int i = 0; i < KT; ++i) {
+      const int s = i % STAGES, round = i / STAGES;
       if (!mbar_wait_bounded(&full[s], (uint32_t)(round & 1), err)) {
         abort_flag = 1;
         break;
@@ -177,7 +261,7 @@ __global__ void __launch_bounds__(128, 1)
       const uint32_t sb = sa + A_BYTES;
 #pragma unroll
       for (int j = 0; j < BK / 8; ++j)  // K 8 per instruction = 32 bytes along the swizzled row
-        mma_tf32(tmem, smem_desc_sw128(sa + j * 32), smem_desc_sw128(sb + j * 32), C::IDESC, (kt | j) != 0);
+        mma_tf32(tmem, smem_desc_sw128(sa + j * 32), smem_desc_sw128(sb + j * 32), C::IDESC, (i | j) != 0);
       mma_commit(&empty[s]);
     }
     mma_commit(done);
@@ -186,63 +270,67 @@ __global__ void __launch_bounds__(128, 1)
   // the TMEM loads below are .sync.aligned: decide CTA-uniformly
   const bool ok = __syncthreads_and(mbar_wait_bounded(done, 0, err) ? 1 : 0) && !abort_flag;
   tc_fence_after();
-  if (ok) {
-    // accumulator row r (TMEM lane) = tile position (r / wt, r % wt)
-    const int r = warp * 32 + lane;
-    const int ly = r / p.wt, lx = r - ly * p.wt;
-    const int qy = qy0 + ly, qx = qx0 + lx;
-    const int oy = qy * p.osy + p.ory, ox = qx * p.osx + p.orx;
-    const bool valid = r < p.wt * p.ht && qy < p.q0y + p.hq && qx < p.q0x + p.wq && oy >= 0 && oy < p.ho &&
-                       ox >= 0 && ox < p.wo;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+  const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+  if constexpr (KSPLIT == 1) {
+    if (ok) {
+      // accumulator row r (TMEM lane) = tile position (r / wt, r % wt)
+      const int r = warp * 32 + lane;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      uint32_t v[16];
-      tmem_ld16(lane_base + (uint32_t)c, v);
-      tmem_wait_ld();
-      if (!valid) continue;
-      const int n = bn + c;
-      float f[16];
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(lane_base + (uint32_t)c, v);
+        tmem_wait_ld();
+        float f[16];
 #pragma unroll
-      for (int q = 0; q < 16; q += 4) {
-        const float4 b4 = *reinterpret_cast<const float4*>(p.bias + n + q);
-        f[q] = __uint_as_float(v[q]) + b4.x;
-        f[q + 1] = __uint_as_float(v[q + 1]) + b4.y;
-        f[q + 2] = __uint_as_float(v[q + 2]) + b4.z;
-        f[q + 3] = __uint_as_float(v[q + 3]) + b4.w;
+        for (int q = 0; q < 16; ++q) f[q] = __uint_as_float(v[q]);
+        epi16(p, img, qy0, qx0, r, bn + c, f);
       }
-      if (p.elu_acc) {
-#pragma unroll
-        for (int q = 0; q < 16; ++q) f[q] = elu1(f[q]);
-      }
-      if (p.resid) {
-        const float* rp = p.resid + (((size_t)img * p.rh + oy / p.rsy) * p.rw + ox / p.rsx) * p.cout + n;
-#pragma unroll
-        for (int q = 0; q < 16; q += 4) {
-          const float4 r4 = *reinterpret_cast<const float4*>(rp + q);
-          f[q] += r4.x;
-          f[q + 1] += r4.y;
-          f[q + 2] += r4.z;
-          f[q + 3] += r4.w;
-        }
-      }
-      int oimg = img, oc = p.cout, nn = n;
-      if (p.split > 0) {
-        oimg = (n / p.split) * p.n_img + img;
-        nn = n - (n / p.split) * p.split;
-        oc = p.split;
-      }
-      const size_t off = (((size_t)oimg * p.ho + oy) * p.wo + ox) * oc + nn;
-      if (p.out_raw) {
-        float4* dst = reinterpret_cast<float4*>(p.out_raw + off);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) dst[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
-      }
-      if (p.out_elu) {
-        float4* dst = reinterpret_cast<float4*>(p.out_elu + off);
+    }
+  } else {
+    constexpr int RS = BM / KSPLIT;  // rows reduced by this CTA
+    constexpr int LD = part_ld<BN>();
+    float* recv = reinterpret_cast<float*>(smem + STAGES * C::STAGE + 256);  // past the barrier words
+    if (ok) {
+      const int r = warp * 32 + lane;
+      const uint32_t owner = (uint32_t)(r / RS);
+      float* slot_row = recv + ((size_t)kz * RS + (r % RS)) * LD;  // the same offset in the owner
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(lane_base + (uint32_t)c, v);
+        tmem_wait_ld();
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-          dst[q] = make_float4(elu1(f[4 * q]), elu1(f[4 * q + 1]), elu1(f[4 * q + 2]), elu1(f[4 * q + 3]));
+          st_cluster_f32x4(slot_row + c + 4 * q, owner, __uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                           __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+      }
+    }
+    cluster_sync_all();  // every pushed partial has landed (every CTA arrives, ok or not)
+    if (ok) {
+      for (int item = tid; item < RS * (BN / 16); item += 128) {
+        const int rr = item / (BN / 16), c = (item - rr * (BN / 16)) * 16;
+        float f[16];
+#pragma unroll
+        for (int q = 0; q < 16; q += 4) {
+          const float4 a = *reinterpret_cast<const float4*>(recv + (size_t)rr * LD + c + q);
+          f[q] = a.x;
+          f[q + 1] = a.y;
+          f[q + 2] = a.z;
+          f[q + 3] = a.w;
+        }
+#pragma unroll 1
+        for (int z = 1; z < KSPLIT; ++z) {
+          const float* src = recv + ((size_t)z * RS + rr) * LD + c;
+#pragma unroll
+          for (int q = 0; q < 16; q += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(src + q);
+            f[q] += a.x;
+            f[q + 1] += a.y;
+            f[q + 2] += a.z;
+            f[q + 3] += a.w;
+          }
+        }
+        epi16(p, img, qy0, qx0, kz * RS + rr, bn + c, f);
       }
     }
   }
@@ -296,17 +384,23 @@ bool make_map_wgt(CUtensorMap* m, const ConvParams& p, int bn) {
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN>
-cudaError_t launch_bn(const ConvParams& p, int* err, cudaStream_t s, bool pdl) {
-  CUtensorMap a, b;
-  if (!make_map_act(&a, p) || !make_map_wgt(&b, p, BN)) return cudaErrorInvalidValue;
+template <int BN, int KSPLIT>
+cudaError_t launch_bn(const CUtensorMap& a, const CUtensorMap& b, const ConvParams& p, int* err, cudaStream_t s,
+                      bool pdl) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(p.tiles_x * p.tiles_y * p.n_img), (unsigned)(p.cout / BN), 1);
+  cfg.gridDim = dim3((unsigned)(p.tiles_x * p.tiles_y * p.n_img), (unsigned)(p.cout / BN), KSPLIT);
   cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = Cfg<BN>::SMEM;
+  cfg.dynamicSmemBytes = KSPLIT > 1 ? smem_split<BN>() : Cfg<BN>::SMEM;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   int n = 0;
+  if (KSPLIT > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = KSPLIT;
+    ++n;
+  }
   if (pdl) {
     attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[n].val.programmaticStreamSerializationAllowed = 1;
@@ -314,7 +408,29 @@ cudaError_t launch_bn(const ConvParams& p, int* err, cudaStream_t s, bool pdl) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  return cudaLaunchKernelEx(&cfg, conv_tc_kernel<BN>, a, b, p, err);
+  return cudaLaunchKernelEx(&cfg, conv_tc_kernel<BN, KSPLIT>, a, b, p, err);
+}
+
+template <int BN>
+cudaError_t launch_split(const ConvParams& p, int ks, int* err, cudaStream_t s, bool pdl) {
+  CUtensorMap a, b;
+  if (!make_map_act(&a, p) || !make_map_wgt(&b, p, BN)) return cudaErrorInvalidValue;
+  switch (ks) {
+    case 2: return launch_bn<BN, 2>(a, b, p, err, s, pdl);
+    case 4: return launch_bn<BN, 4>(a, b, p, err, s, pdl);
+    case 8: return launch_bn<BN, 8>(a, b, p, err, s, pdl);
+    default: return launch_bn<BN, 1>(a, b, p, err, s, pdl);
+  }
+}
+
+// Split-K factor from the layer's tile count for ONE sequence (split_tiles),
+// so the summation order, and with it every output bit, does not depend on
+// how many sequences share the launch: double while the split grid of one
+// sequence stays within half the SMs and each CTA keeps >= 4 k-tiles.
+int choose_ksplit(int split_tiles, int kt, int num_sms) {
+  int k = 1;
+  while (k < 8 && split_tiles * k * 2 <= num_sms && kt >= 4 * k) k *= 2;
+  return k;
 }
 
 // ---- output convolution 7x7, 64 -> 2 (SIMT) --------------------------------
@@ -405,52 +521,85 @@ __global__ void __launch_bounds__(256) out_conv_kernel(const OutConvParams p) {
 }
 
 // ---- iSTFT: irfft (n 960) + synthesis window + overlap-add -----------------
-// Block (hop i, stereo s, batch b) writes samples [480 i, 480 (i + 1)) of
-// channel s: frame i at n = j plus frame i - 1 at n = j + 480. Each frame
-// sample is the real inverse DFT of its 480 bins and a zero Nyquist bin,
+// istft_frames_kernel: block (frame pair, stereo s, batch b) computes the
+// windowed time samples of two consecutive frames, every thread four sample
+// indices n, so each twiddle pair read serves two frames. A frame sample is
+// the real inverse DFT of its 480 bins and a zero Nyquist bin,
 // x[n] = (X_0.re + 2 sum_{k=1}^{479} (X_k.re cos(2 pi k n / 960) -
 // X_k.im sin(2 pi k n / 960))) / 960, with the twiddle index k n mod 960
 // stepped incrementally and sin read from the cosine table shifted by 720.
-constexpr int kFft = 960, kHop = 480;
+// istft_ola_kernel: the overlap-add (frame i at j plus frame i - 1 at
+// j + 480), the trim to `target` and the stereo interleave.
+constexpr int kFft = 960, kHop = 480, kFramesPerBlock = 2;
 
-__device__ __forceinline__ float irfft_sample(const float2* X, const float* cs, int n) {
-  float acc = 0.f;
-  int m = 0;
-#pragma unroll 4
-  for (int k = 1; k < kHop; ++k) {
-    m += n;
-    if (m >= kFft) m -= kFft;
-    int ms = m + 720;
-    if (ms >= kFft) ms -= kFft;
-    acc = fmaf(X[k].x, cs[m], acc);
-    acc = fmaf(-X[k].y, cs[ms], acc);
-  }
-  return (X[0].x + 2.0f * acc) / (float)kFft;
-}
-
-__global__ void __launch_bounds__(256) istft_kernel(const IstftParams p) {
+__global__ void __launch_bounds__(256) istft_frames_kernel(const IstftParams p) {
   __shared__ float cs[kFft];
-  __shared__ float2 Xa[kHop], Xb[kHop];
-  const int i = blockIdx.x, s = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  __shared__ float2 X[kFramesPerBlock][kHop];
+  const int f0 = blockIdx.x * kFramesPerBlock, s = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
   for (int m = tid; m < kFft; m += 256) cs[m] = p.cosv[m];
   pdl_wait();
-  for (int k = tid; k < kHop; k += 256) {
-    float2 a = make_float2(0.f, 0.f), c = make_float2(0.f, 0.f);
-    if (i < p.frames) a = *reinterpret_cast<const float2*>(p.spec + (((size_t)b * p.frames + i) * kHop + k) * 4 + 2 * s);
-    if (i >= 1)
-      c = *reinterpret_cast<const float2*>(p.spec + (((size_t)b * p.frames + i - 1) * kHop + k) * 4 + 2 * s);
-    Xa[k] = a;
-    Xb[k] = c;
+  for (int i = tid; i < kFramesPerBlock * kHop; i += 256) {
+    const int f = i / kHop, k = i - f * kHop;
+    float2 v = make_float2(0.f, 0.f);
+    if (f0 + f < p.frames)
+      v = *reinterpret_cast<const float2*>(p.spec + (((size_t)b * p.frames + f0 + f) * kHop + k) * 4 + 2 * s);
+    X[f][k] = v;
   }
   __syncthreads();
-  for (int j = tid; j < kHop; j += 256) {
-    const int t = i * kHop + j;
-    if (t >= p.target) continue;
-    float v = 0.f;
-    if (i < p.frames) v = irfft_sample(Xa, cs, j) * p.synth[j];
-    if (i >= 1) v += irfft_sample(Xb, cs, j + kHop) * p.synth[j + kHop];
-    p.audio[((size_t)b * p.target + t) * 2 + s] = v;
+  const bool four = tid + 768 < kFft;  // warps 0-5 take four sample indices, warps 6-7 three
+  float acc[4][kFramesPerBlock];
+  int m[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    m[j] = 0;
+#pragma unroll
+    for (int f = 0; f < kFramesPerBlock; ++f) acc[j][f] = 0.f;
   }
+#pragma unroll 2
+  for (int k = 1; k < kHop; ++k) {
+    float2 x[kFramesPerBlock];
+#pragma unroll
+    for (int f = 0; f < kFramesPerBlock; ++f) x[f] = X[f][k];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (j == 3 && !four) break;
+      m[j] += tid + 256 * j;
+      if (m[j] >= kFft) m[j] -= kFft;
+      int ms = m[j] + 720;
+      if (ms >= kFft) ms -= kFft;
+      const float c = cs[m[j]], sn = cs[ms];
+#pragma unroll
+      for (int f = 0; f < kFramesPerBlock; ++f) {
+        acc[j][f] = fmaf(x[f].x, c, acc[j][f]);
+        acc[j][f] = fmaf(-x[f].y, sn, acc[j][f]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int n = tid + 256 * j;
+    if (n >= kFft) break;
+#pragma unroll
+    for (int f = 0; f < kFramesPerBlock; ++f)
+      if (f0 + f < p.frames)
+        p.frames_buf[(((size_t)b * 2 + s) * p.frames + f0 + f) * kFft + n] =
+            ((X[f][0].x + 2.0f * acc[j][f]) / (float)kFft) * p.synth[n];
+  }
+}
+
+__global__ void __launch_bounds__(256) istft_ola_kernel(const IstftParams p) {
+  const size_t idx = (size_t)blockIdx.x * 256 + threadIdx.x;  // (b, t, s) of the interleaved output
+  pdl_wait();
+  if (idx >= (size_t)p.B * p.target * 2) return;
+  const int s = (int)(idx & 1);
+  const size_t bt = idx >> 1;
+  const int b = (int)(bt / p.target), t = (int)(bt - (size_t)b * p.target);
+  const int i = t / kHop, j = t - i * kHop;
+  const float* fr = p.frames_buf + ((size_t)b * 2 + s) * p.frames * kFft;
+  float v = 0.f;
+  if (i < p.frames) v = fr[(size_t)i * kFft + j];
+  if (i >= 1) v += fr[(size_t)(i - 1) * kFft + j + kHop];
+  p.audio[idx] = v;
 }
 
 // ---- RVQ dequantisation ------------------------------------------------------
@@ -496,12 +645,21 @@ cudaError_t launch_simple(K kernel, dim3 grid, dim3 block, size_t smem, const P&
 
 }  // namespace cv
 
+template <int BN>
+static void conv_limits(cudaError_t& e) {
+  auto set = [&](const void* f, int bytes) {
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  };
+  set((const void*)cv::conv_tc_kernel<BN, 1>, cv::Cfg<BN>::SMEM);
+  set((const void*)cv::conv_tc_kernel<BN, 2>, cv::smem_split<BN>());
+  set((const void*)cv::conv_tc_kernel<BN, 4>, cv::smem_split<BN>());
+  set((const void*)cv::conv_tc_kernel<BN, 8>, cv::smem_split<BN>());
+}
+
 cudaError_t conv_tc_set_smem_limits() {
-  cudaError_t e = cudaFuncSetAttribute(cv::conv_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       cv::Cfg<64>::SMEM);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(cv::conv_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             cv::Cfg<128>::SMEM);
+  cudaError_t e = cudaSuccess;
+  conv_limits<64>(e);
+  conv_limits<128>(e);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(cv::out_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, cv::kOcSmem);
   return e;
@@ -520,8 +678,12 @@ cudaError_t launch_conv_tc(const ConvParams& p, int* err, cudaStream_t s, bool p
   if (mis(p.in) || mis(p.wgt) || mis(p.bias) || (p.resid && mis(p.resid)) || (p.out_raw && mis(p.out_raw)) ||
       (p.out_elu && mis(p.out_elu)))
     return cudaErrorInvalidValue;
-  if (p.cout % 128 == 0) return cv::launch_bn<128>(p, err, s, pdl);
-  return cv::launch_bn<64>(p, err, s, pdl);
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int bn = p.cout % 128 == 0 ? 128 : 64;
+  const int ks = cv::choose_ksplit(std::max(1, p.split_tiles) * (p.cout / bn), p.ntaps * (p.cin / cv::BK), sms);
+  if (bn == 128) return cv::launch_split<128>(p, ks, err, s, pdl);
+  return cv::launch_split<64>(p, ks, err, s, pdl);
 }
 
 cudaError_t launch_out_conv(const OutConvParams& p, cudaStream_t s, bool pdl) {
@@ -531,9 +693,13 @@ cudaError_t launch_out_conv(const OutConvParams& p, cudaStream_t s, bool pdl) {
 }
 
 cudaError_t launch_istft(const IstftParams& p, cudaStream_t s, bool pdl) {
-  if (p.B <= 0 || p.frames <= 0 || p.target <= 0 || p.target > (p.frames + 1) * cv::kHop) return cudaErrorInvalidValue;
-  const dim3 grid((p.target + cv::kHop - 1) / cv::kHop, 2, p.B);
-  return cv::launch_simple(cv::istft_kernel, grid, dim3(256), 0, p, s, pdl);
+  if (p.B <= 0 || p.frames <= 0 || p.target <= 0 || p.target > (p.frames + 1) * cv::kHop || !p.frames_buf)
+    return cudaErrorInvalidValue;
+  const dim3 grid((p.frames + cv::kFramesPerBlock - 1) / cv::kFramesPerBlock, 2, p.B);
+  cudaError_t e = cv::launch_simple(cv::istft_frames_kernel, grid, dim3(256), 0, p, s, pdl);
+  if (e != cudaSuccess) return e;
+  const size_t n = (size_t)p.B * p.target * 2;
+  return cv::launch_simple(cv::istft_ola_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, p, s, pdl);
 }
 
 cudaError_t launch_dequant(const DequantParams& p, cudaStream_t s, bool pdl) {

@@ -38,6 +38,9 @@ struct ConvParams {
   int osy, osx, ory, orx, ho, wo, split;
   float* out_raw;
   float* out_elu;
+  // M tiles of this layer for ONE sequence: the split-K factor derives from
+  // it, so results do not depend on the batch size (0 = the grid's tiles)
+  int split_tiles;
 };
 
 // Output convolution 7x7 (64 -> 2, causal padding) fused with the temporal
@@ -56,6 +59,7 @@ struct IstftParams {
   const float* synth;  // (960) synthesis window
   const float* cosv;   // (960) cos(2 pi m / 960)
   float* audio;        // (B, target, 2)
+  float* frames_buf;   // scratch (B, 2, frames, 960): windowed frames
   int B, frames, target;
 };
 
@@ -71,6 +75,7 @@ constexpr int kConvBK = 32;  // fp32 elements per 128-byte operand row
 cudaError_t launch_conv_tc(const ConvParams& p, int* err, cudaStream_t s, bool pdl);
 cudaError_t conv_tc_set_smem_limits();
 cudaError_t launch_out_conv(const OutConvParams& p, cudaStream_t s, bool pdl);
+// two launches: windowed frames, then overlap-add
 cudaError_t launch_istft(const IstftParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_dequant(const DequantParams& p, cudaStream_t s, bool pdl);
 
