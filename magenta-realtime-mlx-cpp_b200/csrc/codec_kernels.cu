@@ -15,7 +15,7 @@
 //                  tiled load of the input (box 32 channels x wt x ht
 //                  positions, 128-byte swizzle; out-of-range coordinates
 //                  read zero, which is the convolution's padding) and one
-//                  2-D load of the weight tile, into a 4-stage ring;
+//                  2-D load of the weight tile, into a 3- or 4-stage ring;
 //   warp 1 lane 0  MMA issuer: 4 x tcgen05.mma kind::tf32 (M 128, N BN,
 //                  K 8) per stage into a BN-column TMEM accumulator;
 //   all 4 warps    epilogue: tcgen05.ld of the thread's accumulator row,
@@ -36,14 +36,20 @@ namespace mrtdf {
 
 namespace cv {
 
-constexpr int BM = 128, BK = kConvBK, STAGES = 4;
+constexpr int BM = 128, BK = kConvBK;
 constexpr int A_BYTES = BM * BK * 4;  // 16 KB, 1024-byte multiple (swizzle atoms)
 
-template <int BN>
+// Unsplit launches use a 3-stage ring (96 KB at BN 128), so two CTAs share an
+// SM and one CTA's epilogue overlaps the other's mainloop; split-K launches
+// keep 4 stages (their receive region leaves room for one CTA per SM).
+template <int BN, int KSPLIT>
 struct Cfg {
+  static constexpr int STAGES = KSPLIT > 1 ? 4 : 3;
   static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int SMEM = STAGES * STAGE + 1024 /* alignment slack */ + 256 /* barriers */;
+  static constexpr int PART_LD = BN + 4;  // floats per partial-tile row in the split-K receive region
+  static constexpr int SMEM = STAGES * STAGE + 1024 /* alignment slack */ + 256 /* barriers */ +
+                              (KSPLIT > 1 ? BM * PART_LD * 4 : 0);
   // instruction descriptor: D f32 (bit 4), A / B tf32 (format 2 at bits 7 /
   // 10), both K-major, N >> 3 at bit 17, M >> 4 at bit 24
   static constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
@@ -122,10 +128,6 @@ __device__ __forceinline__ void st_cluster_f32x4(float* local, uint32_t rank, fl
                : "memory");
 }
 
-template <int BN>
-constexpr int part_ld() { return BN + 4; }  // floats per partial-tile row in the receive region
-template <int BN>
-constexpr int smem_split() { return Cfg<BN>::SMEM + BM * part_ld<BN>() * 4; }
 
 // Epilogue of one accumulator row r, output channels [n, n + 16): the row's
 // output position, then bias, ELU, residual, stores (raw and / or ELU'd,
@@ -182,10 +184,11 @@ __device__ __forceinline__ void epi16(const ConvParams& p, int img, int qy0, int
 }
 
 template <int BN, int KSPLIT>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(128, KSPLIT > 1 ? 1 : 2)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const ConvParams p, int* err) {
-  typedef Cfg<BN> C;
+  typedef Cfg<BN, KSPLIT> C;
+  constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t cv_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(cv_smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE);
@@ -288,7 +291,7 @@ __global__ void __launch_bounds__(128, 1)
     }
   } else {
     constexpr int RS = BM / KSPLIT;  // rows reduced by this CTA
-    constexpr int LD = part_ld<BN>();
+    constexpr int LD = C::PART_LD;
     float* recv = reinterpret_cast<float*>(smem + STAGES * C::STAGE + 256);  // past the barrier words
     if (ok) {
       const int r = warp * 32 + lane;
@@ -390,7 +393,7 @@ cudaError_t launch_bn(const CUtensorMap& a, const CUtensorMap& b, const ConvPara
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(p.tiles_x * p.tiles_y * p.n_img), (unsigned)(p.cout / BN), KSPLIT);
   cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = KSPLIT > 1 ? smem_split<BN>() : Cfg<BN>::SMEM;
+  cfg.dynamicSmemBytes = Cfg<BN, KSPLIT>::SMEM;
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   int n = 0;
@@ -650,10 +653,10 @@ static void conv_limits(cudaError_t& e) {
   auto set = [&](const void* f, int bytes) {
     if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   };
-  set((const void*)cv::conv_tc_kernel<BN, 1>, cv::Cfg<BN>::SMEM);
-  set((const void*)cv::conv_tc_kernel<BN, 2>, cv::smem_split<BN>());
-  set((const void*)cv::conv_tc_kernel<BN, 4>, cv::smem_split<BN>());
-  set((const void*)cv::conv_tc_kernel<BN, 8>, cv::smem_split<BN>());
+  set((const void*)cv::conv_tc_kernel<BN, 1>, cv::Cfg<BN, 1>::SMEM);
+  set((const void*)cv::conv_tc_kernel<BN, 2>, cv::Cfg<BN, 2>::SMEM);
+  set((const void*)cv::conv_tc_kernel<BN, 4>, cv::Cfg<BN, 4>::SMEM);
+  set((const void*)cv::conv_tc_kernel<BN, 8>, cv::Cfg<BN, 8>::SMEM);
 }
 
 cudaError_t conv_tc_set_smem_limits() {
