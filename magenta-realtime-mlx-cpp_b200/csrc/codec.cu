@@ -32,19 +32,6 @@ namespace {
       throw Error{MRTDF_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)};                   \
   } while (0)
 
-template <typename F>
-int guarded(F&& f) {
-  try {
-    f();
-    return MRTDF_OK;
-  } catch (const Error& e) {
-    set_error(e.code, e.msg);
-    return e.code;
-  } catch (const std::exception& e) {
-    set_error(MRTDF_ERR_INVALID, e.what());
-    return MRTDF_ERR_INVALID;
-  }
-}
 
 // Decoder block table (dec_block_specs, spectrostream.cpp:328-338): in, out,
 // stride (h, w), transposed kernel (h, w); every post kernel is 3 x 3.

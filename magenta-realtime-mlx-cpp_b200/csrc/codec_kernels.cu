@@ -31,10 +31,13 @@
 #include "codec_kernels.cuh"
 #include "common.cuh"
 #include "device_errors.h"
+#include "tcgen05.cuh"
 
 namespace mrtdf {
 
 namespace cv {
+
+using namespace tcg;
 
 constexpr int BM = 128, BK = kConvBK;
 constexpr int A_BYTES = BM * BK * 4;  // 16 KB, 1024-byte multiple (swizzle atoms)
@@ -57,28 +60,6 @@ struct Cfg {
   static_assert(B_BYTES % 1024 == 0, "weight tile must keep the 1024-byte swizzle alignment");
 };
 
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
-      "[%6];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
 __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                          uint32_t accumulate) {
   asm volatile(
@@ -88,22 +69,6 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // elu with alpha 1 (nn_ops.h:31-39)
 __device__ __forceinline__ float elu1(float v) { return v > 0.f ? v : expf(v) - 1.0f; }
@@ -118,17 +83,6 @@ __device__ __forceinline__ float elu1(float v) { return v > 0.f ? v : expf(v) - 
 // one cluster barrier each CTA sums its rows over the slots in rank order
 // (deterministic) and runs the epilogue on them. The receive region lies past
 // the pipeline buffers, so no CTA waits for another's mainloop to push.
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void st_cluster_f32x4(float* local, uint32_t rank, float a, float b, float c, float d) {
-  uint32_t ra;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(ra), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
-
-
 // Epilogue of one accumulator row r, output channels [n, n + 16): the row's
 // output position, then bias, ELU, residual, stores (raw and / or ELU'd,
 // the stereo split folded into the address). Rows outside the tile's valid
@@ -345,23 +299,10 @@ __global__ void __launch_bounds__(128, KSPLIT > 1 ? 1 : 2)
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-  });
-  return fn;
-}
-
 // Input activation (in_n, in_h, in_w, cin) as a 4-D map {cin, in_w, in_h,
 // in_n}: box 32 channels x wt x ht x 1, 128-byte swizzle, zero fill.
 bool make_map_act(CUtensorMap* m, const ConvParams& p) {
-  auto fn = encode_fn();
+  auto fn = tcg::encode_tiled_fn();
   if (!fn) return false;
   const cuuint64_t dims[4] = {(cuuint64_t)p.cin, (cuuint64_t)p.in_w, (cuuint64_t)p.in_h, (cuuint64_t)p.in_n};
   const cuuint64_t strides[3] = {(cuuint64_t)p.cin * 4, (cuuint64_t)p.in_w * p.cin * 4,
@@ -375,7 +316,7 @@ bool make_map_act(CUtensorMap* m, const ConvParams& p) {
 
 // Weights (cout, ntaps * cin) row-major: box 32 x bn rows.
 bool make_map_wgt(CUtensorMap* m, const ConvParams& p, int bn) {
-  auto fn = encode_fn();
+  auto fn = tcg::encode_tiled_fn();
   if (!fn) return false;
   const cuuint64_t K = (cuuint64_t)p.ntaps * p.cin;
   const cuuint64_t dims[2] = {K, (cuuint64_t)p.cout};

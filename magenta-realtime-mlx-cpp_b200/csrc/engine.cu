@@ -174,19 +174,6 @@ struct mrtdf_stream {
 // ---------------------------------------------------------------------------
 namespace {
 
-template <typename F>
-int guarded(F&& f) {
-  try {
-    f();
-    return MRTDF_OK;
-  } catch (const Error& e) {
-    set_error(e.code, e.msg);
-    return e.code;
-  } catch (const std::exception& e) {
-    set_error(MRTDF_ERR_INVALID, e.what());
-    return MRTDF_ERR_INVALID;
-  }
-}
 
 void check_cuda(cudaError_t e, const char* what) {
   if (e != cudaSuccess) throw Error{MRTDF_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e)};

@@ -33,10 +33,13 @@
 
 #include "common.cuh"
 #include "encoder_kernels.cuh"
+#include "tcgen05.cuh"
 
 namespace mrtdf {
 
 namespace tc {
+
+using namespace tcg;
 
 constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3;
 constexpr int A_BYTES = BM * BK * 2;  // 16 KB
@@ -49,27 +52,11 @@ constexpr uint32_t TMEM_COLS = 128;
 constexpr int kTileLd = BN + 8;
 static_assert(BM * kTileLd * 2 <= STAGES * STAGE_BYTES, "epilogue tile must fit the pipeline buffers");
 
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu)  // start address
-         | ((uint64_t)1 << 16)                // LBO (unused for swizzled K-major)
-         | ((uint64_t)(1024 >> 4) << 32)      // SBO: 8 rows x 128 B
-         | ((uint64_t)1 << 46)                // version (sm_100)
-         | ((uint64_t)2 << 61);               // SWIZZLE_128B
-}
-
 constexpr uint32_t kIdesc = (1u << 4)              // D: f32
                             | (1u << 7)            // A: bf16
                             | (1u << 10)           // B: bf16
                             | ((uint32_t)(BN >> 3) << 17)
                             | ((uint32_t)(BM >> 4) << 24);
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
 
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                         uint32_t accumulate) {
@@ -80,23 +67,6 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // ---- split-K over a thread-block cluster (few output tiles, long K) -------
 // CTA z of a cluster (z = blockIdx.z, cluster dims (1, 1, KSPLIT)) runs k-tiles
@@ -109,16 +79,6 @@ constexpr int kPartLd = BN + 4;                      // floats per partial-tile 
 constexpr int kPartBytes = BM * kPartLd * 4;         // 66 KB receive region (split-K launches only)
 constexpr int SMEM_SPLIT = SMEM + kPartBytes;
 static_assert(BM * kTileLd * 2 <= SMEM_PIPE, "epilogue tile must fit the pipeline buffers");
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void st_cluster_f32x4(float* local, uint32_t rank, float a, float b, float c, float d) {
-  uint32_t ra;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(ra), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
-
 // 16 fp32 accumulator columns [c, c + 16) of one tile row -> bf16 tile row
 // (GEGLU: 8 output columns at c / 2).
 template <int EPI>
@@ -366,24 +326,11 @@ __global__ void __launch_bounds__(128, 1)
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-  });
-  return fn;
-}
-
 // 2-D bf16 tensor map over a row-major (rows, cols) matrix with leading
 // dimension ld (elements): box 64 columns x 128 rows, 128-byte swizzle,
 // zero fill outside the matrix.
 bool make_map(CUtensorMap* m, const void* base, int rows, int cols, int ld) {
-  auto fn = encode_fn();
+  auto fn = tcg::encode_tiled_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};

@@ -14,17 +14,6 @@ using namespace mrtdf;
 
 namespace {
 constexpr int kMaskToken = 1;  // SystemConfig::vocab_mask_token (system.h:75)
-
-template <typename F>
-int guarded_glue(F&& f) {
-  try {
-    f();
-    return MRTDF_OK;
-  } catch (const Error& e) {
-    set_error(e.code, e.msg);
-    return e.code;
-  }
-}
 }  // namespace
 
 extern "C" {
@@ -32,7 +21,7 @@ extern "C" {
 int mrtdf_build_encoder_inputs(const int32_t* context, int ctx_frames, int rvq_depth, int enc_depth,
                                const int32_t* style, int style_depth, int codebook_size, int codec_offset,
                                int32_t* out) {
-  return guarded_glue([&] {
+  return guarded([&] {
     if (!context || !out || (style_depth > 0 && !style)) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
     if (ctx_frames < 0 || rvq_depth <= 0 || enc_depth < 0 || enc_depth > rvq_depth || style_depth < 0)
       throw Error{MRTDF_ERR_INVALID, "bad sizes"};
@@ -53,7 +42,7 @@ int mrtdf_build_encoder_inputs(const int32_t* context, int ctx_frames, int rvq_d
 
 int mrtdf_context_roll(int32_t* context, int ctx_frames, int rvq_depth, const int32_t* new_codes,
                        int chunk_frames) {
-  return guarded_glue([&] {
+  return guarded([&] {
     if (!context || !new_codes) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
     if (chunk_frames < 0 || chunk_frames > ctx_frames) throw Error{MRTDF_ERR_INVALID, "chunk longer than context"};
     // new[f] = old[(f + chunk_frames) % ctx_frames] for the kept frames,
@@ -65,7 +54,7 @@ int mrtdf_context_roll(int32_t* context, int ctx_frames, int rvq_depth, const in
 }
 
 int mrtdf_llm_to_rvq(const int32_t* llm, int n, int rvq_depth, int codebook_size, int codec_offset, int32_t* out) {
-  return guarded_glue([&] {
+  return guarded([&] {
     if (!llm || !out || codebook_size <= 0) throw Error{MRTDF_ERR_INVALID, "bad argument"};
     for (int i = 0; i < n; ++i)
       for (int d = 0; d < rvq_depth; ++d) {
@@ -81,7 +70,7 @@ int mrtdf_llm_to_rvq(const int32_t* llm, int n, int rvq_depth, int codebook_size
 }
 
 int mrtdf_rvq_to_llm(const int32_t* rvq, int n, int rvq_depth, int codebook_size, int codec_offset, int32_t* out) {
-  return guarded_glue([&] {
+  return guarded([&] {
     if (!rvq || !out) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
     for (int i = 0; i < n; ++i)
       for (int d = 0; d < rvq_depth; ++d) out[i * rvq_depth + d] = codec_offset + d * codebook_size + rvq[i * rvq_depth + d];

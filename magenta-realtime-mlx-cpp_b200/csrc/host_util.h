@@ -7,6 +7,7 @@
 #include <functional>
 #include <map>
 #include <memory>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -21,6 +22,23 @@ struct Error {
 };
 void set_error(int code, const std::string& msg);
 const char* last_error();
+
+// Body of a C ABI entry point: runs f, turns a thrown Error (or any
+// std::exception, as MRTDF_ERR_INVALID) into the status code and the
+// thread-local message of mrtdf_last_error().
+template <typename F>
+int guarded(F&& f) {
+  try {
+    f();
+    return MRTDF_OK;
+  } catch (const Error& e) {
+    set_error(e.code, e.msg);
+    return e.code;
+  } catch (const std::exception& e) {
+    set_error(MRTDF_ERR_INVALID, e.what());
+    return MRTDF_ERR_INVALID;
+  }
+}
 
 // ---- numerics --------------------------------------------------------------
 float bf16_round_host(float x);

@@ -1,0 +1,98 @@
+// Helpers shared by the tcgen05 kernels (bf16 encoder / decode GEMMs in
+// gemm_tc.cu, tf32 convolutions in codec_kernels.cu): shared-memory matrix
+// descriptors, TMA tiled loads (no multicast), the tcgen05 commit / TMEM load /
+// fence forms, thread-block-cluster barrier and distributed-shared-memory
+// stores, and the driver's tensor-map encoder.
+//
+// Descriptor formats follow the sm_100 UMMA definitions (CUTLASS
+// cute/arch/mma_sm100_desc.hpp): shared-memory descriptor = start >> 4, LBO
+// (16-byte units) at bit 16, SBO at bit 32, version 1 at bit 46, layout type at
+// bit 61 (2 = 128-byte swizzle).
+#pragma once
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace mrtdf {
+namespace tcg {
+
+// K-major operand tile with 128-byte rows in the 128-byte swizzle: 8-row
+// atoms of 1024 bytes (SBO), LBO unused.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu)  // start address
+         | ((uint64_t)1 << 16)                // LBO (unused for swizzled K-major)
+         | ((uint64_t)(1024 >> 4) << 32)      // SBO: 8 rows x 128 B
+         | ((uint64_t)1 << 46)                // version (sm_100)
+         | ((uint64_t)2 << 61);               // SWIZZLE_128B
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// arrive on `bar` once the MMAs issued so far by this thread have retired
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns of TMEM (one row per thread)
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// every thread of every CTA in the cluster; release / acquire orders the
+// distributed-shared-memory stores before it against the loads after it
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// 16-byte store into the same shared-memory offset of cluster CTA `rank`
+__device__ __forceinline__ void st_cluster_f32x4(float* local, uint32_t rank, float a, float b, float c, float d) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(ra), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda)
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_tiled_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+}  // namespace tcg
+}  // namespace mrtdf
