@@ -389,7 +389,7 @@ constexpr int kOcXFloats = kOcSpan * kOcSpan * kOcStride;
 constexpr int kOcWFloats = 2 * 49 * 64;
 constexpr int kOcSmem = (kOcXFloats + kOcWFloats) * 4;
 
-__global__ void __launch_bounds__(256) out_conv_kernel(const OutConvParams p) {
+__global__ void __launch_bounds__(256, 2) out_conv_kernel(const OutConvParams p) {
   extern __shared__ float oc_sm[];
   float* xs = oc_sm;
   float* ws = oc_sm + kOcXFloats;
@@ -421,20 +421,25 @@ __global__ void __launch_bounds__(256) out_conv_kernel(const OutConvParams p) {
     __syncthreads();
 #pragma unroll 1
     for (int dx = 0; dx < 7; ++dx) {
+      // the thread's 10 input rows of this column tap, 8 channels each, in
+      // registers: every weight pair read below serves all 4 output rows
+      float4 xa[kOcRows + 6], xb[kOcRows + 6];
 #pragma unroll
       for (int rr = 0; rr < kOcRows + 6; ++rr) {
         const float* xp = xs + ((ty * kOcRows + rr) * kOcSpan + tx + dx) * kOcStride;
-        const float4 a = *reinterpret_cast<const float4*>(xp);
-        const float4 b = *reinterpret_cast<const float4*>(xp + 4);
+        xa[rr] = *reinterpret_cast<const float4*>(xp);
+        xb[rr] = *reinterpret_cast<const float4*>(xp + 4);
+      }
 #pragma unroll
-        for (int i = 0; i < kOcRows; ++i) {
-          const int dy = rr - i;
-          if (dy < 0 || dy > 6) continue;
+      for (int dy = 0; dy < 7; ++dy) {
 #pragma unroll
-          for (int o = 0; o < 2; ++o) {
-            const float* wp = ws + ((o * 7 + dy) * 7 + dx) * 64 + c0;
-            const float4 w0 = *reinterpret_cast<const float4*>(wp);
-            const float4 w1 = *reinterpret_cast<const float4*>(wp + 4);
+        for (int o = 0; o < 2; ++o) {
+          const float* wp = ws + ((o * 7 + dy) * 7 + dx) * 64 + c0;
+          const float4 w0 = *reinterpret_cast<const float4*>(wp);
+          const float4 w1 = *reinterpret_cast<const float4*>(wp + 4);
+#pragma unroll
+          for (int i = 0; i < kOcRows; ++i) {
+            const float4 a = xa[i + dy], b = xb[i + dy];
             float s = acc[i][o];
             s = fmaf(a.x, w0.x, s);
             s = fmaf(a.y, w0.y, s);
