@@ -1,5 +1,7 @@
-"""Committed golden vectors (tests/golden/tiny_golden.npz, made by
-tests/golden/make_golden.py from the CPU oracle on the tiny config).
+"""Committed golden vectors: tests/golden/tiny_golden.npz (made by
+tests/golden/make_golden.py from the Depthformer oracle on the tiny config)
+and tests/golden/codec_golden.npz (made by tests/golden/make_codec_golden.py
+from the SpectroStream oracle).
 
 CPU: the weight generator and the oracle still reproduce them bit for bit.
 GPU: the engine matches them within the parity tolerances."""
@@ -55,3 +57,26 @@ def test_engine_ids_vs_golden(mrtdf, tiny_weights, golden):
     st1 = mrtdf.Stream(eng, 1, False)
     np.testing.assert_array_equal(
         st1.generate_tokens(golden["ids"][:1], mrtdf.gen_opts(cfg, F, temperature=0.0))[0], golden["greedy_fp32_nocfg"])
+
+
+# ---- SpectroStream decode phase (tests/golden/codec_golden.npz) -------------
+CODEC_GOLDEN = os.path.join(HERE, "golden", "codec_golden.npz")
+
+
+def test_codec_oracle_reproduces_golden(mrtdf, oracle, tmp_path):
+    """The codec weight generator writes the same bundles and the float32
+    oracle reproduces the committed outputs (to 1e-6 of each array's largest
+    value: libm's exp / cos may pick a different code path per CPU)."""
+    import make_codec_golden as mcg
+
+    golden = np.load(CODEC_GOLDEN)
+    dec, cb = mcg.bundles(str(tmp_path))
+    assert hashlib.sha256(open(dec, "rb").read()).hexdigest() == str(golden["decoder_sha256"])
+    assert hashlib.sha256(open(cb, "rb").read()).hexdigest() == str(golden["codebooks_sha256"])
+    data = mcg.make(dec, cb)
+    np.testing.assert_array_equal(data["codes"], golden["codes"])
+    np.testing.assert_array_equal(data["dequant"], golden["dequant"])  # float32 adds in level order
+    for k in ("decoded", "audio", "istft"):
+        want = golden[k]
+        assert data[k].shape == want.shape, k
+        assert np.abs(data[k] - want).max() <= 1e-6 * np.abs(want).max(), k

@@ -161,3 +161,37 @@ def test_invalid_config_is_rejected(mrtdf):
     cfg = mrtdf.preset("tiny").replace(d_kv=32)
     with pytest.raises(mrtdf.MrtdfError, match="d_kv"):
         mrtdf.Engine(cfg)
+
+
+def test_codec_create_fails_cleanly_without_sm100(mrtdf):
+    """The SpectroStream decode phase refuses without a B200 too (no CPU
+    fallback)."""
+    import torch
+
+    import mrtss
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    with pytest.raises(mrtdf.MrtdfError) as ei:
+        mrtss.Codec(max_batch=1, max_frames=4)
+    assert ei.value.code == 2  # MRTDF_ERR_CUDA
+
+
+def test_codec_writer_argument_errors(mrtdf, tmp_path):
+    import mrtss
+
+    lib = mrtss.lib()
+    ok_dec, ok_cb = str(tmp_path / "d.safetensors").encode(), str(tmp_path / "c.safetensors").encode()
+    assert lib.mrtss_write_random_safetensors(0, 0, ok_dec, ok_cb) == 1  # levels must be positive
+    assert lib.mrtss_write_random_safetensors(0, 16, None, ok_cb) == 1
+    rc = lib.mrtss_write_random_safetensors(0, 16, str(tmp_path / "nodir" / "d").encode(), ok_cb)
+    assert rc == 3 and b"cannot write" in lib.mrtdf_last_error()  # MRTDF_ERR_IO
+    # the codebook bundle holds "codebooks" (levels, 1024, 256)
+    assert lib.mrtss_write_random_safetensors(0, 4, ok_dec, ok_cb) == 0
+    from safetensors.numpy import load_file
+
+    assert load_file(ok_cb.decode())["codebooks"].shape == (4, 1024, 256)
+    # the same seed writes the same bundle
+    again = str(tmp_path / "d2.safetensors").encode()
+    assert lib.mrtss_write_random_safetensors(0, 4, again, str(tmp_path / "c2.safetensors").encode()) == 0
+    assert open(ok_dec, "rb").read() == open(again, "rb").read()
