@@ -354,7 +354,16 @@ def run_ours(args):
             line["depth_microbench"] = depth_microbench(mrtdf, cfg, st)
         line["multi_stream"] = multi_stream(mrtdf, torch, eng, cfg, device, rank, world, dist)
         if rank == 0:
-            line["codec_decode"] = codec_decode(torch, peaks, device, local, cpu=world == 1 and not args.no_cpu_baseline)
+            # the next stage of a chunk; a failure here is reported in the line
+            # (and its traceback on stderr) without losing the headline number
+            try:
+                line["codec_decode"] = codec_decode(torch, peaks, device, local,
+                                                    cpu=world == 1 and not args.no_cpu_baseline)
+            except Exception as exc:  # noqa: BLE001
+                import traceback
+
+                traceback.print_exc()
+                line["codec_decode"] = {"error": f"{type(exc).__name__}: {exc}"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.timed_only:
         tps, ms_cpu, cores, t_enc, t_frame = cpu_sample(2)
         line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port",
