@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-A step is one 2 s chunk of BASELINE config 2: the benchmark architecture
+A step is one 2 s chunk of BASELINE.json config 2: the benchmark architecture
 ("hybrid": d_model 1024, 16 x 64 heads, d_ff 2816, layers 12/20/4, vocab
 16388) in bf16 with random-init N(0, 0.02) weights (seed 0), batch 1 with
 CFG (cond/uncond rows), guidance 4.0, top-k 40, temperature 1.1, Philox
@@ -348,7 +348,7 @@ def run_ours(args):
         launches = st_launch_count(cfg)
     line["gpu_launches"] = launches * K
     if not args.no_suite and not args.timed_only:
-        # BASELINE configs 3-5 on the same engine (configs 3 and 4 on rank 0 only)
+        # BASELINE.json configs 3-5 on the same engine (configs 3 and 4 on rank 0 only)
         if rank == 0:
             line["encoder_microbench"] = encoder_microbench(eng, peaks)
             line["depth_microbench"] = depth_microbench(mrtdf, cfg, st)
@@ -431,7 +431,7 @@ def roofline_leg(mrtdf, cfg, st, peaks: dict) -> dict:
 
 
 def encoder_microbench(eng, peaks: dict) -> dict:
-    """BASELINE config 3: the encoder pass + cross-K/V projection of all 20
+    """BASELINE.json config 3: the encoder pass + cross-K/V projection of all 20
     temporal layers over 1006 uniform-random ids (seed 2) at 1, 16 and 128
     rows, one CUDA graph per size, against the measured bf16 tensor peak."""
     peak = peaks.get("bf16_tflops", 1590.0)
@@ -444,7 +444,7 @@ def encoder_microbench(eng, peaks: dict) -> dict:
 
 
 def depth_microbench(mrtdf, cfg, st) -> dict:
-    """BASELINE config 4: 1000 frames x 16 sequential depth steps (bf16,
+    """BASELINE.json config 4: 1000 frames x 16 sequential depth steps (bf16,
     CFG pair, sampler feedback), each frame from an N(0, 1) hidden state
     (seed 3); 50-frame graph replayed 20 times. Achieved GB/s = algorithmic
     bytes per step (depth stack + lm_head level slice + K/V reads) / time;
@@ -547,7 +547,7 @@ def codec_decode(torch, peaks: dict, device, local: int, cpu: bool, S: int = 51,
 
 def multi_stream(mrtdf, torch, eng, cfg, device, rank: int, world: int, dist, n_streams: int = 64,
                  per_group: int = 64, rounds: int = 2) -> dict:
-    """BASELINE config 5: 64 independent CFG streams per GPU (bf16, top-k 40,
+    """BASELINE.json config 5: 64 independent CFG streams per GPU (bf16, top-k 40,
     T 1.1), seeds 100 + global stream index, batched as one engine stream of
     64 CFG pairs (128 rows: RMSNorm + tcgen05 GEMM projections; with
     per_group < 64, several engine streams run concurrently on their own

@@ -17,7 +17,7 @@
 // logits, so the oracle follows the code line by line instead.
 //
 // Two numeric modes:
-//   fp32 - every op in float32 (BASELINE config 1).
+//   fp32 - every op in float32 (BASELINE.json config 1).
 //   bf16 - MLX's bf16 semantics: weights rounded to bf16 at load
 //          (modules.cpp:47-54) and every op output rounded to bf16
 //          (round-to-nearest-even); reductions inside matmul, rms_norm and

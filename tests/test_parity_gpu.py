@@ -1,6 +1,6 @@
 """Parity of the CUDA engine (through the C ABI) against the CPU oracle.
 
-Tolerances (BASELINE north_star): teacher-forced logits within 1e-4 max-abs
+Tolerances (BASELINE.json north_star): teacher-forced logits within 1e-4 max-abs
 in fp32 and 2e-2 in bf16; greedy ids bit-exact in fp32; sampled ids
 bit-exact given identical logits and draws.
 """
