@@ -1,6 +1,6 @@
 """Build recipe for the CPU oracle (test infrastructure only).
 
-Compiles the Depthformer and SpectroStream oracles (oracle/*.cpp) into
+Compiles the Depthformer, SpectroStream and MusicCoCa oracles (oracle/*.cpp) into
 oracle/_build/liboracle.so with g++. The
 exact-arithmetic translation unit (bf16 rounding, Philox, Gumbel, CFG mix)
 is built with -ffp-contract=off so no multiply-add is fused; the model code
@@ -20,7 +20,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(BUILD, "liboracle.so")
-SOURCES = ["depthformer_oracle.cpp", "oracle_exact.cpp", "spectrostream_oracle.cpp"]
+SOURCES = ["depthformer_oracle.cpp", "oracle_exact.cpp", "spectrostream_oracle.cpp", "musiccoca_oracle.cpp"]
 HEADERS = ["oracle.h", "safetensors_reader.h"]
 
 

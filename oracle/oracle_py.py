@@ -69,6 +69,13 @@ def lib() -> ctypes.CDLL:
         L.orc_ss_conv2d.argtypes = [P, I, I, I, I, P, P, I, I, I, I, I, I, P]
         L.orc_ss_conv_transpose2d.argtypes = [P, I, I, I, I, P, P, I, I, I, I, I, P]
         L.orc_ss_set_num_threads.argtypes = [I]
+        # MusicCoCa text tower + style RVQ (musiccoca_oracle.cpp)
+        L.orc_mc_last_error.restype = ctypes.c_char_p
+        L.orc_mc_create.restype = P
+        L.orc_mc_create.argtypes = [ctypes.c_char_p, ctypes.c_char_p]
+        L.orc_mc_destroy.argtypes = [P]
+        L.orc_mc_embed_text.argtypes = [P, P, P, I, I, P]
+        L.orc_mc_quantize.argtypes = [P, P, I, I, P]
         _lib = L
     return _lib
 
@@ -298,3 +305,44 @@ def conv_transpose2d(x: np.ndarray, w: np.ndarray, b: np.ndarray, stride=(1, 1))
     _ss_check(lib().orc_ss_conv_transpose2d(x.ctypes.data, N, H, W, C, w.ctypes.data, b.ctypes.data, O, kh, kw, sh,
                                             sw, out.ctypes.data))
     return out
+
+
+# ---------------------------------------------------------------------------
+# MusicCoCa text tower and style-token quantisation (oracle/musiccoca_oracle.cpp)
+# ---------------------------------------------------------------------------
+class StyleOracle:
+    """CPU restatement (float32) of MusicCoCaEncoder::embed_text and of the
+    rvq_quantization StyleModel::tokenize applies to its embedding."""
+
+    def __init__(self, encoder_path: str, codebooks_path: str):
+        h = lib().orc_mc_create(encoder_path.encode(), codebooks_path.encode())
+        if not h:
+            raise RuntimeError("oracle: " + lib().orc_mc_last_error().decode())
+        self.h = h
+
+    def embed_text(self, ids: np.ndarray, padding: np.ndarray) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        pad = np.ascontiguousarray(padding, dtype=np.float32)
+        B, L = ids.shape
+        out = np.empty((B, 768), np.float32)
+        if lib().orc_mc_embed_text(self.h, ids.ctypes.data, pad.ctypes.data, B, L, out.ctypes.data) != 0:
+            raise RuntimeError("oracle: " + lib().orc_mc_last_error().decode())
+        return out
+
+    def quantize(self, emb: np.ndarray, levels: int) -> np.ndarray:
+        emb = np.ascontiguousarray(emb, dtype=np.float32)
+        out = np.empty((emb.shape[0], levels), np.int32)
+        if lib().orc_mc_quantize(self.h, emb.ctypes.data, emb.shape[0], levels, out.ctypes.data) != 0:
+            raise RuntimeError("oracle: " + lib().orc_mc_last_error().decode())
+        return out
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().orc_mc_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
