@@ -20,8 +20,7 @@ and 16 depth steps + sampling per frame = 800 RVQ tokens.
   bytes per launch / its average launch duration, measured with CUDA events
   by replaying exactly the chunk's GEMV launches (mrtdf_bench_gemv).
 * cpu_baseline: the CPU oracle (C++ restatement of the reference's eager
-  Depthformer, all host threads) on a bounded sample: the encoder pass and
-  two frames, extrapolated to a 50-frame chunk.
+  Depthformer, all host threads) on one whole chunk of the same workload.
 
 * codec_decode (rank 0): the next stage of a chunk, the SpectroStream decode
   phase (RVQ codes -> decoder -> iSTFT -> 48 kHz stereo) on the tensor cores;
@@ -33,7 +32,8 @@ per GPU with seed offset by rank, no collective on the data path
 torch.distributed.
 
 `--impl reference` times the reference's algorithm on the host cores: the
-reference (MLX) cannot be built here, so this runs the oracle port.
+reference (MLX) cannot be built here, so this runs the oracle port, one frame
+(16 tokens) per step, without loading the engine library.
 """
 from __future__ import annotations
 
@@ -130,45 +130,41 @@ def host_cores() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_sample(frames: int = 2):
-    """Time the oracle on the encoder + `frames` frames of the same workload;
-    returns (tokens/s extrapolated to a 50-frame chunk, ms per chunk, threads)."""
+def _oracle():
+    """The CPU oracle (test infrastructure; only the CPU legs use it)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import mrtdf
     import oracle_py
 
     oracle_py.set_num_threads(host_cores())
-    cfg = mrtdf.preset("hybrid", mrtdf.DTYPE_BF16)
-    with tempfile.TemporaryDirectory() as td:
-        path = os.path.join(td, "w.safetensors")
-        mrtdf.write_random_safetensors(cfg, 0, path)
-        orc = oracle_py.Oracle(path, cfg.as_ints())
-    ids = _initial_ids(mrtdf, cfg, 0)
-    t0 = time.perf_counter()
-    orc.encode(ids)
-    t_enc = time.perf_counter() - t0
-    rng = np.random.default_rng(0)
-    t0 = time.perf_counter()
-    x = None
-    for f in range(frames):
-        tout = orc.temporal_step(x, f)
-        d = None
-        for l in range(cfg.rvq_depth):
-            orc.depth_step(d, l)
-            d = tout if l == 0 else d
-        x = rng.standard_normal(tout.shape).astype(np.float32) * 0.1
-    t_frame = (time.perf_counter() - t0) / frames
-    ms_chunk = 1e3 * (t_enc + 50 * t_frame)
-    return TOKENS_PER_CHUNK / (ms_chunk / 1e3), ms_chunk, oracle_py.num_threads(), t_enc, t_frame
+    return oracle_py
 
 
-def _initial_ids(mrtdf, cfg, seed: int) -> np.ndarray:
+def cpu_chunk():
+    """One whole chunk of the same workload on the CPU oracle (all host
+    threads): random-init weights of seed 0 built in memory, the chunk-0
+    encoder ids, encode + 50 frames of (temporal step, 16 x (depth step with
+    the level's lm_head rows, CFG mix, top-k 40, T 1.1, Gumbel draws from
+    Philox seed 1, embedding feedback)). Returns (tokens/s, ms, threads)."""
+    oracle_py = _oracle()
+    cfg = oracle_py.preset_ints("hybrid", 1)
+    orc = oracle_py.Oracle.from_random(cfg, 0)
+    ids = _initial_ids(oracle_py.build_encoder_inputs, 0)
+    t0 = time.perf_counter()
+    orc.gen_begin(ids)
+    for f in range(50):
+        orc.gen_frame(f, 4.0, 1.1, 40, True, 1)
+    ms = (time.perf_counter() - t0) * 1e3
+    orc.close()
+    return TOKENS_PER_CHUNK / (ms / 1e3), ms, oracle_py.num_threads()
+
+
+def _initial_ids(build_encoder_inputs, seed: int) -> np.ndarray:
     """Chunk-0 encoder ids: empty context (all MASK) + 6 style ids drawn
     uniformly from the codec range (stand-in for MusicCoCa tokens)."""
     rng = np.random.default_rng(1000 + seed)
-    ctx = -np.ones((250, cfg.rvq_depth), np.int32)
-    style = rng.integers(cfg.codec_offset, cfg.codec_offset + cfg.rvq_depth * cfg.codebook_size, 6).astype(np.int32)
-    return mrtdf.build_encoder_inputs(ctx, style, 4, cfg.codebook_size, cfg.codec_offset)
+    ctx = -np.ones((250, 16), np.int32)
+    style = rng.integers(2, 2 + 16 * 1024, 6).astype(np.int32)
+    return build_encoder_inputs(ctx, style, 4, 1024, 2)
 
 
 # ---------------------------------------------------------------------------
@@ -215,59 +211,52 @@ def barrier(dist, device=None):
 # arms
 # ---------------------------------------------------------------------------
 def run_reference(args):
+    """The reference's algorithm on the host cores: the CPU oracle (the
+    reference itself needs MLX, which cannot be installed here), all host
+    threads, rank 0 only. A step is one frame of the chunk: the temporal
+    step and 16 x (depth step with the level's lm_head rows, CFG mix, top-k /
+    temperature / Gumbel sampling, embedding feedback) = 16 tokens; value =
+    16 / mean step time. The encoder pass runs untimed before frame 0 of
+    every 50-frame chunk (its time is reported in the sample text). This
+    process never loads libmrtdf.so."""
     rank, world, local = dist_env()
     if rank != 0:
         return 0
     W, K = args.warmup, args.steps
-    # one step = one frame of CPU decode; the encoder pass is timed once and
-    # amortised over the chunk
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import mrtdf
-    import oracle_py
-
-    # every host core (torchrun sets OMP_NUM_THREADS=1 per rank; rank 0 runs alone)
-    oracle_py.set_num_threads(host_cores())
-    cfg = mrtdf.preset("hybrid", mrtdf.DTYPE_BF16)
-    with tempfile.TemporaryDirectory() as td:
-        path = os.path.join(td, "w.safetensors")
-        mrtdf.write_random_safetensors(cfg, 0, path)
-        orc = oracle_py.Oracle(path, cfg.as_ints())
-    ids = _initial_ids(mrtdf, cfg, 0)
+    oracle_py = _oracle()
+    cfg = oracle_py.preset_ints("hybrid", 1)
+    orc = oracle_py.Oracle.from_random(cfg, 0)
+    ids = _initial_ids(oracle_py.build_encoder_inputs, 0)
     t0 = time.perf_counter()
-    orc.encode(ids)
+    orc.gen_begin(ids)
     t_enc = time.perf_counter() - t0
-    rng = np.random.default_rng(0)
     times = []
-    x = None
+    chunk = 0
     for s in range(W + K):
-        f = s % cfg.max_frames
+        f = s % 50
         if f == 0 and s:
-            orc.encode(ids)
-            x = None
+            chunk += 1
+            orc.gen_begin(ids)
         t0 = time.perf_counter()
-        tout = orc.temporal_step(x, f)
-        d = None
-        for l in range(cfg.rvq_depth):
-            orc.depth_step(d, l)
-            d = tout
+        orc.gen_frame(f, 4.0, 1.1, 40, True, 1 + chunk)
         if s >= W:
             times.append(time.perf_counter() - t0)
-        x = rng.standard_normal(tout.shape).astype(np.float32) * 0.1
     t_frame = float(np.mean(times))
-    ms_chunk = 1e3 * (t_enc + 50 * t_frame)
-    value = TOKENS_PER_CHUNK / (ms_chunk / 1e3)
+    value = 16 / t_frame
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
-        "warmup": W, "ms_per_step": ms_chunk, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "warmup": W, "ms_per_step": t_frame * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (random-init weights N(0,0.02) seed 0; chunk-0 context)",
         "config": workload_config(world),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": oracle_py.num_threads(), "kind": "port",
-                         "sample": f"encoder pass once ({t_enc:.2f} s) + {K} timed frames "
-                                   f"({t_frame:.2f} s each), extrapolated to 50 frames; "
+                         "sample": f"{K} timed frames of config 2 (16 tokens each: temporal step + 16 depth steps "
+                                   f"with level-slice lm_head, CFG, top-k 40, T 1.1, Gumbel, feedback); "
+                                   f"encoder pass untimed ({t_enc:.2f} s per chunk, not in the value); "
                                    "the reference's MLX build is unavailable here (MLX not installable)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+    orc.close()
     return 0
 
 
@@ -286,7 +275,7 @@ def run_ours(args):
     ext = torch.cuda.ExternalStream(st.cuda_stream(), device=device)
     W, K = args.warmup, args.steps
 
-    ids = _initial_ids(mrtdf, cfg, rank)
+    ids = _initial_ids(mrtdf.build_encoder_inputs, rank)
     ids_dev = torch.from_numpy(ids).to(device)
     out_dev = torch.empty((1, 50, cfg.rvq_depth), dtype=torch.int32, device=device)
 
@@ -365,10 +354,10 @@ def run_ours(args):
                 traceback.print_exc()
                 line["codec_decode"] = {"error": f"{type(exc).__name__}: {exc}"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.timed_only:
-        tps, ms_cpu, cores, t_enc, t_frame = cpu_sample(2)
+        tps, ms_cpu, cores = cpu_chunk()
         line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port",
-                                "sample": f"encoder pass ({t_enc:.2f} s) + 2 frames ({t_frame:.2f} s each) "
-                                          "of the same bf16 workload, extrapolated to a 50-frame chunk"}
+                                "sample": f"one whole chunk of the same workload ({ms_cpu / 1e3:.1f} s: encoder + 50 "
+                                          "frames with sampling and feedback) on the CPU oracle"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     st.close()
@@ -559,7 +548,7 @@ def multi_stream(mrtdf, torch, eng, cfg, device, rank: int, world: int, dist, n_
     ids_dev, out_dev, seeds = [], [], []
     for g in range(groups):
         base = 100 + rank * n_streams + g * per_group
-        ids = np.concatenate([_initial_ids(mrtdf, cfg, base + i) for i in range(per_group)], axis=0)
+        ids = np.concatenate([_initial_ids(mrtdf.build_encoder_inputs, base + i) for i in range(per_group)], axis=0)
         ids_dev.append(torch.from_numpy(ids).to(device))
         out_dev.append(torch.empty((per_group, 50, cfg.rvq_depth), dtype=torch.int32, device=device))
         seeds.append([base + i for i in range(per_group)])

@@ -172,19 +172,12 @@ int mrtdf_token_embedding(mrtdf_engine* eng, const int32_t* ids, int n, float* o
  * (cfg ? 2 : 1, vocab_size); `level` selects the vocab mask when
  * opts->use_vocab_masks; `uniforms` (vocab_size floats in (0, 1)) replaces
  * the Philox draws when not NULL, otherwise the draws for (frame, level)
- * of opts->seed are used.
+ * of opts->seed are used. MRTDF_ERR_INVALID when no candidate can be drawn
+ * (NaN logits, an empty range); `token` is then -1.
  */
 int mrtdf_sample(mrtdf_engine* eng, const float* logits, int cfg, int frame, int level,
                  const mrtdf_gen_opts* opts, const float* uniforms, int32_t* token);
 
-/*
- * generate_tokens (decode.h:112-119, decode.cpp:239-573; non-speculative
- * path): encode + num_frames x (temporal_step + rvq_depth x (depth_step +
- * sample)) entirely on the device. `enc_ids` is (rows, seq_len) int32;
- * `out_ids` receives (num_sequences, num_frames, rvq_depth) int32 LLM ids.
- * `seeds` holds one seed per sequence (NULL: opts->seed + sequence index).
- * The whole chunk runs as one CUDA graph, captured on first use.
- */
 /*
  * mrtdf_sample for callers that cannot allocate GPU memory. No counterpart
  * in the reference: it exists for hosts that must not call cudaMalloc /
@@ -198,19 +191,30 @@ int mrtdf_sample(mrtdf_engine* eng, const float* logits, int cfg, int frame, int
  * Philox draws of opts->seed) and `token_dev` (one int32) are DEVICE
  * pointers owned by the caller, the work is queued on `stream` (a
  * cudaStream_t, NULL = the legacy default stream) and the call does not
- * wait for it. The sampler's scratch is a fixed 64 KiB device array inside
- * the library, held by every GPU that loads it until the process exits:
- * rows x d_model x dtype bytes must be <= 21,760 (MRTDF_ERR_RANGE
- * otherwise); nothing in it needs to start at zero, each call writes what
- * its kernel reads. The first call on a device looks up that array's address;
- * make it before any stream capture. All calls on a device share the
- * scratch, so calls that may overlap on the GPU race; serialise them (one
- * stream). Allocates nothing: no cudaMalloc, cudaFree or allocating
- * library routine.
+ * wait for it: it queues one kernel launch and nothing else (the seed
+ * travels by value). Because the call returns before the draw, a draw that
+ * fails (NaN logits, an empty range) is reported in the result: the kernel
+ * stores -1 in *token_dev. The sampler's scratch is a fixed 64 KiB device
+ * array inside the library, held by every GPU that loads it until the
+ * process exits: rows x d_model x dtype bytes must be <= 21,760
+ * (MRTDF_ERR_RANGE otherwise); nothing in it needs to start at zero, each
+ * call writes what its kernel reads. The first call on a device looks up
+ * that array's address; make it before any stream capture. All calls on a
+ * device share the scratch, so calls that may overlap on the GPU race;
+ * serialise them (one stream). Allocates nothing: no cudaMalloc, cudaFree
+ * or allocating library routine.
  */
 int mrtdf_sample_noalloc(mrtdf_engine* eng, const float* logits_dev, int cfg, int frame, int level,
                          const mrtdf_gen_opts* opts, const float* uniforms_dev, int32_t* token_dev, void* stream);
 
+/*
+ * generate_tokens (decode.h:112-119, decode.cpp:239-573; non-speculative
+ * path): encode + num_frames x (temporal_step + rvq_depth x (depth_step +
+ * sample)) entirely on the device. `enc_ids` is (rows, seq_len) int32;
+ * `out_ids` receives (num_sequences, num_frames, rvq_depth) int32 LLM ids.
+ * `seeds` holds one seed per sequence (NULL: opts->seed + sequence index).
+ * The whole chunk runs as one CUDA graph, captured on first use.
+ */
 int mrtdf_generate_tokens(mrtdf_stream* st, const int32_t* enc_ids, int seq_len,
                           const mrtdf_gen_opts* opts, const uint64_t* seeds, int32_t* out_ids);
 
@@ -235,6 +239,18 @@ int mrtdf_stream_sync(mrtdf_stream* st);
 
 /* The stream's cudaStream_t, for callers that order their own work on it. */
 void* mrtdf_stream_cuda(mrtdf_stream* st);
+
+/*
+ * Failure-detection check (no counterpart in the reference): queue on the
+ * stream one CTA that waits on an mbarrier which no thread and no copy ever
+ * completes, bounded by `timeout_us` microseconds of the GPU's global timer
+ * (1 .. 1,000,000; every production wait uses the same routine with a
+ * 0.5 s bound). The wait gives up, sets the timeout bit of the stream's error
+ * word and the call returns MRTDF_ERR_TIMEOUT, as every call does after a
+ * device-side wait gave up; the error word is cleared and the stream stays
+ * usable.
+ */
+int mrtdf_check_wait_timeout(mrtdf_stream* st, int timeout_us);
 
 /*
  * Measurement hook (no reference counterpart): replay, as one CUDA graph on

@@ -13,9 +13,10 @@
 
 namespace mrtdf {
 
-// Upper bound on mbarrier polls before a wait gives up (~10^8 polls, well
-// above a second even for L2 misses; a healthy wait takes microseconds).
-constexpr long long kSpinLimit = 100000000LL;
+// Longest a device-side wait may take before it gives up and reports
+// through the error word: 0.5 s of %globaltimer. A healthy wait takes
+// microseconds; the bound keeps a lost completion from holding the GPU.
+constexpr unsigned long long kWaitTimeoutNs = 500000000ull;
 
 // ---------------------------------------------------------------------------
 // Storage types
@@ -119,10 +120,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: returns false (and sets `err` bit) if the phase never flips.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
-  for (long long i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: returns false (and sets the kErrMbarTimeout bit of `err`)
+// when the phase has not flipped within `timeout_ns` of %globaltimer. The
+// timer is read once per 32 polls, so the fast path costs one try_wait.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err,
+                                                  unsigned long long timeout_ns = kWaitTimeoutNs) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > timeout_ns) break;
   }
   if (err) atomicOr(err, kErrMbarTimeout);
   return false;

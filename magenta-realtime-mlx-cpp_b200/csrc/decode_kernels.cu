@@ -24,7 +24,6 @@
 namespace mrtdf {
 
 constexpr int kSelfAttnMaxT = 64;  // keys of a decode self-attention (2 chunks of 32)
-constexpr int kFlagSpinLimit = 1 << 20;  // polls of a flag-carrying input (~1 s) before giving up
 
 // ---------------------------------------------------------------------------
 // GEMV phase kernel
@@ -276,78 +275,6 @@ __host__ __device__ inline MmaLayout mma_layout(int cols, int max_rows) {
   return L;
 }
 
-// Self-attention of one query row and head over keys [0, T), T <= 64, by
-// one warp: the arithmetic of attn_self_kernel (lane j scores key j of each
-// 32-key chunk, warp softmax, lane l accumulates output dims 2l, 2l + 1),
-// with every load through L2 only (ld.global.cg): q and the newest key /
-// value were written by other CTAs of the running kernel.
-__device__ __forceinline__ float2 bf16x2_bits_to_float2(uint32_t v) {
-  return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
-}
-
-__device__ __forceinline__ void attn_warp_bf16(const __nv_bfloat16* q, const __nv_bfloat16* K,
-                                               const __nv_bfloat16* V, const float* bias, int T,
-                                               __nv_bfloat16* out, int lane, float* qs) {
-  const uint32_t qbits = __ldcg(reinterpret_cast<const unsigned int*>(q) + lane);
-  uint4 kr[8];
-#pragma unroll
-  for (int ch = 0; ch < 8; ++ch)
-    kr[ch] = lane < T ? __ldcg(reinterpret_cast<const uint4*>(K + (size_t)lane * 64) + ch) : make_uint4(0, 0, 0, 0);
-  const float bias0 = (bias && lane < T) ? bias[lane] : 0.f;
-  const float bias1 = (bias && 32 + lane < T) ? bias[32 + lane] : 0.f;
-  const float2 qv = bf16x2_bits_to_float2(qbits);
-  qs[2 * lane] = qv.x;
-  qs[2 * lane + 1] = qv.y;
-  __syncwarp();
-  float sc[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    const int j = c * 32 + lane;
-    if (c == 1) {
-      if (T <= 32) break;  // no second chunk of keys
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch)
-        kr[ch] = j < T ? __ldcg(reinterpret_cast<const uint4*>(K + (size_t)j * 64) + ch) : make_uint4(0, 0, 0, 0);
-    }
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-      float kf[8];
-      Vec16<__nv_bfloat16>::unpack(kr[ch], kf);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e & 3] = fmaf(qs[ch * 8 + e], kf[e], acc[e & 3]);
-    }
-    float a = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-    if (bias) a += (c == 0 ? bias0 : bias1);
-    sc[c] = j < T ? a : -INFINITY;
-  }
-  const float m = warp_max(fmaxf(sc[0], sc[1]));
-  const float p0 = lane < T ? expf(sc[0] - m) : 0.f;
-  const float p1 = 32 + lane < T ? expf(sc[1] - m) : 0.f;
-  const float l = warp_sum(p0 + p1);
-  float o0 = 0.f, o1 = 0.f;
-#pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    if (c * 32 >= T) break;  // keys past T add exact zeros
-    uint32_t vr[32];
-#pragma unroll
-    for (int jj = 0; jj < 32; ++jj) {
-      const int jv = c * 32 + jj;
-      vr[jj] = jv < T ? __ldcg(reinterpret_cast<const unsigned int*>(V + (size_t)jv * 64) + lane) : 0u;
-    }
-    const float pc = c == 0 ? p0 : p1;
-#pragma unroll
-    for (int jj = 0; jj < 32; ++jj) {
-      const float pw = __shfl_sync(0xffffffffu, pc, jj);
-      const float2 v = bf16x2_bits_to_float2(vr[jj]);
-      o0 = fmaf(pw, v.x, o0);
-      o1 = fmaf(pw, v.y, o1);
-    }
-  }
-  out[2 * lane] = __float2bfloat16_rn(o0 / l);
-  out[2 * lane + 1] = __float2bfloat16_rn(o1 / l);
-}
-
 // ---- thread-block cluster helpers (kGemvQKVCluster) ----------------------
 constexpr int kClusterRows = kQkvRowsPerHead / kQkvCluster;  // q/k/v rows per CTA
 // Shared memory appended to the GEMV layout: the new q, k, v of the (row,
@@ -397,14 +324,11 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
   uint8_t* cl_ext = smem + cluster_ext_offset(L.total);  // kGemvQKVCluster only
   float* cl_recv = reinterpret_cast<float*>(cl_ext + kClusterOffAttF);
   __shared__ float wred[8][BMAX];
-  __shared__ float rstd[BMAX];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, c = blockIdx.x;
-  // flag-carrying output words hold unit pairs: split at even units
-  const int upair = p.out_flag ? 2 : 1;
-  const int u0 = upair * (int)(((long long)c * (p.units / upair)) / G);
-  const int u1 = upair * (int)(((long long)(c + 1) * (p.units / upair)) / G);
+  const int u0 = (int)(((long long)c * p.units) / G);
+  const int u1 = (int)(((long long)(c + 1) * p.units) / G);
   const int R = (u1 - u0) * RPU;
   const int row_bytes = p.cols * 2;
   const int nchunk = p.cols >> 3;  // 16-byte chunks per row
@@ -445,80 +369,33 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
   // ---- every global load of this phase, issued back to back -------------
   // inputs: thread owns 16-byte chunks ch = tid + 256 i (i < 2: cols <= 4096)
   uint4 xin[BMAX][2];
-  bool ll_in = false;
-  if constexpr (BMAX <= 4) ll_in = p.x_flag != 0;
   // RMSNorm without a CTA-wide reduction (B <= 2, cols <= 1024, a multiple
   // of 256): every warp also loads the whole rows (L1 hits after the first
   // warp) and reduces the sum of squares with shuffles alone.
   constexpr int kWJ = 4;  // row chunks per lane
   constexpr int kWB = (NORM && BMAX <= 2) ? BMAX : 1;
   uint4 wx[kWB][kWJ];
-  const bool wnorm = NORM && BMAX <= 2 && !ll_in && (nchunk & 31) == 0 && nchunk <= 32 * kWJ;
-  if (!ll_in) {
-    pdl_wait();
+  const bool wnorm = NORM && BMAX <= 2 && (nchunk & 31) == 0 && nchunk <= 32 * kWJ;
+  pdl_wait();
 #pragma unroll
-    for (int b = 0; b < BMAX; ++b)
+  for (int b = 0; b < BMAX; ++b)
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int ch = tid + i * 256;
-        xin[b][i] = (b < p.B && ch < nchunk) ? *reinterpret_cast<const uint4*>(x_ptr + (size_t)b * p.x_stride + ch * 8)
-                                            : make_uint4(0, 0, 0, 0);
-      }
-    if constexpr (NORM && BMAX <= 2) {
-      if (wnorm) {
-#pragma unroll
-        for (int b = 0; b < kWB; ++b)
-#pragma unroll
-          for (int j = 0; j < kWJ; ++j) {
-            const int ch = lane + 32 * j;
-            wx[b][j] = (b < p.B && ch < nchunk)
-                           ? *reinterpret_cast<const uint4*>(x_ptr + (size_t)b * p.x_stride + ch * 8)
-                           : make_uint4(0, 0, 0, 0);
-          }
-      }
+    for (int i = 0; i < 2; ++i) {
+      const int ch = tid + i * 256;
+      xin[b][i] = (b < p.B && ch < nchunk) ? *reinterpret_cast<const uint4*>(x_ptr + (size_t)b * p.x_stride + ch * 8)
+                                          : make_uint4(0, 0, 0, 0);
     }
-  } else if constexpr (BMAX <= 4) {
-    // Poll the previous launch's flag-carrying words: chunk ch (8 values) is
-    // four 8-byte words = two 16-byte loads; every load is retried until all
-    // its flags read x_flag (L1 bypassed: the words are written while this
-    // launch runs). No dependency wait: this launch only reads data of the
-    // previous launch through these words, and older data, which the previous
-    // launch had fully seen before it let this launch start.
-    const uint32_t f = p.x_flag;
-    const uint4* xw = reinterpret_cast<const uint4*>(p.x);
-    const int wrow = p.x_stride >> 2;  // 16-byte loads per row (2 values each half)
-    uint4 lw[BMAX][2][2];
-    bool gave_up = *reinterpret_cast<volatile const int*>(p.err) & kErrCounterTimeout;
-    for (int it = 0; !gave_up; ++it) {
-      bool ok = true;
+  if constexpr (NORM && BMAX <= 2) {
+    if (wnorm) {
 #pragma unroll
-      for (int b = 0; b < BMAX; ++b)
+      for (int b = 0; b < kWB; ++b)
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int ch = tid + i * 256;
-          if (b < p.B && ch < nchunk) {
-            const uint4* src = xw + (size_t)b * wrow + 2 * ch;
-            lw[b][i][0] = __ldcv(src);
-            lw[b][i][1] = __ldcv(src + 1);
-            ok = ok && lw[b][i][0].y == f && lw[b][i][0].w == f && lw[b][i][1].y == f && lw[b][i][1].w == f;
-          }
+        for (int j = 0; j < kWJ; ++j) {
+          const int ch = lane + 32 * j;
+          wx[b][j] = (b < p.B && ch < nchunk) ? *reinterpret_cast<const uint4*>(x_ptr + (size_t)b * p.x_stride + ch * 8)
+                                              : make_uint4(0, 0, 0, 0);
         }
-      if (ok) break;
-      if (it >= kFlagSpinLimit) {
-        atomicOr(p.err, kErrCounterTimeout);
-        gave_up = true;
-      }
-      __nanosleep(64);  // back off: the polls share L2 bandwidth with the producer
     }
-#pragma unroll
-    for (int b = 0; b < BMAX; ++b)
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int ch = tid + i * 256;
-        xin[b][i] = (b < p.B && ch < nchunk)
-                        ? make_uint4(lw[b][i][0].x, lw[b][i][0].z, lw[b][i][1].x, lw[b][i][1].z)
-                        : make_uint4(0, 0, 0, 0);
-      }
   }
   // residual values of the epilogue (same thread -> (unit, row) mapping)
   const int nunits = u1 - u0;
@@ -531,7 +408,7 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
       if (idx < nunits * p.B) {
         const int uu = idx / p.B, b = idx - uu * p.B;
         const T* rp = reinterpret_cast<const T*>(p.resid) + (size_t)b * p.resid_stride + u0 + uu;
-        resv[i] = ll_in ? __bfloat162float(__ldcg(rp)) : to_f(*rp);
+        resv[i] = to_f(*rp);
       }
     }
   }
@@ -746,34 +623,6 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
   __syncthreads();
 
   // ---- cross-warp reduction + fused epilogue: one thread per (unit, row b)
-  if (MODE == kGemvGeglu && p.out_flag) {
-    // flag-carrying output: one thread per (unit pair, row b) writes one
-    // 8-byte word (bf16 pair, flag)
-    for (int idx = tid; idx < (nunits >> 1) * p.B; idx += 256) {
-      const int pu = idx / p.B, b = idx - pu * p.B;
-      float val[2];
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        float v2[2];
-#pragma unroll
-        for (int qq = 0; qq < 2; ++qq) {
-          const int rr = (2 * pu + q) * 2 + qq;
-          const int nt = rr >> 3, col = rr & 7;
-          float sacc = 0.f;
-#pragma unroll
-          for (int w = 0; w < 8; ++w) sacc += red[((w * 8 + nt) * 8 + col) * BMAX + b];
-          v2[qq] = sacc;
-        }
-        val[q] = __fmul_rn(gelu_approx<T>(rnd<T>(v2[0])), rnd<T>(v2[1]));
-      }
-      const __nv_bfloat162 pr = __floats2bfloat162_rn(val[0], val[1]);
-      uint32_t* dst = reinterpret_cast<uint32_t*>(p.out) + 2 * ((size_t)b * (p.out_stride >> 1) + ((u0 >> 1) + pu));
-      asm volatile("st.global.v2.u32 [%0], {%1, %2};" ::"l"(dst), "r"(*reinterpret_cast<const uint32_t*>(&pr)),
-                   "r"(p.out_flag)
-                   : "memory");
-    }
-    return;
-  }
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const int idx = tid + i * 256;
@@ -899,66 +748,20 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
       out[2 * lane + 1] = from_f<T>(o1 / l);
     }
   }
-  if constexpr (MODE == kGemvQKVAttn) {
-    // Arrival ticket per head: this CTA adds the number of that head's
-    // q/k/v rows it produced; the CTA that brings a head to 3 x 64 rows
-    // runs the head's attention for every batch row (warp b -> row b).
-    __shared__ int att_heads[4];
-    __shared__ int att_n;
-    __syncthreads();  // every epilogue store of the CTA is issued
-    if (tid == 0) {
-      int hs[4], cnt[4], nh = 0;
-      for (int u = u0; u < u1; ++u) {
-        const int h = u / kQkvRowsPerHead;
-        int k = 0;
-        while (k < nh && hs[k] != h) ++k;
-        if (k == nh) {
-          if (nh == 4) break;  // unreachable: a CTA holds <= 32 consecutive rows
-          hs[nh] = h;
-          cnt[nh] = 0;
-          ++nh;
-        }
-        ++cnt[k];
-      }
-      __threadfence();  // release this CTA's q/k/v stores before the tickets
-      int na = 0;
-      for (int k = 0; k < nh; ++k)
-        if (atomicAdd(&p.counters[hs[k]], cnt[k]) + cnt[k] == 3 * 64) {
-          att_heads[na++] = hs[k];
-          p.counters[hs[k]] = 0;  // complete; the next use is a later launch
-        }
-      __threadfence();  // acquire: the head's rows from other CTAs are visible
-      att_n = na;
-    }
-    __syncthreads();
-    float* qs = reinterpret_cast<float*>(wsm) + warp * 64;  // the weights are consumed
-    for (int i = 0; i < att_n; ++i) {
-      const int h = att_heads[i];
-      if (warp < p.B) {
-        const size_t base = (((size_t)warp * p.H + h) * p.cap) * 64;
-        attn_warp_bf16(reinterpret_cast<const T*>(p.out) + (size_t)warp * p.out_stride + h * 64,
-                       reinterpret_cast<const T*>(p.kc) + base, reinterpret_cast<const T*>(p.vc) + base,
-                       p.bias ? p.bias + (size_t)h * p.bias_stride : nullptr, p.pos + 1,
-                       reinterpret_cast<T*>(p.attn_out) + (size_t)warp * p.inner + h * 64, lane, qs);
-      }
-      __syncwarp();
-    }
-  }
 }
 
 // Grid for the tensor-core GEMV: at least one CTA per SM when there are
 // enough units, and no CTA with more rows than fit its shared memory.
-static void mma_plan(int units, int rpu, int cols, int num_sms, int* grid, int* max_rows, int upair = 1) {
+static void mma_plan(int units, int rpu, int cols, int num_sms, int* grid, int* max_rows) {
   const int rstride = cols * 2 + 16;
   int cap_rows = (190 * 1024) / rstride;
   cap_rows = min(cap_rows, kMmaMaxRows);
-  cap_rows -= cap_rows % (rpu * upair);
-  const int groups = units / upair;  // units are split in groups of upair
-  int G = min(groups, num_sms);
+  cap_rows -= cap_rows % rpu;
+  int G = min(units, num_sms);
   const int need = (units * rpu + cap_rows - 1) / cap_rows;
   if (need > G) G = need;
   *grid = G;
-  *max_rows = ((groups + G - 1) / G) * upair * rpu;
+  *max_rows = ((units + G - 1) / G) * rpu;
 }
 
 template <int BMAX, int NT, bool NORM, int MODE>
@@ -1002,9 +805,7 @@ static cudaError_t launch_mma_cluster(const GemvParams& p, cudaStream_t s, bool 
 template <int BMAX, bool NORM, int MODE>
 static cudaError_t launch_mma_t(const GemvParams& p, int num_sms, cudaStream_t s, bool pdl) {
   int grid, max_rows;
-  if (p.out_flag && (MODE != kGemvGeglu || BMAX > 4 || p.units % 2)) return cudaErrorInvalidValue;
-  if (p.x_flag && (BMAX > 4 || p.x_stride % 8)) return cudaErrorInvalidValue;
-  mma_plan(p.units, MODE == kGemvGeglu ? 2 : 1, p.cols, num_sms, &grid, &max_rows, p.out_flag ? 2 : 1);
+  mma_plan(p.units, MODE == kGemvGeglu ? 2 : 1, p.cols, num_sms, &grid, &max_rows);
   if (max_rows > kMmaMaxRows || grid <= 0) return cudaErrorInvalidValue;
   switch ((max_rows + 7) / 8) {
     case 1: return launch_mma_nt<BMAX, 1, NORM, MODE>(p, grid, max_rows, s, pdl);
@@ -1025,9 +826,6 @@ static cudaError_t launch_gemv_mma_b(int mode, bool norm, const GemvParams& p, i
                   : launch_mma_t<BMAX, false, kGemvResid>(p, num_sms, s, pdl);
     case kGemvQKV:
       return launch_mma_t<BMAX, true, kGemvQKV>(p, num_sms, s, pdl);
-    case kGemvQKVAttn:
-      if (p.pos + 1 > kSelfAttnMaxT || !p.counters || !p.attn_out || p.inner % 64 != 0) return cudaErrorInvalidValue;
-      return launch_mma_t<BMAX, true, kGemvQKVAttn>(p, num_sms, s, pdl);
     case kGemvQKVCluster:
       return launch_mma_cluster<BMAX>(p, s, pdl);
     case kGemvGeglu:
@@ -1057,7 +855,6 @@ static cudaError_t set_mma_limits_bn() {
   set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvResid>);
   set((const void*)gemv_mma_kernel<BMAX, NT, false, kGemvResid>);
   set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvQKV>);
-  set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvQKVAttn>);
   if (NT == 3) set((const void*)gemv_mma_kernel<BMAX, 3, true, kGemvQKVCluster>);
   set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvGeglu>);
   set((const void*)gemv_mma_kernel<BMAX, NT, true, kGemvLogits>);
@@ -1582,7 +1379,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
     float best = -INFINITY;
     int bi = 0x7fffffff;
     const float* uni = p.uniforms ? p.uniforms + (size_t)seq * p.uni_seq_stride : nullptr;
-    const uint64_t seed = p.seeds[seq];
+    const uint64_t seed = p.seeds ? p.seeds[seq] : p.seed_value;
     for (int i = tid; i < n; i += kSampleThreads) {
       float v = vals[i];
       if (p.temperature != 0.0f) {
@@ -1611,16 +1408,18 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
       best = rv[0];
       bi = ri[0];
       for (int w = 1; w < kSampleThreads / 32; ++w) argmax_combine(best, bi, rv[w], ri[w]);
-      tok_s = p.lo + (bi == 0x7fffffff ? 0 : bi);
+      tok_s = bi == 0x7fffffff ? -1 : p.lo + bi;  // -1: no candidate survived (NaN logits, empty range)
     }
     __syncthreads();
     token = tok_s;
   }
+  int out_token = token;
   if (token < 0 || token >= p.V) {
-    if (tid == 0) atomicOr(p.err, kErrBadToken);
-    token = 0;
+    if (tid == 0 && p.err) atomicOr(p.err, kErrBadToken);
+    out_token = p.bad_token;
+    token = 0;  // the embedding rows stay defined
   }
-  if (tid == 0 && p.tokens) p.tokens[(size_t)seq * p.tok_stride + p.tok_index] = token;
+  if (tid == 0 && p.tokens) p.tokens[(size_t)seq * p.tok_stride + p.tok_index] = out_token;
 
   // embedding feedback, 16 bytes per thread per row
   const uint4* e = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.emb) + (size_t)token * p.d);
@@ -1678,14 +1477,14 @@ cudaError_t launch_sample(int dtype, const SampleParams& p, int num_seq, cudaStr
 }
 
 // ---------------------------------------------------------------------------
-// Allocation-free sampling (mrtdf_sample_noalloc): the sampler's scratch -
-// the seed word, the error word and the three embedding-feedback rows it
-// writes - lives in this fixed device array instead of cudaMalloc'd buffers.
-// Every GPU that loads the library holds these 64 KiB until process exit;
-// all calls on a device share them, so calls that overlap on the GPU race.
-// Nothing in it has to start at zero: each call zeroes the error word and
-// writes the seed (stream-ordered, before its kernel), and the kernel writes
-// the feedback rows without reading them (first level, not last).
+// Allocation-free sampling (mrtdf_sample_noalloc): the three
+// embedding-feedback rows the sampler writes live in this fixed device array
+// instead of cudaMalloc'd buffers. Every GPU that loads the library holds
+// these 64 KiB until process exit; all calls on a device share them, so
+// calls that overlap on the GPU race. Nothing in it has to start at zero:
+// the kernel writes the feedback rows without reading them (first level, not
+// last). The seed travels by value in the launch parameters and a failed
+// draw is reported through the token itself (-1), so no word here is read.
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) unsigned char g_sample_scratch[kSampleScratchBytes];
 
@@ -1709,6 +1508,26 @@ cudaError_t sample_scratch_address(int device, void** out) {
   }
   *out = addr[device];
   return cudaSuccess;
+}
+
+// ---------------------------------------------------------------------------
+// Failure-detection check: the production bounded wait on an mbarrier whose
+// phase never completes (count 1, no arrival, no copy in flight), with a
+// caller-chosen bound. The CTA gives up, reports kErrMbarTimeout and exits.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(32) wait_timeout_probe_kernel(int* err, unsigned long long timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_bounded(&bar, 0, err, timeout_ns);
+}
+
+cudaError_t launch_wait_timeout_probe(int* err, unsigned long long timeout_ns, cudaStream_t s) {
+  wait_timeout_probe_kernel<<<1, 32, 0, s>>>(err, timeout_ns);
+  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------

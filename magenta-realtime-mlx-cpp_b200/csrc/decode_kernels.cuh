@@ -15,8 +15,6 @@ enum GemvMode : int {
   kGemvQKV = 2,     // fused q/k/v: q -> out, k/v -> cache at `pos`
   kGemvGeglu = 3,   // unit = (wi_0 row, wi_1 row): out[b, u] = R(gelu(R(a)) * R(b))
   kGemvLogits = 4,  // float out[b, off + u] = R(acc)
-  kGemvQKVAttn = 5, // kGemvQKV + the self-attention of each head, run by the
-                    // CTA whose q/k/v rows complete that head (bf16 only)
   kGemvQKVCluster = 6,  // kGemvQKV on one thread-block cluster per head; the
                         // head's attention runs inside the cluster (bf16 only)
 };
@@ -41,19 +39,11 @@ struct GemvParams {
   int out_offset;
   int inner, H, cap, pos;  // kGemvQKV
   int l2_keep;             // 1: keep these weights in L2 (evict_last), 0: stream them (evict_first)
-  // kGemvQKVAttn: relative-position bias of this query (H, bias_stride) or
-  // null, attention output (B, inner), per-head arrival counters (H, zero
-  // between launches)
+  // kGemvQKVCluster: relative-position bias of this query (H, bias_stride)
+  // or null, attention output (B, inner)
   const float* bias;
   int bias_stride;
   void* attn_out;
-  int* counters;
-  // Flag-carrying activations (B <= 4, bf16): x_flag != 0 -> x is stored as
-  // 8-byte words (bf16 pair, 32-bit flag) written by the previous launch,
-  // which this launch polls for x_flag instead of waiting for that launch to
-  // complete; out_flag != 0 -> the GEGLU output is written that way.
-  uint32_t x_flag;
-  uint32_t out_flag;
 };
 
 // Bytes of one TMA stage of the GEMV kernel and the number of stages.
@@ -97,7 +87,8 @@ struct SampleParams {
   int rows_per_seq;      // 2 with CFG, else 1
   float w, temperature;
   int top_k;
-  const uint64_t* seeds;  // per sequence
+  const uint64_t* seeds;  // per sequence, or null: every sequence uses seed_value
+  uint64_t seed_value;
   uint32_t step;          // frame * rvq_depth + level
   const float* uniforms;  // optional draws: this step's row of V for sequence 0
   long long uni_seq_stride;  // floats between the rows of consecutive sequences
@@ -111,6 +102,11 @@ struct SampleParams {
   void* tin;              // (B, d) next temporal input (written on the last level)
   int depth;
   int is_first, is_last;
+  // When no candidate can be chosen (every candidate NaN or -inf, an empty
+  // range) or a forced id is outside [0, V): the kErrBadToken bit goes to
+  // *err (when err is not null), `bad_token` is stored as the token and id 0
+  // feeds the embedding rows.
+  int bad_token;
   int* err;
 };
 cudaError_t launch_sample(int dtype, const SampleParams& p, int num_seq, cudaStream_t s, bool pdl);
@@ -118,13 +114,16 @@ size_t sample_smem_bytes(int n_candidates);
 cudaError_t sample_set_smem_limits();
 constexpr int kSampleMaxSmem = 160 * 1024;
 
-// Fixed device scratch of the allocation-free sampler: 256 bytes of words
-// (seed at 0, error word at 8) then three feedback rows of up to
-// kSampleScratchRowBytes each.
+// Fixed device scratch of the allocation-free sampler: a 256-byte header
+// (reserved) then three feedback rows of up to kSampleScratchRowBytes each.
 constexpr size_t kSampleScratchBytes = 64 * 1024;
 constexpr size_t kSampleScratchRowBytes = (kSampleScratchBytes - 256) / 3 / 256 * 256;
 // Device address of that scratch on `device` (looked up once per device).
 cudaError_t sample_scratch_address(int device, void** out);
+
+// One CTA waiting on an mbarrier that nothing completes, bounded by
+// timeout_ns: sets kErrMbarTimeout in *err (failure-detection check).
+cudaError_t launch_wait_timeout_probe(int* err, unsigned long long timeout_ns, cudaStream_t s);
 
 // out[r, :] = emb[ids[r], :] for r < rows (ids == null: id 0 = PAD).
 cudaError_t launch_embed_rows(int dtype, const void* emb, const int32_t* ids, int rows, int d, void* out,

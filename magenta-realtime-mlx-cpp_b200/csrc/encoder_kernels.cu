@@ -7,8 +7,9 @@
 //                        attention, no mask, no bias, scale 1.0; gated FFN)
 //   project_kv           modules.cpp:323-333 (cross K/V, done for all 20
 //                        temporal layers in one GEMM with N = Lt * 2 * inner)
-// bf16 GEMMs run on the tensor cores (mma.sync m16n8k16, fp32 accumulate);
-// fp32 runs on the CUDA cores so the fp32 parity mode stays exact fp32.
+// bf16 GEMMs run on tcgen05 (gemm_tc.cu); the fp32 GEMM here runs on the
+// CUDA cores so the fp32 parity mode stays exact fp32. The encoder attention
+// uses mma.sync m16n8k16 with fp32 accumulation.
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -20,7 +21,7 @@ namespace mrtdf {
 typedef __nv_bfloat16 bf16;
 
 // ---------------------------------------------------------------------------
-// PTX helpers for the mma.sync path
+// PTX helpers of the encoder attention (cp.async, ldmatrix, mma.sync)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
   const int src = pred ? 16 : 0;
@@ -52,98 +53,6 @@ __device__ __forceinline__ void mma_bf16(float* c, const uint32_t* a, uint32_t b
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
-}
-
-// ---------------------------------------------------------------------------
-// bf16 GEMM, C = A W^T: 128x128x32 CTA tile, 8 warps (2 x 4), warp tile
-// 64x32, 3-stage cp.async pipeline, XOR-swizzled shared tiles read with
-// ldmatrix, mma.sync m16n8k16 with fp32 accumulators.
-// ---------------------------------------------------------------------------
-constexpr int kGBM = 128, kGBN = 128, kGBK = 32, kGStages = 3;
-constexpr int kGemmSmem = kGStages * (kGBM + kGBN) * kGBK * 2;
-
-__device__ __forceinline__ int swz(int row, int chunk) { return row * kGBK + ((chunk ^ ((row >> 1) & 3)) << 3); }
-
-template <int EPI>
-__global__ void __launch_bounds__(256) gemm_bf16_kernel(const GemmParams p) {
-  extern __shared__ __align__(128) uint8_t gsm[];
-  bf16* sA = reinterpret_cast<bf16*>(gsm);
-  bf16* sB = sA + kGStages * kGBM * kGBK;
-  pdl_launch_dependents();
-  pdl_wait();
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int bm = blockIdx.y * kGBM, bn = blockIdx.x * kGBN;
-  const int wm0 = (warp >> 2) * 64, wn0 = (warp & 3) * 32;
-  const bf16* A = reinterpret_cast<const bf16*>(p.A);
-  const bf16* W = reinterpret_cast<const bf16*>(p.W);
-  const int KT = p.K / kGBK;
-
-  auto load = [&](int stage, int kt) {
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int id = tid + i * 256;
-      const int row = id >> 2, ch = id & 3;
-      const int gm = bm + row, gn = bn + row;
-      const bf16* srcA = A + (size_t)min(gm, p.M - 1) * p.lda + kt * kGBK + ch * 8;
-      const bf16* srcB = W + (size_t)min(gn, p.N - 1) * p.K + kt * kGBK + ch * 8;
-      cp_async16(sA + stage * kGBM * kGBK + swz(row, ch), srcA, gm < p.M);
-      cp_async16(sB + stage * kGBN * kGBK + swz(row, ch), srcB, gn < p.N);
-    }
-  };
-
-  float acc[4][4][4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) acc[i][j][k] = 0.f;
-
-#pragma unroll
-  for (int s = 0; s < kGStages - 1; ++s) {
-    if (s < KT) load(s, s);
-    cp_async_commit();
-  }
-  for (int kt = 0; kt < KT; ++kt) {
-    cp_async_wait<kGStages - 2>();
-    __syncthreads();
-    const int nk = kt + kGStages - 1;
-    if (nk < KT) load(nk % kGStages, nk);
-    cp_async_commit();
-    const bf16* a_s = sA + (kt % kGStages) * kGBM * kGBK;
-    const bf16* b_s = sB + (kt % kGStages) * kGBN * kGBK;
-#pragma unroll
-    for (int kk = 0; kk < 2; ++kk) {
-      uint32_t af[4][4], bfr[4][2];
-#pragma unroll
-      for (int mi = 0; mi < 4; ++mi) {
-        const int row = wm0 + mi * 16 + (lane & 15);
-        const int ch = kk * 2 + (lane >> 4);
-        ldsm_x4(af[mi][0], af[mi][1], af[mi][2], af[mi][3], a_s + swz(row, ch));
-      }
-#pragma unroll
-      for (int nj = 0; nj < 2; ++nj) {
-        const int row = wn0 + nj * 16 + (lane & 7) + ((lane >> 4) << 3);
-        const int ch = kk * 2 + ((lane >> 3) & 1);
-        ldsm_x4(bfr[2 * nj][0], bfr[2 * nj][1], bfr[2 * nj + 1][0], bfr[2 * nj + 1][1], b_s + swz(row, ch));
-      }
-#pragma unroll
-      for (int mi = 0; mi < 4; ++mi)
-#pragma unroll
-        for (int ni = 0; ni < 4; ++ni) mma_bf16(acc[mi][ni], af[mi], bfr[ni][0], bfr[ni][1]);
-    }
-  }
-  cp_async_wait<0>();
-  const int g = lane >> 2, t = lane & 3;
-#pragma unroll
-  for (int mi = 0; mi < 4; ++mi)
-#pragma unroll
-    for (int ni = 0; ni < 4; ++ni) {
-      const int r0 = bm + wm0 + mi * 16 + g;
-      const int cn = bn + wn0 + ni * 8 + 2 * t;
-      epi_pair<bf16, EPI>(p, r0, cn, acc[mi][ni][0], acc[mi][ni][1]);
-      epi_pair<bf16, EPI>(p, r0 + 8, cn, acc[mi][ni][2], acc[mi][ni][3]);
-    }
 }
 
 // ---------------------------------------------------------------------------
@@ -208,39 +117,15 @@ static cudaError_t launch_k(void (*kern)(const P), dim3 grid, dim3 block, size_t
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-cudaError_t gemm_set_smem_limits() {
-  cudaError_t e = cudaSuccess;
-  auto set = [&](const void* f) {
-    cudaError_t r = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
-    if (r != cudaSuccess) e = r;
-  };
-  set((const void*)gemm_bf16_kernel<kEpiStore>);
-  set((const void*)gemm_bf16_kernel<kEpiResid>);
-  set((const void*)gemm_bf16_kernel<kEpiGeglu>);
-  set((const void*)gemm_bf16_kernel<kEpiCrossKV>);
-  return e;
-}
-
-cudaError_t launch_gemm(int dtype, int epi, const GemmParams& p, cudaStream_t s, bool pdl) {
+cudaError_t launch_gemm_f32(int epi, const GemmParams& p, cudaStream_t s, bool pdl) {
   if (p.M <= 0 || p.N <= 0) return cudaSuccess;
   if (p.N % 2 != 0) return cudaErrorInvalidValue;
-  if (dtype == 1) {
-    if (p.K % kGBK != 0 || p.lda % 8 != 0) return cudaErrorInvalidValue;
-    const dim3 grid((p.N + kGBN - 1) / kGBN, (p.M + kGBM - 1) / kGBM);
-    switch (epi) {
-      case kEpiStore: return launch_k(gemm_bf16_kernel<kEpiStore>, grid, dim3(256), kGemmSmem, s, pdl, p);
-      case kEpiResid: return launch_k(gemm_bf16_kernel<kEpiResid>, grid, dim3(256), kGemmSmem, s, pdl, p);
-      case kEpiGeglu: return launch_k(gemm_bf16_kernel<kEpiGeglu>, grid, dim3(256), kGemmSmem, s, pdl, p);
-      case kEpiCrossKV: return launch_k(gemm_bf16_kernel<kEpiCrossKV>, grid, dim3(256), kGemmSmem, s, pdl, p);
-    }
-  } else {
-    const dim3 grid((p.N + 63) / 64, (p.M + 63) / 64);
-    switch (epi) {
-      case kEpiStore: return launch_k(gemm_f32_kernel<kEpiStore>, grid, dim3(256), 0, s, pdl, p);
-      case kEpiResid: return launch_k(gemm_f32_kernel<kEpiResid>, grid, dim3(256), 0, s, pdl, p);
-      case kEpiGeglu: return launch_k(gemm_f32_kernel<kEpiGeglu>, grid, dim3(256), 0, s, pdl, p);
-      case kEpiCrossKV: return launch_k(gemm_f32_kernel<kEpiCrossKV>, grid, dim3(256), 0, s, pdl, p);
-    }
+  const dim3 grid((p.N + 63) / 64, (p.M + 63) / 64);
+  switch (epi) {
+    case kEpiStore: return launch_k(gemm_f32_kernel<kEpiStore>, grid, dim3(256), 0, s, pdl, p);
+    case kEpiResid: return launch_k(gemm_f32_kernel<kEpiResid>, grid, dim3(256), 0, s, pdl, p);
+    case kEpiGeglu: return launch_k(gemm_f32_kernel<kEpiGeglu>, grid, dim3(256), 0, s, pdl, p);
+    case kEpiCrossKV: return launch_k(gemm_f32_kernel<kEpiCrossKV>, grid, dim3(256), 0, s, pdl, p);
   }
   return cudaErrorInvalidValue;
 }

@@ -39,8 +39,8 @@ struct GemmParams {
   int max_ksplit;
 };
 
-cudaError_t launch_gemm(int dtype, int epi, const GemmParams& p, cudaStream_t s, bool pdl);
-cudaError_t gemm_set_smem_limits();
+// fp32 GEMM on the CUDA cores (the fp32 parity mode).
+cudaError_t launch_gemm_f32(int epi, const GemmParams& p, cudaStream_t s, bool pdl);
 // bf16 GEMM on tcgen05 tensor cores with TMA-fed operands (gemm_tc.cu).
 cudaError_t launch_gemm_tc(int epi, const GemmParams& p, int* err, cudaStream_t s, bool pdl);
 cudaError_t gemm_tc_set_smem_limits();

@@ -86,20 +86,12 @@ struct mrtdf_engine {
   int esize = 2;  // bytes per element of the compute dtype
   bool loaded = false;
   bool pdl = true;
-  bool tc_gemm = true;  // encoder GEMMs on tcgen05 (MRTDF_TC_GEMM=0 selects mma.sync)
-  // bf16 decode self-attention inside the q/k/v kernel (MRTDF_FUSE_ATTN=1).
-  // Off by default: its per-head arrival tickets and the attention's loads
-  // add ~4 dependent L2 round trips to the q/k/v kernel, which measured
-  // slower than the separate attention launch.
-  bool fuse_attn = false;
   // bf16 decode self-attention inside a thread-block cluster per head that
   // also computes the head's q/k/v rows (MRTDF_CLUSTER_ATTN=0: separate kernel)
   bool cluster_attn = true;
   // wide streams: largest split-K cluster of the tcgen05 decode GEMMs
   // (MRTDF_WIDE_KSPLIT; 64 CFG pairs: 607 ms per chunk unsplit, 504 ms at 8)
   int wide_ksplit = 8;
-  // flag-carrying activations on the FFN-up -> FFN-down edge (MRTDF_LL)
-  bool flag_acts = false;
   Arena weights;
   void* emb = nullptr;
   void* enc_norm = nullptr;
@@ -140,11 +132,6 @@ struct mrtdf_stream {
   int32_t* tokens;  // (nseq, Tmax, depth)
   uint64_t* seeds;  // (nseq)
   int32_t* forced;  // (nseq)
-  int* head_cnt;  // (H) arrival counters of the fused q/k/v + attention kernel
-  // flag-carrying FFN hidden rows (hb as (bf16 pair, flag) words): the
-  // FFN-down launch polls them instead of waiting for the FFN-up launch
-  bool ll = false;
-  uint32_t ll_ctr = 0;
   int* err;
   float* uniforms = nullptr;
   size_t uniforms_cap = 0;
@@ -411,7 +398,7 @@ void gemv(mrtdf_stream* st, int mode, bool norm, GemvParams p) {
   double bytes = (double)p.units * rpu * p.cols * es + (double)p.B * p.cols * es;
   bytes += (double)p.B * p.units * (mode == kGemvLogits ? 4.0 : es) * (mode == kGemvResid ? 2.0 : 1.0);
   if (norm) bytes += (double)p.cols * es;
-  if (mode == kGemvQKVAttn || mode == kGemvQKVCluster)
+  if (mode == kGemvQKVCluster)
     bytes += 2.0 * p.B * p.H * (p.pos + 1) * 64.0 * es;  // fused attention's K/V reads
   st->gemv_launches += 1;
   st->gemv_bytes += bytes;
@@ -442,9 +429,6 @@ void enqueue_decoder_layer(mrtdf_stream* st, const DecLayerDev& L, const void* x
   if (E->cluster_attn && c.dtype == MRTDF_DTYPE_BF16 && st->B <= kQkvCluster) {
     p.bias = bias; p.bias_stride = bias_stride; p.attn_out = st->ao;
     gemv(st, kGemvQKVCluster, true, p);
-  } else if (E->fuse_attn && c.dtype == MRTDF_DTYPE_BF16 && st->B <= kGemvMaxB) {
-    p.bias = bias; p.bias_stride = bias_stride; p.attn_out = st->ao; p.counters = st->head_cnt;
-    gemv(st, kGemvQKVAttn, true, p);
   } else {
     gemv(st, kGemvQKV, true, p);
     AttnParams a{};
@@ -479,18 +463,11 @@ void enqueue_decoder_layer(mrtdf_stream* st, const DecLayerDev& L, const void* x
   p = GemvParams{};
   p.W = L.wi; p.x = xr; p.norm_w = L.n_ffn; p.out = st->hb; p.units = ff; p.cols = d; p.x_stride = d;
   p.out_stride = ff; p.l2_keep = l2_keep;
-  uint32_t hb_flag = 0;
-  if (st->ll) {
-    if (++st->ll_ctr == 0) st->ll_ctr = 1;  // 0 means "plain rows"
-    hb_flag = st->ll_ctr;
-  }
-  p.out_flag = hb_flag;
   gemv(st, kGemvGeglu, true, p);
   // 8. wo + residual
   p = GemvParams{};
   p.W = L.wout; p.x = st->hb; p.out = xr; p.resid = xr; p.units = d; p.cols = ff; p.x_stride = ff;
   p.out_stride = d; p.resid_stride = d; p.l2_keep = l2_keep;
-  p.x_flag = hb_flag;
   gemv(st, kGemvResid, false, p);
 }
 
@@ -538,8 +515,8 @@ void enqueue_depth(mrtdf_stream* st, int level, const void* x_in, int lo, int hi
 // temporal layer (model.cpp:226-241, modules.cpp:323-333).
 cudaError_t encoder_gemm(mrtdf_stream* st, int epi, const GemmParams& g) {
   mrtdf_engine* E = st->eng;
-  if (E->tc_gemm && E->c.dtype == MRTDF_DTYPE_BF16) return launch_gemm_tc(epi, g, st->err, st->s, E->pdl);
-  return launch_gemm(E->c.dtype, epi, g, st->s, E->pdl);
+  if (E->c.dtype == MRTDF_DTYPE_BF16) return launch_gemm_tc(epi, g, st->err, st->s, E->pdl);
+  return launch_gemm_f32(epi, g, st->s, E->pdl);
 }
 
 void enqueue_encode(mrtdf_stream* st, int S) {
@@ -591,6 +568,7 @@ void enqueue_sample(mrtdf_stream* st, int f, int level, const mrtdf_gen_opts& o,
   sp.tokens = st->tokens; sp.tok_stride = c.max_frames * c.rvq_depth; sp.tok_index = f * c.rvq_depth + level;
   sp.emb = E->emb; sp.d = c.d_model; sp.V = c.vocab_size; sp.din = st->din; sp.fsum = st->fsum; sp.tin = st->tin;
   sp.depth = c.rvq_depth; sp.is_first = level == 0; sp.is_last = level == c.rvq_depth - 1; sp.err = st->err;
+  sp.bad_token = 0;
   (void)masked;
   check_cuda(launch_sample(c.dtype, sp, st->nseq, st->s, E->pdl), "sample launch");
 }
@@ -683,7 +661,10 @@ void check_device_err(mrtdf_stream* st) {
   const int h = read_err(st);
   if (h & (kErrMbarTimeout | kErrCounterTimeout))
     throw Error{MRTDF_ERR_TIMEOUT, "a device-side bounded wait gave up (error word " + std::to_string(h) + ")"};
-  if (h & kErrBadToken) throw Error{MRTDF_ERR_INVALID, "a token id outside the vocabulary reached the sampler"};
+  if (h & kErrBadToken)
+    throw Error{MRTDF_ERR_INVALID,
+                "the sampler found no valid candidate (NaN logits or an empty vocabulary range) or an id outside the "
+                "vocabulary"};
 }
 
 void run_chunk(mrtdf_stream* st, int S, const mrtdf_gen_opts& o) {
@@ -777,13 +758,9 @@ int mrtdf_create(const mrtdf_config* cfg, int device, mrtdf_engine** out) {
     E->num_sms = prop.multiProcessorCount;
     E->esize = cfg->dtype == MRTDF_DTYPE_BF16 ? 2 : 4;
     E->pdl = env_flag("MRTDF_PDL", true);
-    E->tc_gemm = env_flag("MRTDF_TC_GEMM", true);
-    E->fuse_attn = env_flag("MRTDF_FUSE_ATTN", false);
     E->cluster_attn = env_flag("MRTDF_CLUSTER_ATTN", true);
-    E->flag_acts = env_flag("MRTDF_LL", false);
     if (const char* v = std::getenv("MRTDF_WIDE_KSPLIT")) E->wide_ksplit = std::max(1, std::min(8, std::atoi(v)));
     CUDA_OK(gemv_set_smem_limits());
-    CUDA_OK(gemm_set_smem_limits());
     CUDA_OK(gemm_tc_set_smem_limits());
     CUDA_OK(sample_set_smem_limits());
     *out = E.release();
@@ -856,7 +833,6 @@ int mrtdf_stream_create(mrtdf_engine* E, int num_sequences, int cfg, mrtdf_strea
     st->nseq = num_sequences;
     st->rps = rps;
     st->B = num_sequences * rps;
-    st->ll = E->flag_acts && E->c.dtype == MRTDF_DTYPE_BF16 && st->B <= 4;
     CUDA_OK(cudaStreamCreateWithFlags(&st->s, cudaStreamNonBlocking));
     const size_t B = st->B, d = c.d_model, in = E->inner(), ff = c.d_ff, V = c.vocab_size, H = c.num_heads;
     const size_t es = E->esize;
@@ -875,7 +851,6 @@ int mrtdf_stream_create(mrtdf_engine* E, int num_sequences, int cfg, mrtdf_strea
         {&st->eh, Mx * ff * es}, {(void**)&st->ids, Mx * 4}, {&st->xn, B * d * es},
         {(void**)&st->tokens, (size_t)num_sequences * c.max_frames * c.rvq_depth * 4},
         {(void**)&st->seeds, (size_t)num_sequences * 8}, {(void**)&st->forced, (size_t)num_sequences * 4},
-        {(void**)&st->head_cnt, H * 4},
         {(void**)&st->err, 64}};
     size_t total = 0;
     for (auto& p : plan) total += (p.second + 255) & ~(size_t)255;
@@ -901,6 +876,17 @@ int mrtdf_stream_destroy(mrtdf_stream* st) {
 int mrtdf_stream_rows(const mrtdf_stream* st) { return st ? st->B : 0; }
 
 void* mrtdf_stream_cuda(mrtdf_stream* st) { return st ? (void*)st->s : nullptr; }
+
+int mrtdf_check_wait_timeout(mrtdf_stream* st, int timeout_us) {
+  return guarded([&] {
+    if (!st) throw Error{MRTDF_ERR_INVALID, "NULL stream"};
+    if (timeout_us < 1 || timeout_us > 1000000) throw Error{MRTDF_ERR_RANGE, "timeout_us must be in [1, 1e6]"};
+    CUDA_OK(cudaSetDevice(st->eng->device));
+    check_cuda(launch_wait_timeout_probe(st->err, (unsigned long long)timeout_us * 1000ull, st->s), "probe launch");
+    CUDA_OK(cudaStreamSynchronize(st->s));
+    check_device_err(st);
+  });
+}
 
 int mrtdf_stream_sync(mrtdf_stream* st) {
   return guarded([&] {
@@ -1034,12 +1020,10 @@ int mrtdf_sample(mrtdf_engine* E, const float* logits, int cfg, int frame, int l
     const int rows = cfg ? 2 : 1;
     const size_t V = c.vocab_size, d = c.d_model;
     float *dl = nullptr, *du = nullptr;
-    uint64_t* ds = nullptr;
     int32_t* dt = nullptr;
     void *din = nullptr, *fs = nullptr, *tin = nullptr;
     int* err = nullptr;
     CUDA_OK(cudaMalloc(&dl, rows * V * 4));
-    CUDA_OK(cudaMalloc(&ds, 8));
     CUDA_OK(cudaMalloc(&dt, 4));
     CUDA_OK(cudaMalloc(&din, rows * d * E->esize));
     CUDA_OK(cudaMalloc(&fs, rows * d * E->esize));
@@ -1047,7 +1031,6 @@ int mrtdf_sample(mrtdf_engine* E, const float* logits, int cfg, int frame, int l
     CUDA_OK(cudaMalloc(&err, 4));
     CUDA_OK(cudaMemset(err, 0, 4));
     CUDA_OK(cudaMemcpy(dl, logits, rows * V * 4, cudaMemcpyHostToDevice));
-    CUDA_OK(cudaMemcpy(ds, &o->seed, 8, cudaMemcpyHostToDevice));
     if (uniforms) {
       CUDA_OK(cudaMalloc(&du, V * 4));
       CUDA_OK(cudaMemcpy(du, uniforms, V * 4, cudaMemcpyHostToDevice));
@@ -1056,16 +1039,21 @@ int mrtdf_sample(mrtdf_engine* E, const float* logits, int cfg, int frame, int l
     level_range(c, o->use_vocab_masks != 0, level, lo, hi);
     SampleParams sp{};
     sp.logits = dl; sp.logits_stride = (int)V; sp.col_offset = 0; sp.lo = lo; sp.hi = hi; sp.rows_per_seq = rows;
-    sp.w = o->guidance_weight; sp.temperature = o->temperature; sp.top_k = o->top_k; sp.seeds = ds;
+    sp.w = o->guidance_weight; sp.temperature = o->temperature; sp.top_k = o->top_k; sp.seeds = nullptr;
+    sp.seed_value = o->seed;
     sp.step = (uint32_t)(frame * c.rvq_depth + level);
     sp.uniforms = du;  // one row of V draws for this step
     sp.uni_seq_stride = 0; sp.forced = nullptr; sp.tokens = dt; sp.tok_stride = 0; sp.tok_index = 0;
     sp.emb = E->emb; sp.d = (int)d; sp.V = (int)V; sp.din = din; sp.fsum = fs; sp.tin = tin; sp.depth = c.rvq_depth;
-    sp.is_first = 1; sp.is_last = 0; sp.err = err;
+    sp.is_first = 1; sp.is_last = 0; sp.err = err; sp.bad_token = -1;
     check_cuda(launch_sample(c.dtype, sp, 1, 0, false), "sample");
+    int herr = 0;
     CUDA_OK(cudaMemcpy(token, dt, 4, cudaMemcpyDeviceToHost));
-    cudaFree(dl); cudaFree(ds); cudaFree(dt); cudaFree(din); cudaFree(fs); cudaFree(tin); cudaFree(err);
+    CUDA_OK(cudaMemcpy(&herr, err, 4, cudaMemcpyDeviceToHost));
+    cudaFree(dl); cudaFree(dt); cudaFree(din); cudaFree(fs); cudaFree(tin); cudaFree(err);
     if (du) cudaFree(du);
+    if (herr & kErrBadToken)
+      throw Error{MRTDF_ERR_INVALID, "sample: no candidate could be drawn (NaN logits or an empty vocabulary range)"};
   });
 }
 
@@ -1089,24 +1077,20 @@ int mrtdf_sample_noalloc(mrtdf_engine* E, const float* logits_dev, int cfg, int 
     CUDA_OK(sample_scratch_address(E->device, &scratch));
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     uint8_t* base = reinterpret_cast<uint8_t*>(scratch);
-    uint64_t* seed = reinterpret_cast<uint64_t*>(base);
-    int* err = reinterpret_cast<int*>(base + 8);
-    // the error word must start at zero; the seed is this call's
-    CUDA_OK(cudaMemsetAsync(err, 0, 4, s));
-    CUDA_OK(cudaMemcpyAsync(seed, &o->seed, 8, cudaMemcpyHostToDevice, s));
     int lo, hi;
     level_range(c, o->use_vocab_masks != 0, level, lo, hi);
     SampleParams sp{};
     sp.logits = logits_dev; sp.logits_stride = c.vocab_size; sp.col_offset = 0; sp.lo = lo; sp.hi = hi;
     sp.rows_per_seq = rows; sp.w = o->guidance_weight; sp.temperature = o->temperature; sp.top_k = o->top_k;
-    sp.seeds = seed; sp.step = (uint32_t)(frame * c.rvq_depth + level);
+    sp.seeds = nullptr; sp.seed_value = o->seed; sp.step = (uint32_t)(frame * c.rvq_depth + level);
     sp.uniforms = uniforms_dev; sp.uni_seq_stride = 0; sp.forced = nullptr;
     sp.tokens = token_dev; sp.tok_stride = 0; sp.tok_index = 0;
     sp.emb = E->emb; sp.d = c.d_model; sp.V = c.vocab_size;
     sp.din = base + 256;
     sp.fsum = base + 256 + kSampleScratchRowBytes;
     sp.tin = base + 256 + 2 * kSampleScratchRowBytes;
-    sp.depth = c.rvq_depth; sp.is_first = 1; sp.is_last = 0; sp.err = err;
+    // no error word: a failed draw stores -1 as the token
+    sp.depth = c.rvq_depth; sp.is_first = 1; sp.is_last = 0; sp.err = nullptr; sp.bad_token = -1;
     check_cuda(launch_sample(c.dtype, sp, 1, s, false), "sample launch");
   });
 }
@@ -1448,7 +1432,7 @@ int mrtdf_bench_depth(mrtdf_stream* st, const mrtdf_gen_opts* o, int frames, int
     *bytes_per_step = (st->gemv_bytes + kv * frames) / steps;
     // per level: layers x (QKV, attention, o_proj, FFN-up, FFN-down) + lm_head + sampler;
     // the attention runs inside the QKV launch when fused
-    const bool fused = c.dtype == MRTDF_DTYPE_BF16 && st->B <= kQkvCluster && (E->fuse_attn || E->cluster_attn);
+    const bool fused = c.dtype == MRTDF_DTYPE_BF16 && st->B <= kQkvCluster && E->cluster_attn;
     *launches_per_step = (long long)c.num_depth_layers * (fused ? 4 : 5) + 2;
     check_device_err(st);
   });

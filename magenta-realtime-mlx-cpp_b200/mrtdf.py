@@ -37,7 +37,8 @@ EXPORTS = [
     "mrtdf_destroy", "mrtdf_load_safetensors", "mrtdf_load_random", "mrtdf_stream_create", "mrtdf_stream_destroy",
     "mrtdf_stream_rows", "mrtdf_encode", "mrtdf_temporal_step", "mrtdf_depth_step", "mrtdf_token_embedding",
     "mrtdf_sample", "mrtdf_sample_noalloc", "mrtdf_generate_tokens", "mrtdf_generate_tokens_dev",
-    "mrtdf_teacher_forced_logits", "mrtdf_stream_sync", "mrtdf_stream_cuda", "mrtdf_bench_gemv",
+    "mrtdf_teacher_forced_logits", "mrtdf_stream_sync", "mrtdf_stream_cuda", "mrtdf_check_wait_timeout",
+    "mrtdf_bench_gemv",
     "mrtdf_bench_encoder", "mrtdf_bench_depth", "mrtdf_stream_chunk_kernels", "mrtdf_generate_stream_dev",
     "mrtdf_build_encoder_inputs",
     "mrtdf_context_roll", "mrtdf_llm_to_rvq", "mrtdf_rvq_to_llm",
@@ -288,6 +289,11 @@ class Stream:
 
     def sync(self) -> None:
         _check(lib().mrtdf_stream_sync(self.h))
+
+    def check_wait_timeout(self, timeout_us: int) -> None:
+        """Queue a device wait that nothing completes, bounded by timeout_us;
+        raises MrtdfError with MRTDF_ERR_TIMEOUT (6) when it gives up."""
+        _check(lib().mrtdf_check_wait_timeout(self.h, timeout_us))
 
     def chunk_kernels(self) -> int:
         """Kernel nodes of the last chunk's CUDA graph (-1: no graph)."""

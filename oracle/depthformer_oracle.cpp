@@ -38,7 +38,9 @@
 #include <cstdio>
 #include <cstring>
 #include <limits>
+#include <functional>
 #include <map>
+#include <memory>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -219,6 +221,8 @@ struct Model {
   std::vector<std::vector<float>> tk, tv;        // per temporal layer (B, H, Tmax, dk)
   std::vector<std::vector<float>> dk_, dv_;      // per depth layer (B, H, depth, dk)
   std::vector<float> last_temporal;              // (B, d)
+  std::vector<float> last_depth;                 // (B, d) depth-stack output before decoder_norm
+  std::vector<float> gen_tin;                    // (B, d) next temporal input of frame-by-frame generation
 };
 
 static std::vector<float> sinusoid_table(int max_length, int features) {
@@ -240,23 +244,107 @@ static std::vector<float> sinusoid_table(int max_length, int features) {
   return data;
 }
 
-static void load_lin(const SafeTensors& st, const std::string& key, int out, int in, Lin& l, const Round& R) {
+// A weight bundle: key -> float32 values (n elements).
+struct Source {
+  std::function<std::vector<float>(const std::string&, int64_t)> get;
+};
+
+static void load_lin(const Source& st, const std::string& key, int out, int in, Lin& l, const Round& R) {
   l.out = out;
   l.in = in;
   l.w = st.get(key + ".weight", (int64_t)out * in);
   R.vec(l.w.data(), l.w.size());
 }
-static std::vector<float> load_vec(const SafeTensors& st, const std::string& key, int64_t n, const Round& R) {
+static std::vector<float> load_vec(const Source& st, const std::string& key, int64_t n, const Round& R) {
   std::vector<float> v = st.get(key, n);
   R.vec(v.data(), v.size());
   return v;
 }
 
+// ---------------------------------------------------------------------------
+// Random-init bundle, restated independently of the engine's writer. The
+// reference only loads bundles (weights.cpp:29-35), so the benchmark's
+// "N(0, 0.02) from seed 0" weights are defined by this generator: tensors in
+// model-construction order (the key layout of model.cpp:82-109, 173-198),
+// element i of tensor t = Box-Muller over Philox4x32-10 with key = seed and
+// counter (i/2 low word, i/2 high word, t, 0x5EED), times stddev; RMSNorm
+// scales are 1.0 when norm_ones.
+// ---------------------------------------------------------------------------
+struct WeightSpec {
+  std::string key;
+  int64_t n;
+  bool norm;
+};
+
+static std::vector<WeightSpec> weight_order(const Cfg& c) {
+  const int64_t d = c.d, in = c.inner(), ff = c.dff, V = c.V;
+  std::vector<WeightSpec> s;
+  s.push_back({"token_embedding.weight", V * d, false});
+  for (int i = 0; i < c.Le; ++i) {
+    const std::string p = "encoder_layers." + std::to_string(i) + ".";
+    s.push_back({p + "pre_attn_norm.weight", d, true});
+    for (const char* q : {"q", "k", "v"}) s.push_back({p + "self_attn." + q + "_proj.weight", in * d, false});
+    s.push_back({p + "self_attn.o_proj.weight", d * in, false});
+    s.push_back({p + "pre_ffn_norm.weight", d, true});
+    s.push_back({p + "ffn.wi_0.weight", ff * d, false});
+    s.push_back({p + "ffn.wi_1.weight", ff * d, false});
+    s.push_back({p + "ffn.wo.weight", d * ff, false});
+  }
+  s.push_back({"encoder_norm.weight", d, true});
+  s.push_back({"temporal_rel_pos.relative_attention_bias.weight", (int64_t)c.tnb * c.H, false});
+  auto dec = [&](const std::string& fam, int n, bool cross) {
+    for (int i = 0; i < n; ++i) {
+      const std::string p = fam + "." + std::to_string(i) + ".";
+      s.push_back({p + "pre_self_attn_norm.weight", d, true});
+      for (const char* q : {"q", "k", "v"}) s.push_back({p + "self_attn." + q + "_proj.weight", in * d, false});
+      s.push_back({p + "self_attn.o_proj.weight", d * in, false});
+      if (cross) {
+        s.push_back({p + "pre_cross_attn_norm.weight", d, true});
+        for (const char* q : {"q", "k", "v"}) s.push_back({p + "cross_attn." + q + "_proj.weight", in * d, false});
+        s.push_back({p + "cross_attn.o_proj.weight", d * in, false});
+      }
+      s.push_back({p + "pre_ffn_norm.weight", d, true});
+      s.push_back({p + "ffn.wi_0.weight", ff * d, false});
+      s.push_back({p + "ffn.wi_1.weight", ff * d, false});
+      s.push_back({p + "ffn.wo.weight", d * ff, false});
+    }
+  };
+  dec("temporal_layers", c.Lt, true);
+  s.push_back({"depth_rel_pos.relative_attention_bias.weight", (int64_t)c.dnb * c.H, false});
+  dec("depth_layers", c.Ld, false);
+  s.push_back({"decoder_norm.weight", d, true});
+  s.push_back({"lm_head.weight", V * d, false});
+  return s;
+}
+
+static std::vector<float> random_tensor(uint64_t seed, int ordinal, float stddev, bool norm, bool norm_ones,
+                                        int64_t n) {
+  std::vector<float> out((size_t)n);
+  if (norm && norm_ones) {
+    std::fill(out.begin(), out.end(), 1.0f);
+    return out;
+  }
+  const uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+  const int64_t pairs = (n + 1) / 2;
+#pragma omp parallel for schedule(static)
+  for (int64_t pr = 0; pr < pairs; ++pr) {
+    const uint32_t ctr[4] = {(uint32_t)pr, (uint32_t)((uint64_t)pr >> 32), (uint32_t)ordinal, 0x5EEDu};
+    uint32_t o[4];
+    philox4x32_10(ctr, key, o);
+    const double u1 = ((double)o[0] + 0.5) * (1.0 / 4294967296.0);
+    const double u2 = ((double)o[1] + 0.5) * (1.0 / 4294967296.0);
+    const double r = std::sqrt(-2.0 * std::log(u1));
+    const double th = 6.283185307179586 * u2;
+    out[(size_t)(2 * pr)] = (float)(r * std::cos(th) * stddev);
+    if (2 * pr + 1 < n) out[(size_t)(2 * pr + 1)] = (float)(r * std::sin(th) * stddev);
+  }
+  return out;
+}
+
 // Depthformer constructor wiring and key names (model.cpp:173-198,
 // modules.cpp:62-70, 90-96, 106-108, 118-134, 215-220, 232-241, 339-347,
 // 364-382).
-static Model* load_model(const char* path, const Cfg& c) {
-  SafeTensors st(path);
+static Model* load_model(const Source& st, const Cfg& c) {
   Model* m = new Model();
   m->c = c;
   m->R = Round{c.dtype == 1};
@@ -349,12 +437,11 @@ static void attend_one(const float* q, const float* K, const float* Vv, int T, i
 // (modules.cpp:349-358), then the cross K/V projection of every temporal
 // layer (MultiHeadAttention::project_kv, modules.cpp:323-333), which the
 // reference performs on frame 0 of temporal_step (modules.cpp:258-278).
-static void encode(Model& m, const int32_t* ids, int B, int S) {
+// Embedding + sinusoid (model.cpp:228-236): x = R(emb[id] + R(pe)).
+static void embed_pe(const Model& m, const int32_t* ids, int B, int S, float* x) {
   const Cfg& c = m.c;
   const Round& R = m.R;
-  const int d = c.d, in = c.inner(), H = c.H, dk = c.dk;
-  const size_t M = (size_t)B * S;
-  std::vector<float> x(M * d), n(M * d), q(M * in), k(M * in), v(M * in), o(M * in), h(M * d);
+  const int d = c.d;
   for (int b = 0; b < B; ++b)
     for (int s = 0; s < S; ++s) {
       const int id = ids[(size_t)b * S + s];
@@ -363,36 +450,57 @@ static void encode(Model& m, const int32_t* ids, int B, int S) {
       float* xr = &x[((size_t)b * S + s) * d];
       for (int i = 0; i < d; ++i) xr[i] = R(e[i] + R(p[i]));
     }
-  for (const EncLayer& L : m.enc) {
-    rms_norm(x.data(), (int)M, d, L.n_attn, n.data(), R);
-    L.q.apply(n.data(), (int)M, q.data(), R);
-    L.k.apply(n.data(), (int)M, k.data(), R);
-    L.v.apply(n.data(), (int)M, v.data(), R);
+}
+
+// One EncoderLayer (modules.cpp:349-358) over x (B, S, d), in place.
+static void encoder_layer(const Model& m, const EncLayer& L, float* x, int B, int S) {
+  const Cfg& c = m.c;
+  const Round& R = m.R;
+  const int d = c.d, in = c.inner(), H = c.H, dk = c.dk;
+  const size_t M = (size_t)B * S;
+  std::vector<float> n(M * d), q(M * in), k(M * in), v(M * in), o(M * in), h(M * d);
+  rms_norm(x, (int)M, d, L.n_attn, n.data(), R);
+  L.q.apply(n.data(), (int)M, q.data(), R);
+  L.k.apply(n.data(), (int)M, k.data(), R);
+  L.v.apply(n.data(), (int)M, v.data(), R);
 #pragma omp parallel
-    {
-      std::vector<float> Kh((size_t)S * dk), Vh((size_t)S * dk), qh(dk), oh(dk);
+  {
+    std::vector<float> Kh((size_t)S * dk), Vh((size_t)S * dk), qh(dk), oh(dk);
 #pragma omp for collapse(2) schedule(dynamic, 4)
-      for (int b = 0; b < B; ++b)
-        for (int hh = 0; hh < H; ++hh) {
-          // thread-private copies of this head's K, V: (S, dk)
-          for (int s = 0; s < S; ++s)
-            for (int cc = 0; cc < dk; ++cc) {
-              Kh[(size_t)s * dk + cc] = k[((size_t)b * S + s) * in + hh * dk + cc];
-              Vh[(size_t)s * dk + cc] = v[((size_t)b * S + s) * in + hh * dk + cc];
-            }
-          for (int i = 0; i < S; ++i) {
-            for (int cc = 0; cc < dk; ++cc) qh[cc] = q[((size_t)b * S + i) * in + hh * dk + cc];
-            attend_one(qh.data(), Kh.data(), Vh.data(), S, dk, nullptr, oh.data(), R);
-            for (int cc = 0; cc < dk; ++cc) o[((size_t)b * S + i) * in + hh * dk + cc] = oh[cc];
+    for (int b = 0; b < B; ++b)
+      for (int hh = 0; hh < H; ++hh) {
+        // thread-private copies of this head's K, V: (S, dk)
+        for (int s2 = 0; s2 < S; ++s2)
+          for (int cc = 0; cc < dk; ++cc) {
+            Kh[(size_t)s2 * dk + cc] = k[((size_t)b * S + s2) * in + hh * dk + cc];
+            Vh[(size_t)s2 * dk + cc] = v[((size_t)b * S + s2) * in + hh * dk + cc];
           }
+        for (int i = 0; i < S; ++i) {
+          for (int cc = 0; cc < dk; ++cc) qh[cc] = q[((size_t)b * S + i) * in + hh * dk + cc];
+          attend_one(qh.data(), Kh.data(), Vh.data(), S, dk, nullptr, oh.data(), R);
+          for (int cc = 0; cc < dk; ++cc) o[((size_t)b * S + i) * in + hh * dk + cc] = oh[cc];
         }
-    }
-    L.o.apply(o.data(), (int)M, h.data(), R);
-    for (size_t i = 0; i < M * d; ++i) x[i] = R(x[i] + h[i]);
-    rms_norm(x.data(), (int)M, d, L.n_ffn, n.data(), R);
-    ffn(m, L.wi0, L.wi1, L.wo, n.data(), (int)M, h.data());
-    for (size_t i = 0; i < M * d; ++i) x[i] = R(x[i] + h[i]);
+      }
   }
+  L.o.apply(o.data(), (int)M, h.data(), R);
+  for (size_t i = 0; i < M * d; ++i) x[i] = R(x[i] + h[i]);
+  rms_norm(x, (int)M, d, L.n_ffn, n.data(), R);
+  ffn(m, L.wi0, L.wi1, L.wo, n.data(), (int)M, h.data());
+  for (size_t i = 0; i < M * d; ++i) x[i] = R(x[i] + h[i]);
+}
+
+// Depthformer::encode (model.cpp:226-241) with EncoderLayer
+// (modules.cpp:349-358), then the cross K/V projection of every temporal
+// layer (MultiHeadAttention::project_kv, modules.cpp:323-333), which the
+// reference performs on frame 0 of temporal_step (modules.cpp:258-278).
+static void encode(Model& m, const int32_t* ids, int B, int S) {
+  const Cfg& c = m.c;
+  const Round& R = m.R;
+  const int d = c.d, in = c.inner(), H = c.H, dk = c.dk;
+  const size_t M = (size_t)B * S;
+  std::vector<float> x(M * d), k(M * in), v(M * in);
+  embed_pe(m, ids, B, S, x.data());
+  for (const EncLayer& L : m.enc) encoder_layer(m, L, x.data(), B, S);
   m.enc_out.assign(M * d, 0.f);
   rms_norm(x.data(), (int)M, d, m.enc_norm, m.enc_out.data(), R);
   m.B = B;
@@ -496,9 +604,22 @@ static void temporal_step(Model& m, const float* xin, int f, float* out) {
   std::memcpy(out, x.data(), x.size() * 4);
 }
 
+// decoder_norm + lm_head rows [lo, hi) for B rows (model.cpp:653-658):
+// out (B, hi - lo).
+static void lm_head_rows(const Model& m, const float* x, int B, int lo, int hi, float* out) {
+  const Cfg& c = m.c;
+  std::vector<float> n((size_t)B * c.d);
+  rms_norm(x, B, c.d, m.dec_norm, n.data(), m.R);
+  gemm_nt(n.data(), B, c.d, m.lm.w.data() + (size_t)lo * c.d, hi - lo, out);
+  m.R.vec(out, (size_t)B * (hi - lo));
+}
+
 // Depthformer::depth_step, eager path (model.cpp:638-659): 4 layers,
-// decoder_norm, lm_head -> (B, V).
-static void depth_step(Model& m, const float* xin, int di, float* logits) {
+// decoder_norm, lm_head -> (B, V). With lo/hi given, only lm_head rows
+// [lo, hi) are computed and every other logit is -inf: the rows outside the
+// level's vocab mask, which apply_vocab_mask (decode.cpp:87-91) sets to -inf
+// before any use, so sampling sees the same values.
+static void depth_step(Model& m, const float* xin, int di, float* logits, int lo = -1, int hi = -1) {
   const Cfg& c = m.c;
   std::vector<float> x(xin, xin + (size_t)m.B * c.d);
   m.R.vec(x.data(), x.size());
@@ -507,9 +628,16 @@ static void depth_step(Model& m, const float* xin, int di, float* logits) {
     decoder_layer(m, m.dl[l], x.data(), m.B, di, c.depth, m.dk_[l].data(), m.dv_[l].data(), bias.data(), nullptr,
                   nullptr, 0);
   m.d_len = di + 1;
-  std::vector<float> n((size_t)m.B * c.d);
-  rms_norm(x.data(), m.B, c.d, m.dec_norm, n.data(), m.R);
-  m.lm.apply(n.data(), m.B, logits, m.R);
+  m.last_depth = x;
+  if (lo < 0) {
+    lm_head_rows(m, x.data(), m.B, 0, c.V, logits);
+    return;
+  }
+  std::vector<float> part((size_t)m.B * (hi - lo));
+  lm_head_rows(m, x.data(), m.B, lo, hi, part.data());
+  std::fill(logits, logits + (size_t)m.B * c.V, -std::numeric_limits<float>::infinity());
+  for (int b = 0; b < m.B; ++b)
+    std::memcpy(logits + (size_t)b * c.V + lo, &part[(size_t)b * (hi - lo)], (size_t)(hi - lo) * 4);
 }
 
 // One sampling step (decode.cpp:465-474 with cfg_combine 71-85,
@@ -546,44 +674,62 @@ static int sample_step(const float* logits, int rows, int V, int level, bool mas
   return argmax_first(g);
 }
 
-// generate_tokens, non-speculative path (decode.cpp:239-573): frame 0
-// input = embedding of PAD (0), depth 0 input = temporal output, depth d > 0
-// input = embedding of the sampled token for every row, next temporal input
-// = R(R-summed embeddings / rvq_depth) (decode.cpp:383-386, 476-477, 484).
-// `forced` (optional) replaces the sampled tokens (teacher forcing);
-// `logits_out` (optional) receives (F, depth, B, V).
+// generate_tokens, non-speculative path (decode.cpp:239-573), frame by
+// frame: gen_begin encodes and sets frame 0's input = embedding of PAD (0);
+// gen_frame runs one frame: temporal step, then per level the depth step
+// (depth 0 input = temporal output, depth d > 0 input = embedding of the
+// sampled token for every row), the sampler, and the running sum; the next
+// temporal input is R(R-summed embeddings / rvq_depth) (decode.cpp:383-386,
+// 476-477, 484). `forced` (optional, depth ids) replaces the sampled
+// tokens (teacher forcing); `logits_out` (optional) receives (depth, B, V).
+// With masked sampling and no logits wanted, only the level's lm_head rows
+// are computed (depth_step's lo/hi), the work the engine does.
+static void gen_begin(Model& m, const int32_t* ids, int B, int S) {
+  encode(m, ids, B, S);
+  m.gen_tin.assign((size_t)B * m.c.d, 0.f);
+  for (int b = 0; b < B; ++b) std::memcpy(&m.gen_tin[(size_t)b * m.c.d], &m.emb[0], m.c.d * 4);  // PAD = 0
+}
+
+static void gen_frame(Model& m, int f, float w, float T, int top_k, bool masked, uint64_t seed,
+                      const float* uniforms /* (depth, V) of this frame */, const int32_t* forced, int32_t* out_ids,
+                      float* logits_out) {
+  const Cfg& c = m.c;
+  const Round& R = m.R;
+  const int B = m.B, d = c.d, D = c.depth, V = c.V;
+  std::vector<float> tout((size_t)B * d), din((size_t)B * d), sum((size_t)B * d, 0.f), logits((size_t)B * V), u(V);
+  temporal_step(m, m.gen_tin.data(), f, tout.data());
+  din = tout;
+  for (int l = 0; l < D; ++l) {
+    const bool slice = masked && !logits_out && !forced;
+    const int lo = c.off + l * c.cb;
+    depth_step(m, din.data(), l, logits.data(), slice ? lo : -1, slice ? lo + c.cb : -1);
+    if (logits_out) std::memcpy(logits_out + (size_t)l * B * V, logits.data(), logits.size() * 4);
+    int tok;
+    if (forced) {
+      tok = forced[l];
+    } else {
+      const uint32_t step = (uint32_t)(f * D + l);
+      for (int i = 0; i < V; ++i)
+        u[i] = uniforms ? uniforms[(size_t)l * V + i] : philox_uniform(seed, step, (uint32_t)i);
+      tok = sample_step(logits.data(), B, V, l, masked, c.cb, c.off, w, T, top_k, u.data());
+    }
+    if (out_ids) out_ids[l] = tok;
+    for (int b = 0; b < B; ++b) std::memcpy(&din[(size_t)b * d], &m.emb[(size_t)tok * d], d * 4);
+    for (size_t i = 0; i < sum.size(); ++i) sum[i] = R(sum[i] + din[i]);
+  }
+  for (size_t i = 0; i < sum.size(); ++i) m.gen_tin[i] = R(sum[i] / (float)D);
+}
+
 static void generate(Model& m, const int32_t* ids, int B, int S, int F, float w, float T, int top_k, bool masked,
                      uint64_t seed, const float* uniforms, const int32_t* forced, int32_t* out_ids,
                      float* logits_out) {
   const Cfg& c = m.c;
-  const Round& R = m.R;
-  const int d = c.d, D = c.depth, V = c.V;
-  encode(m, ids, B, S);
-  std::vector<float> tin((size_t)B * d), tout((size_t)B * d), din((size_t)B * d), sum((size_t)B * d),
-      logits((size_t)B * V), u(V);
-  for (int b = 0; b < B; ++b) std::memcpy(&tin[(size_t)b * d], &m.emb[0], d * 4);  // PAD = 0
-  for (int f = 0; f < F; ++f) {
-    temporal_step(m, tin.data(), f, tout.data());
-    din = tout;
-    std::fill(sum.begin(), sum.end(), 0.f);
-    for (int l = 0; l < D; ++l) {
-      depth_step(m, din.data(), l, logits.data());
-      if (logits_out) std::memcpy(logits_out + ((size_t)f * D + l) * B * V, logits.data(), logits.size() * 4);
-      int tok;
-      if (forced) {
-        tok = forced[(size_t)f * D + l];
-      } else {
-        const uint32_t step = (uint32_t)(f * D + l);
-        for (int i = 0; i < V; ++i)
-          u[i] = uniforms ? uniforms[(size_t)step * V + i] : philox_uniform(seed, step, (uint32_t)i);
-        tok = sample_step(logits.data(), B, V, l, masked, c.cb, c.off, w, T, top_k, u.data());
-      }
-      if (out_ids) out_ids[(size_t)f * D + l] = tok;
-      for (int b = 0; b < B; ++b) std::memcpy(&din[(size_t)b * d], &m.emb[(size_t)tok * d], d * 4);
-      for (size_t i = 0; i < sum.size(); ++i) sum[i] = R(sum[i] + din[i]);
-    }
-    for (size_t i = 0; i < sum.size(); ++i) tin[i] = R(sum[i] / (float)D);
-  }
+  const int D = c.depth;
+  gen_begin(m, ids, B, S);
+  for (int f = 0; f < F; ++f)
+    gen_frame(m, f, w, T, top_k, masked, seed, uniforms ? uniforms + (size_t)f * D * c.V : nullptr,
+              forced ? forced + (size_t)f * D : nullptr, out_ids ? out_ids + (size_t)f * D : nullptr,
+              logits_out ? logits_out + (size_t)f * D * B * c.V : nullptr);
 }
 
 }  // namespace oracle
@@ -611,7 +757,32 @@ void orc_set_num_threads(int n) { omp_set_num_threads(n); }
 
 void* orc_create(const char* path, const int* cfg_ints) {
   try {
-    return load_model(path, cfg_from_ints(cfg_ints));
+    auto st = std::make_shared<SafeTensors>(path);
+    Source src;
+    src.get = [st](const std::string& key, int64_t n) { return st->get(key, n); };
+    return load_model(src, cfg_from_ints(cfg_ints));
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return nullptr;
+  }
+}
+
+// The random-init bundle of `seed` generated in memory (no file).
+void* orc_create_random(const int* cfg_ints, uint64_t seed, float stddev, int norm_ones) {
+  try {
+    const Cfg c = cfg_from_ints(cfg_ints);
+    std::map<std::string, int> ordinal;
+    const std::vector<WeightSpec> specs = weight_order(c);
+    for (size_t i = 0; i < specs.size(); ++i) ordinal[specs[i].key] = (int)i;
+    Source src;
+    src.get = [&](const std::string& key, int64_t n) {
+      auto it = ordinal.find(key);
+      if (it == ordinal.end()) throw std::out_of_range("random bundle: no tensor " + key);
+      const WeightSpec& sp = specs[(size_t)it->second];
+      if (sp.n != n) throw std::runtime_error("random bundle: size mismatch for " + key);
+      return random_tensor(seed, it->second, stddev, sp.norm, norm_ones != 0, n);
+    };
+    return load_model(src, c);
   } catch (const std::exception& e) {
     g_err = e.what();
     return nullptr;
@@ -665,6 +836,93 @@ int orc_generate(void* mp, const int32_t* ids, int B, int S, int F, float w, flo
 int orc_teacher_forced(void* mp, const int32_t* ids, int B, int S, int F, const int32_t* tokens, float* logits) {
   ORC_TRY({
     generate(*(Model*)mp, ids, B, S, F, 0.f, 0.f, 0, 0, 0, nullptr, tokens, nullptr, logits);
+  })
+}
+
+// Frame-by-frame generate_tokens (gen_begin / gen_frame above); Philox draws.
+int orc_gen_begin(void* mp, const int32_t* ids, int B, int S) {
+  ORC_TRY({
+    Model& m = *(Model*)mp;
+    if (S > m.c.Smax) throw std::out_of_range("seq_len exceeds max_encoder_length");
+    gen_begin(m, ids, B, S);
+  })
+}
+
+int orc_gen_frame(void* mp, int f, float w, float T, int top_k, int masked, uint64_t seed, int32_t* out_ids) {
+  ORC_TRY({
+    Model& m = *(Model*)mp;
+    if (!m.encoded || m.gen_tin.empty()) throw std::runtime_error("gen_frame before gen_begin");
+    if (f != m.t_len || f >= m.c.Tmax) throw std::runtime_error("gen_frame: frame index out of order");
+    gen_frame(m, f, w, T, top_k, masked != 0, seed, nullptr, nullptr, out_ids, nullptr);
+  })
+}
+
+// ---- single-layer probes (per-layer parity tests) ------------------------
+// Encoder layer-0 input: R(emb[id] + R(pe)), (B, S, d).
+int orc_embed_pe(void* mp, const int32_t* ids, int B, int S, float* out) {
+  ORC_TRY({ embed_pe(*(Model*)mp, ids, B, S, out); })
+}
+
+// EncoderLayer `layer` over x (B, S, d) (rounded to the compute dtype first).
+int orc_encoder_layer(void* mp, int layer, const float* x, int B, int S, float* out) {
+  ORC_TRY({
+    Model& m = *(Model*)mp;
+    if (layer < 0 || layer >= m.c.Le) throw std::out_of_range("encoder layer");
+    std::vector<float> v(x, x + (size_t)B * S * m.c.d);
+    m.R.vec(v.data(), v.size());
+    encoder_layer(m, m.enc[(size_t)layer], v.data(), B, S);
+    std::memcpy(out, v.data(), v.size() * 4);
+  })
+}
+
+// One DecoderLayer of the temporal (stack 0) or depth (stack 1) stack at
+// cache position `pos`, over the model's caches (written at `pos`); x is
+// (B, d) with B the rows of the last encode.
+int orc_decoder_layer(void* mp, int stack, int layer, int pos, const float* x, float* out) {
+  ORC_TRY({
+    Model& m = *(Model*)mp;
+    const Cfg& c = m.c;
+    if (!m.encoded) throw std::runtime_error("decoder_layer before encode");
+    std::vector<float> v(x, x + (size_t)m.B * c.d);
+    m.R.vec(v.data(), v.size());
+    if (stack == 0) {
+      if (layer < 0 || layer >= c.Lt || pos < 0 || pos >= c.Tmax) throw std::out_of_range("temporal layer / pos");
+      const std::vector<float> bias = step_bias(m.trel, c.tnb, c.tmd, c.H, pos);
+      decoder_layer(m, m.tl[(size_t)layer], v.data(), m.B, pos, c.Tmax, m.tk[(size_t)layer].data(),
+                    m.tv[(size_t)layer].data(), bias.data(), m.ck[(size_t)layer].data(), m.cv[(size_t)layer].data(),
+                    m.S);
+    } else {
+      if (layer < 0 || layer >= c.Ld || pos < 0 || pos >= c.depth) throw std::out_of_range("depth layer / pos");
+      const std::vector<float> bias = step_bias(m.drel, c.dnb, c.dmd, c.H, pos);
+      decoder_layer(m, m.dl[(size_t)layer], v.data(), m.B, pos, c.depth, m.dk_[(size_t)layer].data(),
+                    m.dv_[(size_t)layer].data(), bias.data(), nullptr, nullptr, 0);
+    }
+    std::memcpy(out, v.data(), v.size() * 4);
+  })
+}
+
+// Cache contents: kind 0 temporal self (B, H, Tmax, dk), 1 depth self
+// (B, H, depth, dk), 2 cross (B, H, S, dk).
+int orc_get_cache(void* mp, int kind, int layer, float* K, float* V) {
+  ORC_TRY({
+    Model& m = *(Model*)mp;
+    if (!m.encoded) throw std::runtime_error("get_cache before encode");
+    const std::vector<std::vector<float>>& ks = kind == 0 ? m.tk : kind == 1 ? m.dk_ : m.ck;
+    const std::vector<std::vector<float>>& vs = kind == 0 ? m.tv : kind == 1 ? m.dv_ : m.cv;
+    if (layer < 0 || layer >= (int)ks.size()) throw std::out_of_range("cache layer");
+    std::memcpy(K, ks[(size_t)layer].data(), ks[(size_t)layer].size() * 4);
+    std::memcpy(V, vs[(size_t)layer].data(), vs[(size_t)layer].size() * 4);
+  })
+}
+
+// decoder_norm + lm_head rows [lo, hi) of x (B, d) -> (B, hi - lo).
+int orc_lm_head(void* mp, const float* x, int B, int lo, int hi, float* out) {
+  ORC_TRY({
+    Model& m = *(Model*)mp;
+    if (lo < 0 || hi > m.c.V || lo >= hi) throw std::out_of_range("lm_head rows");
+    std::vector<float> v(x, x + (size_t)B * m.c.d);
+    m.R.vec(v.data(), v.size());
+    lm_head_rows(m, v.data(), B, lo, hi, out);
   })
 }
 

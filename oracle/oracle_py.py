@@ -56,6 +56,19 @@ def lib() -> ctypes.CDLL:
         L.orc_gelu.restype = ctypes.c_float
         L.orc_gelu.argtypes = [ctypes.c_float, ctypes.c_int]
         L.orc_set_num_threads.argtypes = [ctypes.c_int]
+        L.orc_create_random.restype = ctypes.c_void_p
+        L.orc_create_random.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.c_uint64, ctypes.c_float, ctypes.c_int]
+        L.orc_gen_begin.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+        L.orc_gen_frame.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int,
+                                    ctypes.c_int, ctypes.c_uint64, ctypes.c_void_p]
+        L.orc_embed_pe.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+        L.orc_encoder_layer.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_void_p]
+        L.orc_decoder_layer.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                        ctypes.c_void_p]
+        L.orc_get_cache.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+        L.orc_lm_head.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                  ctypes.c_void_p]
         # SpectroStream decode phase (spectrostream_oracle.cpp)
         P, I = ctypes.c_void_p, ctypes.c_int
         L.orc_ss_last_error.restype = ctypes.c_char_p
@@ -89,18 +102,121 @@ def _check(rc: int):
         raise RuntimeError("oracle: " + lib().orc_last_error().decode())
 
 
+# Config field order of include/mrtdf.h (DepthformerConfig, model.h:47-68).
+CONFIG_FIELDS = [
+    "vocab_size", "d_model", "d_kv", "d_ff", "num_heads", "num_encoder_layers", "num_temporal_layers",
+    "num_depth_layers", "max_encoder_length", "rvq_depth", "temporal_num_buckets", "temporal_max_distance",
+    "depth_num_buckets", "depth_max_distance", "codebook_size", "codec_offset", "max_frames", "dtype",
+]
+
+
+def preset_ints(name: str, dtype: int = 1) -> list:
+    """Model presets as config ints, restated for the CPU arms: "base"
+    (DepthformerConfig::base(), model.cpp:34-36), "large" (model.cpp:38-48)
+    and "hybrid", the benchmark architecture of BASELINE.json (large widths,
+    base depths, 32 / 128 temporal buckets, vocab 16 x 1024 + 4)."""
+    c = dict(vocab_size=29824, d_model=768, d_kv=64, d_ff=2048, num_heads=12, num_encoder_layers=12,
+             num_temporal_layers=20, num_depth_layers=4, max_encoder_length=1006, rvq_depth=16,
+             temporal_num_buckets=128, temporal_max_distance=128, depth_num_buckets=16, depth_max_distance=16,
+             codebook_size=1024, codec_offset=2, max_frames=50, dtype=dtype)
+    if name == "large":
+        c.update(d_model=1024, d_ff=2816, num_heads=16, num_encoder_layers=24, num_temporal_layers=40,
+                 num_depth_layers=8)
+    elif name == "hybrid":
+        c.update(d_model=1024, d_ff=2816, num_heads=16, vocab_size=16388, temporal_num_buckets=32)
+    elif name != "base":
+        raise ValueError(f"unknown preset {name}")
+    return [c[f] for f in CONFIG_FIELDS]
+
+
+def build_encoder_inputs(context: np.ndarray, style: np.ndarray, enc_depth: int, codebook_size: int,
+                         codec_offset: int) -> np.ndarray:
+    """build_encoder_inputs_host (system.cpp:62-95): row 0 = the context's
+    first enc_depth levels per frame mapped to codec_offset + level *
+    codebook_size + code (MASK = 1 where the code is negative), then the
+    style ids; row 1 = the same context with the style masked."""
+    ctx = np.asarray(context, np.int64)[:, :enc_depth]
+    lvl = np.arange(enc_depth, dtype=np.int64)[None, :]
+    row = np.where(ctx >= 0, codec_offset + lvl * codebook_size + ctx, 1).reshape(-1)
+    style = np.asarray(style, np.int64).reshape(-1)
+    out = np.empty((2, row.size + style.size), np.int32)
+    out[0] = np.concatenate([row, style])
+    out[1] = np.concatenate([row, np.ones_like(style)])
+    return out
+
+
 class Oracle:
     """CPU restatement of the Depthformer (fp32 or bf16-emulating)."""
 
-    def __init__(self, safetensors_path: str, cfg_ints):
-        arr = (ctypes.c_int * 18)(*cfg_ints)
-        h = lib().orc_create(safetensors_path.encode(), arr)
-        if not h:
-            raise RuntimeError("oracle: " + lib().orc_last_error().decode())
-        self.h = h
+    def __init__(self, safetensors_path: Optional[str], cfg_ints, _handle=None):
+        if _handle is None:
+            arr = (ctypes.c_int * 18)(*cfg_ints)
+            _handle = lib().orc_create(safetensors_path.encode(), arr)
+            if not _handle:
+                raise RuntimeError("oracle: " + lib().orc_last_error().decode())
+        self.h = _handle
         self.cfg = list(cfg_ints)
         self.V, self.d, self.depth = cfg_ints[0], cfg_ints[1], cfg_ints[9]
         self.rows = 0
+
+    @classmethod
+    def from_random(cls, cfg_ints, seed: int, stddev: float = 0.02, norm_ones: bool = True) -> "Oracle":
+        """The random-init bundle of `seed` (the oracle's own restatement of
+        the generator), built in memory without a file."""
+        arr = (ctypes.c_int * 18)(*cfg_ints)
+        h = lib().orc_create_random(arr, seed, stddev, int(norm_ones))
+        if not h:
+            raise RuntimeError("oracle: " + lib().orc_last_error().decode())
+        return cls(None, cfg_ints, _handle=h)
+
+    def gen_begin(self, ids: np.ndarray) -> None:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        B, S = ids.shape
+        _check(lib().orc_gen_begin(self.h, _p(ids), B, S))
+        self.rows = B
+
+    def gen_frame(self, f: int, w: float, temperature: float, top_k: int, masked: bool, seed: int) -> np.ndarray:
+        """One frame of generate_tokens (temporal step, rvq_depth x (depth
+        step + sampler + feedback)) with Philox draws; returns the frame's ids."""
+        out = np.empty(self.depth, np.int32)
+        _check(lib().orc_gen_frame(self.h, f, w, temperature, top_k, int(masked), seed, _p(out)))
+        return out
+
+    # ---- single-layer probes ----------------------------------------------
+    def embed_pe(self, ids: np.ndarray) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        B, S = ids.shape
+        out = np.empty((B, S, self.d), np.float32)
+        _check(lib().orc_embed_pe(self.h, _p(ids), B, S, _p(out)))
+        return out
+
+    def encoder_layer(self, layer: int, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        B, S, _ = x.shape
+        out = np.empty_like(x)
+        _check(lib().orc_encoder_layer(self.h, layer, _p(x), B, S, _p(out)))
+        return out
+
+    def decoder_layer(self, stack: int, layer: int, pos: int, x: np.ndarray) -> np.ndarray:
+        """stack 0 = temporal, 1 = depth; writes this step's K/V at `pos`."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty_like(x)
+        _check(lib().orc_decoder_layer(self.h, stack, layer, pos, _p(x), _p(out)))
+        return out
+
+    def get_cache(self, kind: int, layer: int, cap: int):
+        """kind 0 temporal self, 1 depth self, 2 cross: (K, V) as (rows, H, cap, 64)."""
+        H = self.cfg[4]
+        K = np.empty((self.rows, H, cap, 64), np.float32)
+        V = np.empty_like(K)
+        _check(lib().orc_get_cache(self.h, kind, layer, _p(K), _p(V)))
+        return K, V
+
+    def lm_head(self, x: np.ndarray, lo: int, hi: int) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty((x.shape[0], hi - lo), np.float32)
+        _check(lib().orc_lm_head(self.h, _p(x), x.shape[0], lo, hi, _p(out)))
+        return out
 
     def encode(self, ids: np.ndarray) -> np.ndarray:
         ids = np.ascontiguousarray(ids, dtype=np.int32)

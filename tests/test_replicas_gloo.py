@@ -37,7 +37,7 @@ def _worker(rank: int, world: int, port: int, q):
     bench.barrier(dist)
     mx = bench.max_over_ranks(dist, 10.0 + rank)
     cfg = mrtdf.preset("hybrid")
-    ids = bench._initial_ids(mrtdf, cfg, r)
+    ids = bench._initial_ids(mrtdf.build_encoder_inputs, r)
     # the reference arm prints from rank 0 only and returns 0 elsewhere
     rc = bench.run_reference(type("A", (), {"warmup": 0, "steps": 0})()) if r != 0 else 0
     q.put((r, mx, ids[0, -6:].tolist(), rc))

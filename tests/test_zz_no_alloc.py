@@ -66,6 +66,26 @@ def test_noalloc_sample_equals_sample_hybrid(mrtdf):
     _check_pairs(mrtdf, cfg, eng, np.random.default_rng(50), 12)
 
 
+def test_noalloc_reports_a_failed_draw(mrtdf, tiny_weights):
+    """The call returns before the draw, so a draw without a valid candidate
+    (NaN logits) is reported in the result: the token is -1. A good draw
+    right after it on the same stream is unaffected."""
+    cfg = mrtdf.preset("tiny", mrtdf.DTYPE_BF16)
+    eng = mrtdf.Engine(cfg).load_safetensors(tiny_weights)
+    bad = torch.full((2, cfg.vocab_size), float("nan"), dtype=torch.float32, device="cuda:0")
+    good_h = np.random.default_rng(3).standard_normal((2, cfg.vocab_size)).astype(np.float32)
+    good = torch.from_numpy(good_h).to("cuda:0")
+    tok = torch.full((2,), 7, dtype=torch.int32, device="cuda:0")
+    o = mrtdf.gen_opts(cfg, 1, temperature=1.1, top_k=40, guidance_weight=4.0, seed=5)
+    torch.cuda.synchronize()
+    eng.sample_noalloc(bad.data_ptr(), True, 0, 2, o, None, tok[0:].data_ptr(), 0)
+    eng.sample_noalloc(good.data_ptr(), True, 0, 2, o, None, tok[1:].data_ptr(), 0)
+    torch.cuda.synchronize()
+    got = tok.cpu().tolist()
+    assert got[0] == -1
+    assert got[1] == eng.sample(good_h, 0, 2, o)
+
+
 def test_noalloc_rejects_rows_beyond_scratch(mrtdf):
     # fp32, CFG pair: 2 x 2752 x 4 bytes = 22016 > the fixed 21760-byte row
     cfg = mrtdf.preset("tiny", mrtdf.DTYPE_FP32, d_model=2752)
