@@ -296,6 +296,34 @@ int mrtdf_bench_depth(mrtdf_stream* st, const mrtdf_gen_opts* opts, int frames, 
  */
 long long mrtdf_stream_chunk_kernels(const mrtdf_stream* st);
 
+/* ---- single-layer probes ----------------------------------------------------
+ * No counterpart in the reference: each runs ONE step of the production
+ * launch sequence (the same kernels, launch shapes and epilogues as a chunk)
+ * on caller-given float32 inputs, rounded to the compute dtype on upload, so
+ * a CPU restatement can be checked layer by layer on identical inputs. They
+ * use and overwrite the stream's activation and cache buffers.
+ */
+
+/* EncoderLayer `layer` (modules.cpp:349-358) over x (rows, seq_len,
+ * d_model) -> out, same shape. */
+int mrtdf_probe_encoder_layer(mrtdf_stream* st, int layer, const float* x, int seq_len, float* out);
+
+/* Overwrite positions [0, len) of one layer's cache with (rows, H, len,
+ * d_kv) float32 k / v: kind 0 = temporal self-attention, 1 = depth
+ * self-attention, 2 = cross-attention (len = the encoder length the
+ * temporal layers then attend over). */
+int mrtdf_probe_set_cache(mrtdf_stream* st, int kind, int layer, const float* k, const float* v, int len);
+
+/* DecoderLayer::forward (modules.cpp:384-446) of the temporal (stack 0) or
+ * depth (stack 1) stack at cache position `pos`: x (rows, d_model) -> out;
+ * the step's k / v are appended to the layer's cache at `pos`. */
+int mrtdf_probe_decoder_layer(mrtdf_stream* st, int stack, int layer, int pos, const float* x, float* out);
+
+/* decoder_norm + lm_head (model.cpp:653-658) of x (rows, d_model): the
+ * codebook rows of RVQ level `level` (rows x codebook_size logits), or all
+ * vocab_size rows when level < 0. */
+int mrtdf_probe_lm_head(mrtdf_stream* st, int level, const float* x, float* logits);
+
 /* ---- streaming glue (System, system.cpp) ---------------------------------- */
 
 /*

@@ -4,8 +4,10 @@
 
 CUDA sources are compiled by nvcc with -gencode arch=compute_100a,code=sm_100a;
 host C++ sources by g++; the shared library lands in
-magenta-realtime-mlx-cpp_b200/lib/libmrtdf.so. Objects are cached in _build/
-and rebuilt when a source or header is newer. No GPU is needed to build.
+magenta-realtime-mlx-cpp_b200/lib/libmrtdf.so. The C++ dry-run driver
+(cli/mrtdf_dry_run.cpp, built against include/mrtdf.hpp) lands beside it as
+lib/mrtdf_dry_run. Objects are cached in _build/ and rebuilt when a source or
+header is newer. No GPU is needed to build.
 """
 from __future__ import annotations
 
@@ -21,6 +23,8 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libmrtdf.so")
+DRIVER_SRC = os.path.join(HERE, "cli", "mrtdf_dry_run.cpp")
+DRIVER = os.path.join(LIBDIR, "mrtdf_dry_run")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -34,7 +38,7 @@ def _nvcc() -> str:
 def _headers() -> list[str]:
     return glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(
         os.path.join(INCLUDE, "*.h")
-    )
+    ) + glob.glob(os.path.join(INCLUDE, "*.hpp"))
 
 
 def _compile(src: str, verbose: bool) -> str:
@@ -69,15 +73,33 @@ def build(force: bool = False, verbose: bool = False) -> str:
     sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose), sources))
-    if os.path.exists(LIB) and os.path.getmtime(LIB) >= max(os.path.getmtime(o) for o in objs):
-        return LIB
-    tmp = LIB + ".tmp"
-    cmd = [_nvcc(), "-shared", *ARCH, "-o", tmp, *objs, "-lcudart_static", "-lpthread", "-ldl", "-lrt"]
+    if not (os.path.exists(LIB) and os.path.getmtime(LIB) >= max(os.path.getmtime(o) for o in objs)):
+        tmp = LIB + ".tmp"
+        cmd = [_nvcc(), "-shared", *ARCH, "-o", tmp, *objs, "-lcudart_static", "-lpthread", "-ldl", "-lrt"]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        subprocess.check_call(cmd)
+        os.replace(tmp, LIB)
+    build_driver(verbose)
+    return LIB
+
+
+def build_driver(verbose: bool = False) -> str:
+    """The C++ dry-run driver, linked against libmrtdf.so (found next to it)."""
+    newest = max([os.path.getmtime(DRIVER_SRC), os.path.getmtime(LIB)] + [os.path.getmtime(h) for h in _headers()])
+    if os.path.exists(DRIVER) and os.path.getmtime(DRIVER) >= newest:
+        return DRIVER
+    tmp = DRIVER + ".tmp"
+    cmd = ["g++", "-std=c++17", "-O2", "-Wall", "-I", INCLUDE, DRIVER_SRC, "-o", tmp, "-L", LIBDIR, "-lmrtdf",
+           "-Wl,-rpath,$ORIGIN"]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
-    subprocess.check_call(cmd)
-    os.replace(tmp, LIB)
-    return LIB
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+        raise RuntimeError("compile failed: " + DRIVER_SRC)
+    os.replace(tmp, DRIVER)
+    return DRIVER
 
 
 if __name__ == "__main__":

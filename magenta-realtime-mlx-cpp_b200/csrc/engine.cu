@@ -519,34 +519,42 @@ cudaError_t encoder_gemm(mrtdf_stream* st, int epi, const GemmParams& g) {
   return launch_gemm_f32(epi, g, st->s, E->pdl);
 }
 
-void enqueue_encode(mrtdf_stream* st, int S) {
+// One EncoderLayer (modules.cpp:349-358) over st->ex, (B * S, d), in place.
+void enqueue_encoder_layer(mrtdf_stream* st, const EncLayerDev& L, int S) {
   mrtdf_engine* E = st->eng;
   const mrtdf_config& c = E->c;
   const int d = c.d_model, in = E->inner(), ff = c.d_ff;
   const int M = st->B * S;
   const int dt = c.dtype;
   const bool pdl = E->pdl;
+  check_cuda(launch_rmsnorm_rows(dt, st->ex, L.n_attn, M, d, st->en, st->s, pdl), "rmsnorm");
+  GemmParams g{};
+  g.A = st->en; g.W = L.wqkv; g.out = st->eqkv; g.M = M; g.N = 3 * in; g.K = d; g.lda = d; g.ldo = 3 * in;
+  check_cuda(encoder_gemm(st, kEpiStore, g), "gemm qkv");
+  EncAttnParams a{st->eqkv, st->eo, st->B, S, c.num_heads, in};
+  check_cuda(launch_enc_attention(dt, a, st->s, pdl), "enc attention");
+  g = GemmParams{};
+  g.A = st->eo; g.W = L.wo; g.out = st->ex; g.M = M; g.N = d; g.K = in; g.lda = in; g.ldo = d;
+  check_cuda(encoder_gemm(st, kEpiResid, g), "gemm o");
+  check_cuda(launch_rmsnorm_rows(dt, st->ex, L.n_ffn, M, d, st->en, st->s, pdl), "rmsnorm");
+  g = GemmParams{};
+  g.A = st->en; g.W = L.wi; g.out = st->eh; g.M = M; g.N = 2 * ff; g.K = d; g.lda = d; g.ldo = ff;
+  check_cuda(encoder_gemm(st, kEpiGeglu, g), "gemm wi");
+  g = GemmParams{};
+  g.A = st->eh; g.W = L.wout; g.out = st->ex; g.M = M; g.N = d; g.K = ff; g.lda = ff; g.ldo = d;
+  check_cuda(encoder_gemm(st, kEpiResid, g), "gemm wo");
+}
+
+void enqueue_encode(mrtdf_stream* st, int S) {
+  mrtdf_engine* E = st->eng;
+  const mrtdf_config& c = E->c;
+  const int d = c.d_model, in = E->inner();
+  const int M = st->B * S;
+  const int dt = c.dtype;
+  const bool pdl = E->pdl;
   check_cuda(launch_embed_pe(dt, E->emb, E->pe, st->ids, M, S, d, c.vocab_size, st->ex, st->err, st->s, pdl),
              "embed_pe");
-  for (int l = 0; l < c.num_encoder_layers; ++l) {
-    const EncLayerDev& L = E->enc[l];
-    check_cuda(launch_rmsnorm_rows(dt, st->ex, L.n_attn, M, d, st->en, st->s, pdl), "rmsnorm");
-    GemmParams g{};
-    g.A = st->en; g.W = L.wqkv; g.out = st->eqkv; g.M = M; g.N = 3 * in; g.K = d; g.lda = d; g.ldo = 3 * in;
-    check_cuda(encoder_gemm(st, kEpiStore, g), "gemm qkv");
-    EncAttnParams a{st->eqkv, st->eo, st->B, S, c.num_heads, in};
-    check_cuda(launch_enc_attention(dt, a, st->s, pdl), "enc attention");
-    g = GemmParams{};
-    g.A = st->eo; g.W = L.wo; g.out = st->ex; g.M = M; g.N = d; g.K = in; g.lda = in; g.ldo = d;
-    check_cuda(encoder_gemm(st, kEpiResid, g), "gemm o");
-    check_cuda(launch_rmsnorm_rows(dt, st->ex, L.n_ffn, M, d, st->en, st->s, pdl), "rmsnorm");
-    g = GemmParams{};
-    g.A = st->en; g.W = L.wi; g.out = st->eh; g.M = M; g.N = 2 * ff; g.K = d; g.lda = d; g.ldo = ff;
-    check_cuda(encoder_gemm(st, kEpiGeglu, g), "gemm wi");
-    g = GemmParams{};
-    g.A = st->eh; g.W = L.wout; g.out = st->ex; g.M = M; g.N = d; g.K = ff; g.lda = ff; g.ldo = d;
-    check_cuda(encoder_gemm(st, kEpiResid, g), "gemm wo");
-  }
+  for (int l = 0; l < c.num_encoder_layers; ++l) enqueue_encoder_layer(st, E->enc[l], S);
   check_cuda(launch_rmsnorm_rows(dt, st->ex, E->enc_norm, M, d, st->en, st->s, pdl), "encoder_norm");
   GemmParams g{};
   g.A = st->en; g.W = E->wckv; g.out = nullptr; g.M = M; g.N = c.num_temporal_layers * 2 * in; g.K = d; g.lda = d;
@@ -1440,5 +1448,117 @@ int mrtdf_bench_depth(mrtdf_stream* st, const mrtdf_gen_opts* o, int frames, int
 
 
 long long mrtdf_stream_chunk_kernels(const mrtdf_stream* st) { return st ? st->last_chunk_kernels : -1; }
+
+// ---- single-layer probes -----------------------------------------------------
+int mrtdf_probe_encoder_layer(mrtdf_stream* st, int layer, const float* x, int seq_len, float* out) {
+  return guarded([&] {
+    if (!st || !x || !out) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    mrtdf_engine* E = st->eng;
+    const mrtdf_config& c = E->c;
+    if (layer < 0 || layer >= c.num_encoder_layers) throw Error{MRTDF_ERR_RANGE, "encoder layer out of range"};
+    if (seq_len <= 0 || seq_len > c.max_encoder_length) throw Error{MRTDF_ERR_RANGE, "seq_len out of range"};
+    CUDA_OK(cudaSetDevice(E->device));
+    const size_t n = (size_t)st->B * seq_len * c.d_model;
+    float* tmp = nullptr;
+    CUDA_OK(cudaMalloc(&tmp, n * 4));
+    struct Free {
+      float* p;
+      ~Free() { cudaFree(p); }
+    } free_tmp{tmp};
+    CUDA_OK(cudaMemcpyAsync(tmp, x, n * 4, cudaMemcpyHostToDevice, st->s));
+    check_cuda(launch_f32_to_act(c.dtype, tmp, n, st->ex, st->s), "convert");
+    enqueue_encoder_layer(st, E->enc[layer], seq_len);
+    check_cuda(launch_act_to_f32(c.dtype, st->ex, n, tmp, st->s), "convert");
+    CUDA_OK(cudaMemcpyAsync(out, tmp, n * 4, cudaMemcpyDeviceToHost, st->s));
+    CUDA_OK(cudaStreamSynchronize(st->s));
+    check_device_err(st);
+  });
+}
+
+int mrtdf_probe_set_cache(mrtdf_stream* st, int kind, int layer, const float* k, const float* v, int len) {
+  return guarded([&] {
+    if (!st || !k || !v) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    mrtdf_engine* E = st->eng;
+    const mrtdf_config& c = E->c;
+    const int layers = kind == 1 ? c.num_depth_layers : c.num_temporal_layers;
+    const int cap = kind == 0 ? c.max_frames : kind == 1 ? c.rvq_depth : c.max_encoder_length;
+    if (kind < 0 || kind > 2 || layer < 0 || layer >= layers) throw Error{MRTDF_ERR_RANGE, "cache kind / layer"};
+    if (len < 0 || len > cap || (kind == 2 && len == 0)) throw Error{MRTDF_ERR_RANGE, "cache length"};
+    CUDA_OK(cudaSetDevice(E->device));
+    const size_t rows_h = (size_t)st->B * c.num_heads, es = E->esize;
+    const size_t per_layer = rows_h * cap * 64 * es;
+    uint8_t* kd = (uint8_t*)(kind == 0 ? st->tk : kind == 1 ? st->dk : st->ck) + per_layer * layer;
+    uint8_t* vd = (uint8_t*)(kind == 0 ? st->tv : kind == 1 ? st->dv : st->cv) + per_layer * layer;
+    if (len > 0) {
+      const size_t n = rows_h * len * 64;
+      const std::vector<uint8_t> kb = to_dtype(k, n, c.dtype), vb = to_dtype(v, n, c.dtype);
+      CUDA_OK(cudaMemcpy2DAsync(kd, cap * 64 * es, kb.data(), len * 64 * es, len * 64 * es, rows_h,
+                                cudaMemcpyHostToDevice, st->s));
+      CUDA_OK(cudaMemcpy2DAsync(vd, cap * 64 * es, vb.data(), len * 64 * es, len * 64 * es, rows_h,
+                                cudaMemcpyHostToDevice, st->s));
+      CUDA_OK(cudaStreamSynchronize(st->s));  // kb / vb are locals
+    }
+    if (kind == 2) {
+      st->S = len;
+      st->encoded = true;
+    }
+  });
+}
+
+int mrtdf_probe_decoder_layer(mrtdf_stream* st, int stack, int layer, int pos, const float* x, float* out) {
+  return guarded([&] {
+    if (!st || !x || !out) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    mrtdf_engine* E = st->eng;
+    const mrtdf_config& c = E->c;
+    if (stack != 0 && stack != 1) throw Error{MRTDF_ERR_INVALID, "stack must be 0 (temporal) or 1 (depth)"};
+    const int layers = stack == 0 ? c.num_temporal_layers : c.num_depth_layers;
+    const int cap = stack == 0 ? c.max_frames : c.rvq_depth;
+    if (layer < 0 || layer >= layers || pos < 0 || pos >= cap) throw Error{MRTDF_ERR_RANGE, "layer / pos"};
+    if (stack == 0 && !st->encoded) throw Error{MRTDF_ERR_STATE, "temporal layer: no cross-attention cache"};
+    CUDA_OK(cudaSetDevice(E->device));
+    const size_t es = E->esize;
+    if (stack == 0) {
+      const size_t tcs = layer_cache_elems(st, c.max_frames), ccs = layer_cache_elems(st, c.max_encoder_length);
+      upload_act(st, x, st->tin);
+      enqueue_decoder_layer(st, E->tl[layer], st->tin, st->tx, (uint8_t*)st->tk + tcs * es * layer,
+                            (uint8_t*)st->tv + tcs * es * layer, c.max_frames, pos,
+                            E->tbias + (size_t)pos * c.num_heads * c.max_frames, c.max_frames,
+                            (const uint8_t*)st->ck + ccs * es * layer, (const uint8_t*)st->cv + ccs * es * layer,
+                            false);
+      download_act(st, st->tx, out);
+    } else {
+      const size_t dcs = layer_cache_elems(st, c.rvq_depth);
+      upload_act(st, x, st->din);
+      enqueue_decoder_layer(st, E->dl[layer], st->din, st->dx, (uint8_t*)st->dk + dcs * es * layer,
+                            (uint8_t*)st->dv + dcs * es * layer, c.rvq_depth, pos,
+                            E->dbias + (size_t)pos * c.num_heads * c.rvq_depth, c.rvq_depth, nullptr, nullptr, true);
+      download_act(st, st->dx, out);
+    }
+    CUDA_OK(cudaStreamSynchronize(st->s));
+    check_device_err(st);
+  });
+}
+
+int mrtdf_probe_lm_head(mrtdf_stream* st, int level, const float* x, float* logits) {
+  return guarded([&] {
+    if (!st || !x || !logits) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    mrtdf_engine* E = st->eng;
+    const mrtdf_config& c = E->c;
+    if (level >= c.rvq_depth) throw Error{MRTDF_ERR_RANGE, "level out of range"};
+    int lo, hi;
+    level_range(c, level >= 0, level < 0 ? 0 : level, lo, hi);
+    CUDA_OK(cudaSetDevice(E->device));
+    upload_act(st, x, st->dx);
+    GemvParams p{};
+    p.W = (const uint8_t*)E->lm_head + act_bytes(E, (size_t)lo * c.d_model);
+    p.x = st->dx; p.norm_w = E->dec_norm; p.out = st->logits; p.units = hi - lo; p.cols = c.d_model;
+    p.x_stride = c.d_model; p.out_stride = c.vocab_size; p.out_offset = lo; p.l2_keep = 1;
+    gemv(st, kGemvLogits, true, p);
+    CUDA_OK(cudaMemcpy2DAsync(logits, (size_t)(hi - lo) * 4, st->logits + lo, (size_t)c.vocab_size * 4,
+                              (size_t)(hi - lo) * 4, st->B, cudaMemcpyDeviceToHost, st->s));
+    CUDA_OK(cudaStreamSynchronize(st->s));
+    check_device_err(st);
+  });
+}
 
 }  // extern "C"

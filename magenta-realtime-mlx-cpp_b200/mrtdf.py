@@ -39,7 +39,8 @@ EXPORTS = [
     "mrtdf_sample", "mrtdf_sample_noalloc", "mrtdf_generate_tokens", "mrtdf_generate_tokens_dev",
     "mrtdf_teacher_forced_logits", "mrtdf_stream_sync", "mrtdf_stream_cuda", "mrtdf_check_wait_timeout",
     "mrtdf_bench_gemv",
-    "mrtdf_bench_encoder", "mrtdf_bench_depth", "mrtdf_stream_chunk_kernels", "mrtdf_generate_stream_dev",
+    "mrtdf_bench_encoder", "mrtdf_bench_depth", "mrtdf_stream_chunk_kernels", "mrtdf_probe_encoder_layer",
+    "mrtdf_probe_set_cache", "mrtdf_probe_decoder_layer", "mrtdf_probe_lm_head", "mrtdf_generate_stream_dev",
     "mrtdf_build_encoder_inputs",
     "mrtdf_context_roll", "mrtdf_llm_to_rvq", "mrtdf_rvq_to_llm",
 ]
@@ -321,6 +322,32 @@ class Stream:
 
     def cuda_stream(self) -> int:
         return lib().mrtdf_stream_cuda(self.h)
+
+    # ---- single-layer probes (one step of the production launch sequence) ----
+    def probe_encoder_layer(self, layer: int, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty_like(x)
+        _check(lib().mrtdf_probe_encoder_layer(self.h, layer, _fp(x), x.shape[1], _fp(out)))
+        return out
+
+    def probe_set_cache(self, kind: int, layer: int, k: np.ndarray, v: np.ndarray) -> None:
+        """kind 0 temporal self, 1 depth self, 2 cross; k / v (rows, H, len, 64)."""
+        k = np.ascontiguousarray(k, dtype=np.float32)
+        v = np.ascontiguousarray(v, dtype=np.float32)
+        _check(lib().mrtdf_probe_set_cache(self.h, kind, layer, _fp(k), _fp(v), k.shape[2]))
+
+    def probe_decoder_layer(self, stack: int, layer: int, pos: int, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty_like(x)
+        _check(lib().mrtdf_probe_decoder_layer(self.h, stack, layer, pos, _fp(x), _fp(out)))
+        return out
+
+    def probe_lm_head(self, level: int, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        n = self.cfg.codebook_size if level >= 0 else self.cfg.vocab_size
+        out = np.empty((x.shape[0], n), np.float32)
+        _check(lib().mrtdf_probe_lm_head(self.h, level, _fp(x), _fp(out)))
+        return out
 
     def close(self):
         if self.h:

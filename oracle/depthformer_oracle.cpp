@@ -915,6 +915,33 @@ int orc_get_cache(void* mp, int kind, int layer, float* K, float* V) {
   })
 }
 
+// Overwrite a cache (kind as in orc_get_cache) with full-capacity arrays;
+// kind 2 also sets the encoder length S the temporal layers attend over.
+// Lets a second oracle (e.g. fp32) run a layer on another one's state.
+int orc_set_cache(void* mp, int kind, int layer, const float* K, const float* V, int B, int S) {
+  ORC_TRY({
+    Model& m = *(Model*)mp;
+    const Cfg& c = m.c;
+    if (!m.encoded) {  // shape the state for B rows without an encode
+      m.B = B;
+      m.S = S;
+      m.ck.assign(c.Lt, std::vector<float>((size_t)B * c.H * S * c.dk, 0.f));
+      m.cv.assign(c.Lt, std::vector<float>((size_t)B * c.H * S * c.dk, 0.f));
+      m.tk.assign(c.Lt, std::vector<float>((size_t)B * c.H * c.Tmax * c.dk, 0.f));
+      m.tv.assign(c.Lt, std::vector<float>((size_t)B * c.H * c.Tmax * c.dk, 0.f));
+      m.dk_.assign(c.Ld, std::vector<float>((size_t)B * c.H * c.depth * c.dk, 0.f));
+      m.dv_.assign(c.Ld, std::vector<float>((size_t)B * c.H * c.depth * c.dk, 0.f));
+      m.encoded = true;
+    }
+    if (B != m.B || S != m.S) throw std::runtime_error("set_cache: rows / encoder length differ from the state");
+    std::vector<std::vector<float>>& ks = kind == 0 ? m.tk : kind == 1 ? m.dk_ : m.ck;
+    std::vector<std::vector<float>>& vs = kind == 0 ? m.tv : kind == 1 ? m.dv_ : m.cv;
+    if (layer < 0 || layer >= (int)ks.size()) throw std::out_of_range("cache layer");
+    std::memcpy(ks[(size_t)layer].data(), K, ks[(size_t)layer].size() * 4);
+    std::memcpy(vs[(size_t)layer].data(), V, vs[(size_t)layer].size() * 4);
+  })
+}
+
 // decoder_norm + lm_head rows [lo, hi) of x (B, d) -> (B, hi - lo).
 int orc_lm_head(void* mp, const float* x, int B, int lo, int hi, float* out) {
   ORC_TRY({

@@ -67,6 +67,8 @@ def lib() -> ctypes.CDLL:
         L.orc_decoder_layer.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                         ctypes.c_void_p]
         L.orc_get_cache.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+        L.orc_set_cache.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_int, ctypes.c_int]
         L.orc_lm_head.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                   ctypes.c_void_p]
         # SpectroStream decode phase (spectrostream_oracle.cpp)
@@ -211,6 +213,14 @@ class Oracle:
         V = np.empty_like(K)
         _check(lib().orc_get_cache(self.h, kind, layer, _p(K), _p(V)))
         return K, V
+
+    def set_cache(self, kind: int, layer: int, K: np.ndarray, V: np.ndarray, enc_len: int) -> None:
+        """Overwrite a full-capacity cache (kinds as in get_cache) for
+        K.shape[0] rows and an encoder length of enc_len."""
+        K = np.ascontiguousarray(K, dtype=np.float32)
+        V = np.ascontiguousarray(V, dtype=np.float32)
+        _check(lib().orc_set_cache(self.h, kind, layer, _p(K), _p(V), K.shape[0], enc_len))
+        self.rows = K.shape[0]
 
     def lm_head(self, x: np.ndarray, lo: int, hi: int) -> np.ndarray:
         x = np.ascontiguousarray(x, dtype=np.float32)

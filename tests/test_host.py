@@ -33,7 +33,8 @@ def test_library_exports_every_declared_symbol(mrtdf):
     missing = [s for s in codec if not hasattr(lib, s)]
     assert not missing, missing
     assert sorted(mrtss.EXPORTS) == sorted(codec)
-    assert sorted(os.listdir(os.path.join(ROOT, "include"))) == ["mrtdf.h", "mrtss.h"]
+    # the C ABI headers, plus the header-only C++ wrapper over mrtdf.h
+    assert sorted(os.listdir(os.path.join(ROOT, "include"))) == ["mrtdf.h", "mrtdf.hpp", "mrtss.h"]
 
 
 def test_version(mrtdf):
