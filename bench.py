@@ -16,9 +16,11 @@ and 16 depth steps + sampling per frame = 800 RVQ tokens.
   System::generate_chunk drives it (system.cpp:177-333): host context ->
   encoder ids -> mrtdf_generate_tokens (host->device ids, device->host
   tokens) -> llm_to_rvq -> context roll, streaming K chunks.
-* roofline: the dominant kernel is the decode GEMV phase; its algorithmic
-  bytes per launch / its average launch duration, measured with CUDA events
-  by replaying exactly the chunk's GEMV launches (mrtdf_bench_gemv).
+* roofline: the decode phases, split by stack: the temporal stack against
+  the measured HBM peak, the depth stack + lm_head against an L2 read peak
+  measured by the engine's own kernel; algorithmic bytes per launch / the
+  average launch time, from replaying exactly one stack's launches of a
+  chunk (mrtdf_bench_phases).
 * cpu_baseline: the CPU oracle (C++ restatement of the reference's eager
   Depthformer, all host threads) on one whole chunk of the same workload.
 
@@ -316,7 +318,7 @@ def run_ours(args):
     e2e = roofline = None
     if not args.timed_only:
         e2e = e2e_leg(mrtdf, torch, cfg, st, ext, ids, K, rank, dist, device)
-        roofline = roofline_leg(mrtdf, cfg, st, peaks)
+        roofline = roofline_leg(mrtdf, eng, cfg, st, peaks)
 
     value = TOKENS_PER_CHUNK * world / (ms_dev / 1e3)
     line = {
@@ -395,28 +397,32 @@ def e2e_leg(mrtdf, torch, cfg, st, ext, ids, K: int, rank: int, dist, device) ->
             "ms_per_chunk": ms_e2e, "rtf": CHUNK_SECONDS * 1e3 / ms_e2e}
 
 
-# DRAM bytes / algorithmic bytes of the decode GEMV launches, from one ncu
-# --set full capture of three consecutive temporal-step launches (FFN-up,
-# FFN-down, q/k/v): dram__bytes_read.sum + dram__bytes_write.sum = 23.705 MB
-# against 23.648 MB of weights, inputs and outputs.
-GEMV_TRAFFIC_OVER_ALGORITHMIC = 1.0025
-
-
-def roofline_leg(mrtdf, cfg, st, peaks: dict) -> dict:
-    """Dominant kernel = the decode GEMV phases (gemv_mma_kernel): algorithmic bytes per
-    launch / average launch time, replaying exactly the chunk's GEMV launches
-    as one CUDA graph between CUDA events (mrtdf_bench_gemv)."""
+def roofline_leg(mrtdf, eng, cfg, st, peaks: dict) -> dict:
+    """The decode phases split by where their weights live. Temporal stack
+    (fused self / cross / FFN phases, weights and cross K/V streamed from
+    HBM): algorithmic bytes per launch / average launch time against the
+    measured HBM peak. Depth stack + lm_head (weights kept in L2 with
+    evict-last hints): the same against the L2 read peak, measured here with
+    the engine's own read kernel over a 64 MiB L2-resident buffer. Each stack
+    is timed by replaying exactly its launches of one chunk as one CUDA graph
+    between CUDA events (mrtdf_bench_phases)."""
     o = mrtdf.gen_opts(cfg, 50, seed=1)
-    g_ms, g_launches, g_bytes = st.bench_gemv(o, 3)
-    per_launch_s = g_ms / 1e3 / g_launches
-    achieved = g_bytes / g_launches / per_launch_s / 1e9
-    peak = peaks.get("hbm_gbs", 6650.0)
-    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-            "traffic": g_bytes / g_launches * GEMV_TRAFFIC_OVER_ALGORITHMIC, "traffic_unit": "bytes per launch",
-            "traffic_source": "ncu capture of 3 launches, DRAM/algorithmic ratio applied to the average launch",
-            "kernel": "gemv_mma_kernel (decode GEMV phases)",
-            "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "launches_per_chunk": g_launches,
-            "bytes_per_launch": g_bytes / g_launches, "us_per_launch": per_launch_s * 1e6, "gemv_ms_per_chunk": g_ms}
+    t_ms, t_n, t_b = st.bench_phases(o, 1, 3)
+    d_ms, d_n, d_b = st.bench_phases(o, 2, 3)
+    l2_peak = eng.bench_l2_read(64 << 20, 20)
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    t_ach = t_b / t_n / (t_ms / 1e3 / t_n) / 1e9
+    d_ach = d_b / d_n / (d_ms / 1e3 / d_n) / 1e9
+    return {"bound": "hbm", "achieved": t_ach, "peak": hbm, "unit": "GB/s", "frac": t_ach / hbm,
+            "traffic": None, "traffic_unit": "bytes per launch",
+            "kernel": "temporal-stack decode phases (fused_self_kernel / fused_cross_kernel / fused_ffn_kernel)",
+            "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+            "launches_per_chunk": t_n, "bytes_per_launch": t_b / t_n, "us_per_launch": t_ms * 1e3 / t_n,
+            "ms_per_chunk": t_ms,
+            "depth": {"bound": "l2", "achieved": d_ach, "peak": l2_peak, "unit": "GB/s", "frac": d_ach / l2_peak,
+                      "peak_source": "measured: engine L2 read kernel, 64 MiB buffer, 16-byte loads on every SM",
+                      "kernel": "depth-stack decode phases + lm_head level slice", "launches_per_chunk": d_n,
+                      "bytes_per_launch": d_b / d_n, "us_per_launch": d_ms * 1e3 / d_n, "ms_per_chunk": d_ms}}
 
 
 def encoder_microbench(eng, peaks: dict) -> dict:
@@ -590,13 +596,15 @@ def multi_stream(mrtdf, torch, eng, cfg, device, rank: int, world: int, dist, n_
             "streams_rtf_ge_1": total if ms_round <= CHUNK_SECONDS * 1e3 else 0}
 
 
-def st_launch_count(cfg, frames: int = 50) -> int:
-    """Kernels of one bf16 chunk graph (our own): encoder + PAD embedding +
-    50 x (temporal layers + 16 x (depth layers + lm_head + sampler)); the
-    self-attention runs inside the q/k/v cluster launch."""
+def st_launch_count(cfg, frames: int = 50, fused: bool = True) -> int:
+    """Kernels of one bf16 chunk graph (our own) for one CFG pair: encoder +
+    PAD embedding + 50 x (temporal layers + 16 x (depth layers + lm_head +
+    sampler)). Fused phases: 3 launches per temporal layer (self, cross,
+    FFN), 2 per depth layer; otherwise 7 and 4 (the self-attention inside
+    the q/k/v cluster launch)."""
     enc = 1 + cfg.num_encoder_layers * 7 + 2
-    temporal = cfg.num_temporal_layers * 7  # qkv+attn, o, cross-q, cross-attn, cross-o, ffn-up, ffn-down
-    depth = cfg.num_depth_layers * 4 + 1 + 1  # (qkv+attn, o, ffn-up, ffn-down) x layers, lm_head, sampler
+    temporal = cfg.num_temporal_layers * (3 if fused else 7)
+    depth = cfg.num_depth_layers * (2 if fused else 4) + 1 + 1
     return enc + 1 + frames * (temporal + cfg.rvq_depth * depth)
 
 

@@ -254,15 +254,26 @@ int mrtdf_check_wait_timeout(mrtdf_stream* st, int timeout_us);
 
 /*
  * Measurement hook (no reference counterpart): replay, as one CUDA graph on
- * the stream, only the GEMV-phase launches of one generate_tokens chunk with
- * options `opts` (same buffers and parameters as the real chunk; attention
- * and sampler launches left out), `reps` times between two CUDA events.
- * Returns the milliseconds per replay, the GEMV launches per replay and their
- * algorithmic bytes (weights + input vectors + outputs). The stream must have
- * run a chunk or an encode before.
+ * the stream, only the weight-streaming decode launches of one
+ * generate_tokens chunk with options `opts` (same buffers and parameters as
+ * the real chunk; encoder and sampler left out) of the stacks in
+ * `stack_mask` (bit 0: the temporal layers, bit 1: the depth layers and
+ * lm_head), `reps` times between two CUDA events. Returns the milliseconds
+ * per replay, the launches per replay and their algorithmic bytes (weights,
+ * attention K/V reads, input and output vectors). The stream must have run
+ * a chunk or an encode before.
  */
-int mrtdf_bench_gemv(mrtdf_stream* st, const mrtdf_gen_opts* opts, int reps, float* ms_per_rep,
-                     long long* launches_per_rep, double* bytes_per_rep);
+int mrtdf_bench_phases(mrtdf_stream* st, const mrtdf_gen_opts* opts, int stack_mask, int reps, float* ms_per_rep,
+                       long long* launches_per_rep, double* bytes_per_rep);
+
+/*
+ * Measurement hook (no reference counterpart): read a `bytes` device buffer
+ * (rounded down to a multiple of 16 MiB) `reps` times with 16-byte loads
+ * spread over every SM, after one untimed pass; a buffer well under the L2
+ * size stays L2-resident, so this is the L2 read bandwidth the depth stack
+ * can reach. Reports GB/s (bytes read / CUDA-event time).
+ */
+int mrtdf_bench_l2_read(mrtdf_engine* eng, size_t bytes, int reps, double* gbs);
 
 /*
  * Measurement hook (no counterpart in the reference): the encoder pass

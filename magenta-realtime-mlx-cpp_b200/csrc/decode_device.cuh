@@ -11,6 +11,10 @@
 
 namespace mrtdf {
 
+// int64 fixed-point split sums of the fused decode phases: value x 2^32.
+constexpr float kFixInv = 2.3283064365386963e-10f;  // 2^-32
+__device__ __forceinline__ float fixed_to_float(long long a) { return __ll2float_rn(a) * kFixInv; }
+
 __device__ __forceinline__ uint64_t l2_policy(bool keep) {
   uint64_t pol;
   if (keep) asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
@@ -51,6 +55,12 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Split cluster barrier: arrive at kernel entry, wait before the first store
+// into another CTA's shared memory, so every CTA of the cluster has started.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 // Store to the same shared-memory offset in CTA `rank` of the cluster.
 __device__ __forceinline__ void st_cluster_f32(float* local, uint32_t rank, float v) {
   uint32_t ra;

@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
   constexpr int kWJ = 4;  // row chunks per lane
   constexpr int kWB = (NORM && BMAX <= 2) ? BMAX : 1;
   uint4 wx[kWB][kWJ];
-  const bool wnorm = NORM && BMAX <= 2 && (nchunk & 31) == 0 && nchunk <= 32 * kWJ;
+  const bool wnorm = NORM && BMAX <= 2 && (nchunk & 31) == 0 && nchunk <= 32 * kWJ && !p.acc;
   pdl_wait();
 #pragma unroll
   for (int b = 0; b < BMAX; ++b)
@@ -347,6 +347,31 @@ __global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const GemvParams p, co
                                               : make_uint4(0, 0, 0, 0);
         }
     }
+  }
+  if (p.acc) {
+    // x = R(residual + R(acc / 2^32)): the hidden state the fused decode
+    // phases leave (rows of x_stride elements in both buffers)
+#pragma unroll
+    for (int b = 0; b < BMAX; ++b)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int ch = tid + i * 256;
+        if (b < p.B && ch < nchunk) {
+          float f[8];
+          Vec16<T>::unpack(xin[b][i], f);
+          const longlong2* ap = reinterpret_cast<const longlong2*>(p.acc + (size_t)b * p.x_stride + ch * 8);
+          uint32_t o[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const longlong2 a = ap[q];
+            const float v0 = rnd<T>(__fadd_rn(f[2 * q], rnd<T>(fixed_to_float(a.x))));
+            const float v1 = rnd<T>(__fadd_rn(f[2 * q + 1], rnd<T>(fixed_to_float(a.y))));
+            const __nv_bfloat162 pr = __floats2bfloat162_rn(v0, v1);
+            o[q] = *reinterpret_cast<const uint32_t*>(&pr);
+          }
+          xin[b][i] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
   }
   // residual values of the epilogue (same thread -> (unit, row) mapping)
   const int nunits = u1 - u0;
@@ -789,6 +814,7 @@ static cudaError_t launch_gemv_mma_b(int mode, bool norm, const GemvParams& p, i
 
 static cudaError_t launch_gemv_mma(int mode, bool norm, const GemvParams& p, int num_sms, cudaStream_t s, bool pdl) {
   if (p.cols % 16 != 0 || p.cols > 4096 || p.B > kGemvMaxB || p.B <= 0) return cudaErrorInvalidValue;
+  if (p.acc && (p.B > 2 || (p.x_stride & 7) != 0)) return cudaErrorInvalidValue;
   if (p.B <= 2) return launch_gemv_mma_b<2>(mode, norm, p, num_sms, s, pdl);
   if (p.B <= 4) return launch_gemv_mma_b<4>(mode, norm, p, num_sms, s, pdl);
   return launch_gemv_mma_b<8>(mode, norm, p, num_sms, s, pdl);
@@ -878,6 +904,7 @@ static cudaError_t dispatch_b(int mode, bool norm, const GemvParams& p, int grid
 cudaError_t launch_gemv(int dtype, int mode, bool norm, const GemvParams& p, int num_sms, cudaStream_t s, bool pdl) {
   if (p.units <= 0) return cudaSuccess;
   if (dtype == 1) return launch_gemv_mma(mode, norm, p, num_sms, s, pdl);
+  if (p.acc) return cudaErrorInvalidValue;
   const int rpu = mode == kGemvGeglu ? 2 : 1;
   if (p.cols % 4 != 0 || rpu * p.cols * 4 > kGemvStageBytes) return cudaErrorInvalidValue;
   const int grid = p.units < num_sms ? p.units : num_sms;
@@ -1459,6 +1486,33 @@ cudaError_t sample_scratch_address(int device, void** out) {
   }
   *out = addr[device];
   return cudaSuccess;
+}
+
+// ---------------------------------------------------------------------------
+// Read bandwidth probe: every thread streams 16-byte loads (L1 bypassed) over
+// a grid-strided range and folds them into one word per CTA, so the loads
+// cannot be elided.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) l2_read_kernel(const uint4* buf, size_t n16, unsigned* sink) {
+  unsigned acc = 0;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < n16; i += 4 * stride) {
+    const uint4 a = __ldcg(buf + i), b = __ldcg(buf + i + stride), c = __ldcg(buf + i + 2 * stride),
+                d = __ldcg(buf + i + 3 * stride);
+    acc ^= a.x ^ a.y ^ a.z ^ a.w ^ b.x ^ b.y ^ b.z ^ b.w ^ c.x ^ c.y ^ c.z ^ c.w ^ d.x ^ d.y ^ d.z ^ d.w;
+  }
+  for (; i < n16; i += stride) {
+    const uint4 a = __ldcg(buf + i);
+    acc ^= a.x ^ a.y ^ a.z ^ a.w;
+  }
+  acc = __reduce_xor_sync(0xffffffffu, acc);
+  if ((threadIdx.x & 31) == 0) atomicXor(sink + (blockIdx.x & 4095), acc);
+}
+
+cudaError_t launch_l2_read(const void* buf, size_t bytes, unsigned* sink, int num_sms, cudaStream_t s) {
+  l2_read_kernel<<<num_sms * 4, 256, 0, s>>>(reinterpret_cast<const uint4*>(buf), bytes / 16, sink);
+  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------

@@ -32,6 +32,9 @@ struct GemvParams {
   void* kc;
   void* vc;
   int* err;
+  // bf16 only, B <= 2: when not null, x = R(x + R(acc / 2^32)) per element
+  // (a hidden state left by the fused decode phases; x is its residual)
+  const long long* acc;
   int units;
   int cols;
   int B;
@@ -120,6 +123,10 @@ constexpr size_t kSampleScratchBytes = 64 * 1024;
 constexpr size_t kSampleScratchRowBytes = (kSampleScratchBytes - 256) / 3 / 256 * 256;
 // Device address of that scratch on `device` (looked up once per device).
 cudaError_t sample_scratch_address(int device, void** out);
+
+// Read `bytes` (a multiple of 16 MiB) of `buf` once with 16-byte loads over
+// 4 CTAs per SM; `sink` (4096 words) receives one word per CTA.
+cudaError_t launch_l2_read(const void* buf, size_t bytes, unsigned* sink, int num_sms, cudaStream_t s);
 
 // One CTA waiting on an mbarrier that nothing completes, bounded by
 // timeout_ns: sets kErrMbarTimeout in *err (failure-detection check).

@@ -29,6 +29,7 @@
 #include "glue_kernels.cuh"
 #include "device_errors.h"
 #include "encoder_kernels.cuh"
+#include "fused_decode.cuh"
 #include "host_util.h"
 
 using namespace mrtdf;
@@ -75,6 +76,16 @@ struct EncLayerDev {
 };
 struct DecLayerDev {
   void *wqkv, *wo, *n_self, *wcq, *wco, *n_cross, *wi, *wout, *n_ffn;
+  // blocked copies for the fused phases (bf16): o_proj / cross o_proj as
+  // [H][8][d/8][64 + 8 pad], wo as [nclusters][8][d/8][Uc + 8 pad]
+  void *wo_blk = nullptr, *wco_blk = nullptr, *wout_blk = nullptr;
+};
+
+// A hidden state between decode phases: `x` itself, or (fused phases)
+// R(x + R(acc / 2^32)) with x the residual stream and acc the split sums.
+struct Hidden {
+  const void* x;
+  const long long* acc;
 };
 
 }  // namespace
@@ -92,6 +103,9 @@ struct mrtdf_engine {
   // wide streams: largest split-K cluster of the tcgen05 decode GEMMs
   // (MRTDF_WIDE_KSPLIT; 64 CFG pairs: 607 ms per chunk unsplit, 504 ms at 8)
   int wide_ksplit = 8;
+  // fused decode phases for streams of at most two bf16 rows (one CFG pair)
+  bool fused = false;
+  FfnPlan ffn_plan;
   Arena weights;
   void* emb = nullptr;
   void* enc_norm = nullptr;
@@ -128,6 +142,12 @@ struct mrtdf_stream {
   // encoder scratch
   void *ex, *en, *eqkv, *eo, *eh;
   void* xn;  // (B, d) normalised rows of the wide decode path
+  // fused phases: three int64 accumulators (B, d) in a rotation, two bf16
+  // residual buffers (B, d), and their ring positions
+  bool fused = false;
+  long long* facc = nullptr;
+  void* fx[2] = {nullptr, nullptr};
+  int fk = 0, fj = 0;
   int32_t* ids;
   int32_t* tokens;  // (nseq, Tmax, depth)
   uint64_t* seeds;  // (nseq)
@@ -147,7 +167,12 @@ struct mrtdf_stream {
   long long last_chunk_kernels = 0;              // of the chunk run last (graph or stream launches)
   // measurement hook: when set, only the GEMV phases are enqueued and their
   // launches / algorithmic bytes are counted
+  // measurement hook: when set, only the weight-streaming decode phases of
+  // the selected stacks (bit 0 temporal, bit 1 depth + lm_head) are
+  // enqueued and their launches / algorithmic bytes are counted
   bool gemv_only = false;
+  int phase_mask = 3;
+  bool in_depth = false;
   long long gemv_launches = 0;
   double gemv_bytes = 0.0;
   ~mrtdf_stream() {
@@ -212,6 +237,12 @@ static void upload_weights(mrtdf_engine* E, const WeightSource& src) {
   const size_t tb = (size_t)c.max_frames * c.num_heads * c.max_frames * 4;
   const size_t db = (size_t)c.rvq_depth * c.num_heads * c.rvq_depth * 4;
   const size_t pb = (size_t)c.max_encoder_length * d * 4;
+  if (E->fused) {
+    const int64_t blk = (int64_t)c.num_heads * kFusedCluster * (d / kFusedCluster) * 72;  // o_proj block elements
+    const int64_t oblk = (int64_t)E->ffn_plan.nclusters * kFusedCluster * (d / kFusedCluster) * (E->ffn_plan.Uc + 8);
+    for (int i = 0; i < c.num_temporal_layers; ++i) { add(blk); add(blk); add(oblk); }
+    for (int i = 0; i < c.num_depth_layers; ++i) { add(blk); add(oblk); }
+  }
   total += tb + db + pb + 3 * 256;
   E->weights.reserve(total);
 
@@ -322,6 +353,50 @@ static void upload_weights(mrtdf_engine* E, const WeightSource& src) {
   E->dec_norm = single("decoder_norm.weight", d);
   E->lm_head = single("lm_head.weight", V * d);
 
+  if (E->fused) {
+    // o_proj (d, inner) -> [h][r][n][c]: row n of slice r = output dim
+    // r * d/8 + n, columns c < 64 = head h's attention outputs, 8 zeros after
+    const int64_t dpc = d / kFusedCluster, H = c.num_heads;
+    auto o_block = [&](const std::string& key) {
+      const float* w = fetch(key, d * in);
+      tmp.assign((size_t)(H * kFusedCluster * dpc * 72), 0.f);
+      for (int64_t h = 0; h < H; ++h)
+        for (int64_t r = 0; r < kFusedCluster; ++r)
+          for (int64_t n = 0; n < dpc; ++n)
+            for (int64_t cc = 0; cc < 64; ++cc)
+              tmp[(size_t)((((h * kFusedCluster + r) * dpc + n) * 72) + cc)] = w[(r * dpc + n) * in + h * 64 + cc];
+      void* dst = E->weights.take(tmp.size() * es);
+      put(dst, tmp.data(), (int64_t)tmp.size());
+      return dst;
+    };
+    // wo (d, ff) -> [j][r][n][u]: row n of slice r = output dim r * d/8 + n,
+    // columns u < Uc = d_ff units j * Uc + u (zero past ff), 8 zeros after
+    const int64_t NC = E->ffn_plan.nclusters, Uc = E->ffn_plan.Uc, Ur = Uc + 8;
+    auto ffn_block = [&](const std::string& key) {
+      const float* w = fetch(key, d * ff);
+      tmp.assign((size_t)(NC * kFusedCluster * dpc * Ur), 0.f);
+      for (int64_t j = 0; j < NC; ++j)
+        for (int64_t r = 0; r < kFusedCluster; ++r)
+          for (int64_t n = 0; n < dpc; ++n)
+            for (int64_t u = 0; u < Uc && j * Uc + u < ff; ++u)
+              tmp[(size_t)((((j * kFusedCluster + r) * dpc + n) * Ur) + u)] = w[(r * dpc + n) * ff + j * Uc + u];
+      void* dst = E->weights.take(tmp.size() * es);
+      put(dst, tmp.data(), (int64_t)tmp.size());
+      return dst;
+    };
+    for (int i = 0; i < c.num_temporal_layers; ++i) {
+      const std::string p = "temporal_layers." + std::to_string(i) + ".";
+      E->tl[i].wo_blk = o_block(p + "self_attn.o_proj.weight");
+      E->tl[i].wco_blk = o_block(p + "cross_attn.o_proj.weight");
+      E->tl[i].wout_blk = ffn_block(p + "ffn.wo.weight");
+    }
+    for (int i = 0; i < c.num_depth_layers; ++i) {
+      const std::string p = "depth_layers." + std::to_string(i) + ".";
+      E->dl[i].wo_blk = o_block(p + "self_attn.o_proj.weight");
+      E->dl[i].wout_blk = ffn_block(p + "ffn.wo.weight");
+    }
+  }
+
   // Relative-position bias per query position (precompute_*_biases,
   // model.cpp:302-320): bias[q][h][j] = table[bucket(j - q)][h], j <= q,
   // table values in the compute dtype (load_param casts, modules.cpp:127-128).
@@ -388,8 +463,12 @@ void wide_gemv(mrtdf_stream* st, int mode, bool norm, const GemvParams& p) {
   check_cuda(launch_gemm_tc(epi, g, st->err, st->s, E->pdl), "wide decode gemm");
 }
 
+// In the measurement hook, whether the current stack's phases are enqueued.
+bool phase_on(const mrtdf_stream* st) { return !st->gemv_only || (st->phase_mask & (st->in_depth ? 2 : 1)); }
+
 void gemv(mrtdf_stream* st, int mode, bool norm, GemvParams p) {
   mrtdf_engine* E = st->eng;
+  if (!phase_on(st)) return;
   p.err = st->err;
   p.B = st->B;
   // algorithmic bytes: weight rows + input rows + output rows (+ residual)
@@ -475,40 +554,148 @@ size_t layer_cache_elems(const mrtdf_stream* st, int cap) {
   return (size_t)st->B * st->eng->c.num_heads * cap * 64;
 }
 
-// temporal_step: 20 decoder layers over tin -> tx (model.cpp:493-513).
-void enqueue_temporal(mrtdf_stream* st, int f) {
+// ---- fused phases (bf16, at most two rows) ----------------------------------
+// Start of a phase chain: the three accumulators are zero, the ring at 0.
+void fused_reset(mrtdf_stream* st) {
+  if (!st->fused) return;
+  CUDA_OK(cudaMemsetAsync(st->facc, 0, (size_t)3 * st->B * st->eng->c.d_model * 8, st->s));
+  st->fk = 0;
+  st->fj = 0;
+}
+
+long long* facc_at(mrtdf_stream* st, int k) { return st->facc + (size_t)(k % 3) * st->B * st->eng->c.d_model; }
+
+// Inputs / outputs of the next phase consuming `in`; returns the hidden
+// state after that phase (its residual stream + the accumulator it adds to).
+Hidden fused_io(mrtdf_stream* st, Hidden in, FusedIn& f) {
+  if (in.acc && in.acc != facc_at(st, st->fk)) throw Error{MRTDF_ERR_STATE, "fused phase ring out of order"};
+  f = FusedIn{};
+  f.x = in.x;
+  f.acc = in.acc;
+  f.err = st->err;
+  f.B = st->B;
+  f.d = st->eng->c.d_model;
+  const void* resid = in.x;
+  if (in.acc) {
+    f.x_out = st->fx[st->fj];
+    resid = st->fx[st->fj];
+    st->fj ^= 1;
+  }
+  f.acc_out = facc_at(st, st->fk + 1);
+  f.acc_clear = facc_at(st, st->fk + 2);
+  st->fk = (st->fk + 1) % 3;
+  return Hidden{resid, f.acc_out};
+}
+
+// One DecoderLayer::forward as fused phases: self (+ cross) + FFN.
+Hidden enqueue_fused_layer(mrtdf_stream* st, const DecLayerDev& L, Hidden in, void* kc, void* vc, int cap, int pos,
+                           const float* bias, int bias_stride, const void* ck, const void* cv, bool l2_keep) {
+  mrtdf_engine* E = st->eng;
+  const mrtdf_config& c = E->c;
+  const double es = E->esize, d = c.d_model, in_ = E->inner(), ff = c.d_ff, B = st->B;
+  const bool on = phase_on(st);
+  FusedSelfParams sp{};
+  Hidden h = fused_io(st, in, sp.in);
+  sp.wqkv = L.wqkv; sp.norm_w = L.n_self; sp.wo_blk = L.wo_blk; sp.kc = kc; sp.vc = vc; sp.bias = bias;
+  sp.bias_stride = bias_stride; sp.H = c.num_heads; sp.cap = cap; sp.pos = pos; sp.l2_keep = l2_keep;
+  if (on) {
+    check_cuda(launch_fused_self(sp, st->s, E->pdl), "fused self phase");
+    st->gemv_launches += 1;
+    st->gemv_bytes += (4.0 * in_ * d + d) * es + 2.0 * B * c.num_heads * (pos + 1) * 64.0 * es + 2.0 * B * d * es;
+  }
+  if (ck) {
+    FusedCrossParams cp{};
+    h = fused_io(st, h, cp.in);
+    cp.wcq = L.wcq; cp.norm_w = L.n_cross; cp.wco_blk = L.wco_blk; cp.ck = ck; cp.cv = cv; cp.H = c.num_heads;
+    cp.Smax = c.max_encoder_length; cp.S = st->S; cp.l2_keep = l2_keep;
+    if (on) {
+      check_cuda(launch_fused_cross(cp, st->s, E->pdl), "fused cross phase");
+      st->gemv_launches += 1;
+      st->gemv_bytes += (2.0 * in_ * d + d) * es + 2.0 * B * c.num_heads * st->S * 64.0 * es + 2.0 * B * d * es;
+    }
+  }
+  FusedFfnParams fp{};
+  h = fused_io(st, h, fp.in);
+  fp.wi = L.wi; fp.norm_w = L.n_ffn; fp.wout_blk = L.wout_blk; fp.ff = c.d_ff; fp.Uc = E->ffn_plan.Uc;
+  fp.nclusters = E->ffn_plan.nclusters; fp.l2_keep = l2_keep;
+  if (on) {
+    check_cuda(launch_fused_ffn(fp, st->s, E->pdl), "fused ffn phase");
+    st->gemv_launches += 1;
+    st->gemv_bytes += (3.0 * ff * d + d) * es + 2.0 * B * d * es;
+  }
+  return h;
+}
+
+// Write a hidden state out as plain bf16 rows (the step-level entry points).
+void materialize(mrtdf_stream* st, Hidden h, void* out) {
+  if (!h.acc) {
+    if (h.x != out)
+      CUDA_OK(cudaMemcpyAsync(out, h.x, act_bytes(st->eng, (size_t)st->B * st->eng->c.d_model),
+                              cudaMemcpyDeviceToDevice, st->s));
+    return;
+  }
+  FusedIn f{};
+  f.x = h.x;
+  f.acc = h.acc;
+  f.B = st->B;
+  f.d = st->eng->c.d_model;
+  check_cuda(launch_fused_materialize(f, out, st->s, st->eng->pdl), "materialize");
+}
+
+// temporal_step: 20 decoder layers over tin (model.cpp:493-513). Returns
+// the stack output (tx when the phases are not fused).
+Hidden enqueue_temporal(mrtdf_stream* st, int f) {
   mrtdf_engine* E = st->eng;
   const mrtdf_config& c = E->c;
   const size_t tcs = layer_cache_elems(st, c.max_frames);
   const size_t ccs = layer_cache_elems(st, c.max_encoder_length);
+  st->in_depth = false;
+  Hidden h{st->tin, nullptr};
   for (int l = 0; l < c.num_temporal_layers; ++l) {
     uint8_t* tk = (uint8_t*)st->tk + act_bytes(E, tcs * l);
     uint8_t* tv = (uint8_t*)st->tv + act_bytes(E, tcs * l);
     const uint8_t* ck = (const uint8_t*)st->ck + act_bytes(E, ccs * l);
     const uint8_t* cv = (const uint8_t*)st->cv + act_bytes(E, ccs * l);
-    enqueue_decoder_layer(st, E->tl[l], l == 0 ? st->tin : st->tx, st->tx, tk, tv, c.max_frames, f,
-                          E->tbias + (size_t)f * c.num_heads * c.max_frames, c.max_frames, ck, cv,
-                          /*l2_keep=*/false);
+    const float* bias = E->tbias + (size_t)f * c.num_heads * c.max_frames;
+    if (st->fused) {
+      h = enqueue_fused_layer(st, E->tl[l], h, tk, tv, c.max_frames, f, bias, c.max_frames, ck, cv,
+                              /*l2_keep=*/false);
+    } else {
+      enqueue_decoder_layer(st, E->tl[l], l == 0 ? st->tin : st->tx, st->tx, tk, tv, c.max_frames, f, bias,
+                            c.max_frames, ck, cv, /*l2_keep=*/false);
+      h = Hidden{st->tx, nullptr};
+    }
   }
+  return h;
 }
 
 // depth_step: 4 decoder layers + decoder_norm + lm_head rows [lo, hi).
-void enqueue_depth(mrtdf_stream* st, int level, const void* x_in, int lo, int hi) {
+void enqueue_depth(mrtdf_stream* st, int level, Hidden in, int lo, int hi) {
   mrtdf_engine* E = st->eng;
   const mrtdf_config& c = E->c;
   const size_t dcs = layer_cache_elems(st, c.rvq_depth);
+  st->in_depth = true;
+  Hidden h = in;
   for (int l = 0; l < c.num_depth_layers; ++l) {
     uint8_t* dk = (uint8_t*)st->dk + act_bytes(E, dcs * l);
     uint8_t* dv = (uint8_t*)st->dv + act_bytes(E, dcs * l);
-    enqueue_decoder_layer(st, E->dl[l], l == 0 ? x_in : st->dx, st->dx, dk, dv, c.rvq_depth, level,
-                          E->dbias + (size_t)level * c.num_heads * c.rvq_depth, c.rvq_depth, nullptr, nullptr,
-                          /*l2_keep=*/true);
+    const float* bias = E->dbias + (size_t)level * c.num_heads * c.rvq_depth;
+    if (st->fused) {
+      h = enqueue_fused_layer(st, E->dl[l], h, dk, dv, c.rvq_depth, level, bias, c.rvq_depth, nullptr, nullptr,
+                              /*l2_keep=*/true);
+    } else {
+      if (h.acc) throw Error{MRTDF_ERR_STATE, "depth_step: unfused layers need a plain input"};
+      enqueue_decoder_layer(st, E->dl[l], l == 0 ? h.x : st->dx, st->dx, dk, dv, c.rvq_depth, level, bias,
+                            c.rvq_depth, nullptr, nullptr, /*l2_keep=*/true);
+    }
   }
   GemvParams p{};
   p.W = (const uint8_t*)E->lm_head + act_bytes(E, (size_t)lo * c.d_model);
-  p.x = st->dx; p.norm_w = E->dec_norm; p.out = st->logits; p.units = hi - lo; p.cols = c.d_model;
+  p.x = st->fused ? h.x : st->dx; p.acc = st->fused ? h.acc : nullptr;
+  p.norm_w = E->dec_norm; p.out = st->logits; p.units = hi - lo; p.cols = c.d_model;
   p.x_stride = c.d_model; p.out_stride = c.vocab_size; p.out_offset = lo; p.l2_keep = 1;
   gemv(st, kGemvLogits, true, p);
+  st->in_depth = false;
 }
 
 // encode: embed + PE, encoder layers, encoder_norm, cross K/V of every
@@ -601,12 +788,13 @@ void enqueue_chunk(mrtdf_stream* st, int S, const mrtdf_gen_opts& o) {
     check_cuda(launch_embed_rows(c.dtype, E->emb, nullptr, st->B, c.d_model, st->tin, st->s, E->pdl), "embed pad");
   }
   const bool masked = o.use_vocab_masks != 0;
+  fused_reset(st);
   for (int f = 0; f < o.num_frames; ++f) {
-    enqueue_temporal(st, f);
+    const Hidden t = enqueue_temporal(st, f);
     for (int l = 0; l < c.rvq_depth; ++l) {
       int lo, hi;
       level_range(c, masked, l, lo, hi);
-      enqueue_depth(st, l, l == 0 ? st->tx : st->din, lo, hi);
+      enqueue_depth(st, l, l == 0 ? t : Hidden{st->din, nullptr}, lo, hi);
       if (!st->gemv_only) enqueue_sample(st, f, l, o, masked, lo, hi, false);
     }
   }
@@ -669,6 +857,9 @@ void check_device_err(mrtdf_stream* st) {
   const int h = read_err(st);
   if (h & (kErrMbarTimeout | kErrCounterTimeout))
     throw Error{MRTDF_ERR_TIMEOUT, "a device-side bounded wait gave up (error word " + std::to_string(h) + ")"};
+  if (h & kErrFixedRange)
+    throw Error{MRTDF_ERR_INVALID,
+                "a decode activation left the range of the fixed-point split sums (NaN or |x| >= 2^30)"};
   if (h & kErrBadToken)
     throw Error{MRTDF_ERR_INVALID,
                 "the sampler found no valid candidate (NaN logits or an empty vocabulary range) or an id outside the "
@@ -770,6 +961,13 @@ int mrtdf_create(const mrtdf_config* cfg, int device, mrtdf_engine** out) {
     if (const char* v = std::getenv("MRTDF_WIDE_KSPLIT")) E->wide_ksplit = std::max(1, std::min(8, std::atoi(v)));
     CUDA_OK(gemv_set_smem_limits());
     CUDA_OK(gemm_tc_set_smem_limits());
+    CUDA_OK(fused_set_smem_limits());
+    E->fused = cfg->dtype == MRTDF_DTYPE_BF16 && env_flag("MRTDF_FUSED", true) &&
+               fused_supported(cfg->d_model, cfg->num_heads, cfg->d_kv, cfg->d_ff);
+    if (E->fused && fused_ffn_plan(cfg->d_model, cfg->d_ff, E->num_sms, &E->ffn_plan) != cudaSuccess) {
+      cudaGetLastError();  // no FFN plan fits this device: the per-projection path serves every stream
+      E->fused = false;
+    }
     CUDA_OK(sample_set_smem_limits());
     *out = E.release();
   });
@@ -860,6 +1058,12 @@ int mrtdf_stream_create(mrtdf_engine* E, int num_sequences, int cfg, mrtdf_strea
         {(void**)&st->tokens, (size_t)num_sequences * c.max_frames * c.rvq_depth * 4},
         {(void**)&st->seeds, (size_t)num_sequences * 8}, {(void**)&st->forced, (size_t)num_sequences * 4},
         {(void**)&st->err, 64}};
+    st->fused = E->fused && st->B <= kFusedMaxRows;
+    if (st->fused) {
+      plan.push_back({(void**)&st->facc, 3 * B * d * 8});
+      plan.push_back({&st->fx[0], B * d * es});
+      plan.push_back({&st->fx[1], B * d * es});
+    }
     size_t total = 0;
     for (auto& p : plan) total += (p.second + 255) & ~(size_t)255;
     st->mem.reserve(total);
@@ -957,7 +1161,8 @@ int mrtdf_temporal_step(mrtdf_stream* st, const float* x, int frame_idx, float* 
     CUDA_OK(cudaSetDevice(E->device));
     if (x) upload_act(st, x, st->tin);
     else check_cuda(launch_embed_rows(E->c.dtype, E->emb, nullptr, st->B, E->c.d_model, st->tin, st->s, false), "pad");
-    enqueue_temporal(st, frame_idx);
+    fused_reset(st);
+    materialize(st, enqueue_temporal(st, frame_idx), st->tx);
     st->t_len = frame_idx + 1;
     st->have_temporal = true;
     if (out) download_act(st, st->tx, out);
@@ -982,7 +1187,8 @@ int mrtdf_depth_step(mrtdf_stream* st, const float* x, int depth_idx, float* log
       if (!st->have_temporal) throw Error{MRTDF_ERR_STATE, "depth_step: no temporal output to start from"};
       in = st->tx;
     }
-    enqueue_depth(st, depth_idx, in, 0, c.vocab_size);
+    fused_reset(st);
+    enqueue_depth(st, depth_idx, Hidden{in, nullptr}, 0, c.vocab_size);
     st->d_len = depth_idx + 1;
     if (logits)
       CUDA_OK(cudaMemcpyAsync(logits, st->logits, (size_t)st->B * c.vocab_size * 4, cudaMemcpyDeviceToHost, st->s));
@@ -1226,10 +1432,11 @@ int mrtdf_teacher_forced_logits(mrtdf_stream* st, const int32_t* enc_ids, int se
     enqueue_encode(st, seq_len);
     check_cuda(launch_embed_rows(c.dtype, E->emb, nullptr, st->B, c.d_model, st->tin, st->s, false), "pad");
     const size_t V = c.vocab_size;
+    fused_reset(st);
     for (int f = 0; f < num_frames; ++f) {
-      enqueue_temporal(st, f);
+      const Hidden t = enqueue_temporal(st, f);
       for (int l = 0; l < c.rvq_depth; ++l) {
-        enqueue_depth(st, l, l == 0 ? st->tx : st->din, 0, c.vocab_size);
+        enqueue_depth(st, l, l == 0 ? t : Hidden{st->din, nullptr}, 0, c.vocab_size);
         CUDA_OK(cudaMemcpyAsync(logits + ((size_t)f * c.rvq_depth + l) * st->B * V, st->logits,
                                 (size_t)st->B * V * 4, cudaMemcpyDeviceToHost, st->s));
         const int32_t tok = tokens[(size_t)f * c.rvq_depth + l];
@@ -1247,16 +1454,17 @@ int mrtdf_teacher_forced_logits(mrtdf_stream* st, const int32_t* enc_ids, int se
   });
 }
 
-int mrtdf_bench_gemv(mrtdf_stream* st, const mrtdf_gen_opts* o, int reps, float* ms_per_rep,
-                     long long* launches_per_rep, double* bytes_per_rep) {
+int mrtdf_bench_phases(mrtdf_stream* st, const mrtdf_gen_opts* o, int stack_mask, int reps, float* ms_per_rep,
+                       long long* launches_per_rep, double* bytes_per_rep) {
   return guarded([&] {
-    if (!st || !o || reps <= 0 || !ms_per_rep || !launches_per_rep || !bytes_per_rep)
+    if (!st || !o || reps <= 0 || !ms_per_rep || !launches_per_rep || !bytes_per_rep || stack_mask < 1 || stack_mask > 3)
       throw Error{MRTDF_ERR_INVALID, "bad argument"};
     if (!st->encoded) throw Error{MRTDF_ERR_STATE, "run a chunk (or encode) first"};
     validate_opts(st, o, st->S);
     CUDA_OK(cudaSetDevice(st->eng->device));
     cudaGraph_t g = nullptr;
     st->gemv_only = true;
+    st->phase_mask = stack_mask;
     st->gemv_launches = 0;
     st->gemv_bytes = 0.0;
     CUDA_OK(cudaStreamBeginCapture(st->s, cudaStreamCaptureModeThreadLocal));
@@ -1264,11 +1472,13 @@ int mrtdf_bench_gemv(mrtdf_stream* st, const mrtdf_gen_opts* o, int reps, float*
       enqueue_chunk(st, st->S, *o);
     } catch (...) {
       st->gemv_only = false;
+      st->phase_mask = 3;
       cudaStreamEndCapture(st->s, &g);
       if (g) cudaGraphDestroy(g);
       throw;
     }
     st->gemv_only = false;
+    st->phase_mask = 3;
     CUDA_OK(cudaStreamEndCapture(st->s, &g));
     cudaGraphExec_t ex = nullptr;
     const cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
@@ -1294,6 +1504,45 @@ int mrtdf_bench_gemv(mrtdf_stream* st, const mrtdf_gen_opts* o, int reps, float*
   });
 }
 
+int mrtdf_bench_l2_read(mrtdf_engine* E, size_t bytes, int reps, double* gbs) {
+  return guarded([&] {
+    if (!E || !gbs || reps <= 0) throw Error{MRTDF_ERR_INVALID, "bad argument"};
+    const size_t unit = (size_t)16 << 20;
+    bytes = bytes / unit * unit;
+    if (bytes == 0 || bytes > ((size_t)1 << 34)) throw Error{MRTDF_ERR_RANGE, "bytes must be in [16 MiB, 16 GiB]"};
+    CUDA_OK(cudaSetDevice(E->device));
+    uint8_t* buf = nullptr;
+    unsigned* sink = nullptr;
+    CUDA_OK(cudaMalloc(&buf, bytes));
+    struct Free {
+      void* a;
+      void* b;
+      ~Free() {
+        cudaFree(a);
+        cudaFree(b);
+      }
+    } fr{buf, nullptr};
+    CUDA_OK(cudaMalloc(&sink, 4 * 4096));
+    fr.b = sink;
+    cudaStream_t s = nullptr;
+    CUDA_OK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    CUDA_OK(cudaMemsetAsync(buf, 1, bytes, s));
+    check_cuda(launch_l2_read(buf, bytes, sink, E->num_sms, s), "l2 read");  // warm-up: the buffer lands in L2
+    cudaEvent_t a, b;
+    CUDA_OK(cudaEventCreate(&a));
+    CUDA_OK(cudaEventCreate(&b));
+    CUDA_OK(cudaEventRecord(a, s));
+    for (int r = 0; r < reps; ++r) check_cuda(launch_l2_read(buf, bytes, sink, E->num_sms, s), "l2 read");
+    CUDA_OK(cudaEventRecord(b, s));
+    CUDA_OK(cudaEventSynchronize(b));
+    float ms = 0.f;
+    CUDA_OK(cudaEventElapsedTime(&ms, a, b));
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    cudaStreamDestroy(s);
+    *gbs = (double)bytes * reps / (ms * 1e-3) / 1e9;
+  });
+}
 
 int mrtdf_bench_encoder(mrtdf_engine* E, int rows, int seq_len, int reps, float* ms_per_rep, double* flops_per_rep) {
   return guarded([&] {
@@ -1401,11 +1650,13 @@ int mrtdf_bench_depth(mrtdf_stream* st, const mrtdf_gen_opts* o, int frames, int
     cudaGraph_t g = nullptr;
     CUDA_OK(cudaStreamBeginCapture(st->s, cudaStreamCaptureModeThreadLocal));
     try {
+      fused_reset(st);
       for (int f = 0; f < frames; ++f)
         for (int l = 0; l < c.rvq_depth; ++l) {
           int lo, hi;
           level_range(c, masked, l, lo, hi);
-          enqueue_depth(st, l, l == 0 ? (const void*)(xd + act_bytes(E, per_frame * f)) : st->din, lo, hi);
+          enqueue_depth(st, l, Hidden{l == 0 ? (const void*)(xd + act_bytes(E, per_frame * f)) : st->din, nullptr},
+                        lo, hi);
           enqueue_sample(st, f, l, *o, masked, lo, hi, false);
         }
     } catch (...) {
@@ -1438,10 +1689,11 @@ int mrtdf_bench_depth(mrtdf_stream* st, const mrtdf_gen_opts* o, int frames, int
     for (int l = 0; l < c.rvq_depth; ++l)
       kv += 2.0 * c.num_depth_layers * st->B * c.num_heads * (l + 1) * 64.0 * E->esize;
     *bytes_per_step = (st->gemv_bytes + kv * frames) / steps;
-    // per level: layers x (QKV, attention, o_proj, FFN-up, FFN-down) + lm_head + sampler;
-    // the attention runs inside the QKV launch when fused
-    const bool fused = c.dtype == MRTDF_DTYPE_BF16 && st->B <= kQkvCluster && E->cluster_attn;
-    *launches_per_step = (long long)c.num_depth_layers * (fused ? 4 : 5) + 2;
+    // per level: layers x (self phase, FFN phase) + lm_head + sampler on the
+    // fused path; else layers x (QKV, attention, o_proj, FFN-up, FFN-down)
+    // with the attention inside the QKV launch for bf16 cluster attention
+    const bool cl = c.dtype == MRTDF_DTYPE_BF16 && st->B <= kQkvCluster && E->cluster_attn;
+    *launches_per_step = (long long)c.num_depth_layers * (st->fused ? 2 : cl ? 4 : 5) + 2;
     check_device_err(st);
   });
 }
@@ -1520,18 +1772,36 @@ int mrtdf_probe_decoder_layer(mrtdf_stream* st, int stack, int layer, int pos, c
     if (stack == 0) {
       const size_t tcs = layer_cache_elems(st, c.max_frames), ccs = layer_cache_elems(st, c.max_encoder_length);
       upload_act(st, x, st->tin);
-      enqueue_decoder_layer(st, E->tl[layer], st->tin, st->tx, (uint8_t*)st->tk + tcs * es * layer,
-                            (uint8_t*)st->tv + tcs * es * layer, c.max_frames, pos,
-                            E->tbias + (size_t)pos * c.num_heads * c.max_frames, c.max_frames,
-                            (const uint8_t*)st->ck + ccs * es * layer, (const uint8_t*)st->cv + ccs * es * layer,
-                            false);
+      void* tk = (uint8_t*)st->tk + tcs * es * layer;
+      void* tv = (uint8_t*)st->tv + tcs * es * layer;
+      const float* bias = E->tbias + (size_t)pos * c.num_heads * c.max_frames;
+      const void* ck = (const uint8_t*)st->ck + ccs * es * layer;
+      const void* cv = (const uint8_t*)st->cv + ccs * es * layer;
+      if (st->fused) {
+        fused_reset(st);
+        materialize(st, enqueue_fused_layer(st, E->tl[layer], Hidden{st->tin, nullptr}, tk, tv, c.max_frames, pos,
+                                            bias, c.max_frames, ck, cv, false),
+                    st->tx);
+      } else {
+        enqueue_decoder_layer(st, E->tl[layer], st->tin, st->tx, tk, tv, c.max_frames, pos, bias, c.max_frames, ck,
+                              cv, false);
+      }
       download_act(st, st->tx, out);
     } else {
       const size_t dcs = layer_cache_elems(st, c.rvq_depth);
       upload_act(st, x, st->din);
-      enqueue_decoder_layer(st, E->dl[layer], st->din, st->dx, (uint8_t*)st->dk + dcs * es * layer,
-                            (uint8_t*)st->dv + dcs * es * layer, c.rvq_depth, pos,
-                            E->dbias + (size_t)pos * c.num_heads * c.rvq_depth, c.rvq_depth, nullptr, nullptr, true);
+      void* dk = (uint8_t*)st->dk + dcs * es * layer;
+      void* dv = (uint8_t*)st->dv + dcs * es * layer;
+      const float* bias = E->dbias + (size_t)pos * c.num_heads * c.rvq_depth;
+      if (st->fused) {
+        fused_reset(st);
+        materialize(st, enqueue_fused_layer(st, E->dl[layer], Hidden{st->din, nullptr}, dk, dv, c.rvq_depth, pos,
+                                            bias, c.rvq_depth, nullptr, nullptr, true),
+                    st->dx);
+      } else {
+        enqueue_decoder_layer(st, E->dl[layer], st->din, st->dx, dk, dv, c.rvq_depth, pos, bias, c.rvq_depth,
+                              nullptr, nullptr, true);
+      }
       download_act(st, st->dx, out);
     }
     CUDA_OK(cudaStreamSynchronize(st->s));

@@ -38,7 +38,7 @@ EXPORTS = [
     "mrtdf_stream_rows", "mrtdf_encode", "mrtdf_temporal_step", "mrtdf_depth_step", "mrtdf_token_embedding",
     "mrtdf_sample", "mrtdf_sample_noalloc", "mrtdf_generate_tokens", "mrtdf_generate_tokens_dev",
     "mrtdf_teacher_forced_logits", "mrtdf_stream_sync", "mrtdf_stream_cuda", "mrtdf_check_wait_timeout",
-    "mrtdf_bench_gemv",
+    "mrtdf_bench_phases", "mrtdf_bench_l2_read",
     "mrtdf_bench_encoder", "mrtdf_bench_depth", "mrtdf_stream_chunk_kernels", "mrtdf_probe_encoder_layer",
     "mrtdf_probe_set_cache", "mrtdf_probe_decoder_layer", "mrtdf_probe_lm_head", "mrtdf_generate_stream_dev",
     "mrtdf_build_encoder_inputs",
@@ -113,6 +113,8 @@ def lib() -> ctypes.CDLL:
             getattr(L, name).restype = ctypes.c_int
         L.mrtdf_stream_chunk_kernels.restype = ctypes.c_longlong
         L.mrtdf_stream_chunk_kernels.argtypes = [ctypes.c_void_p]
+        L.mrtdf_bench_l2_read.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
+                                          ctypes.POINTER(ctypes.c_double)]
         L.mrtdf_sample_noalloc.restype = ctypes.c_int
         L.mrtdf_sample_noalloc.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                            ctypes.POINTER(GenOpts), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
@@ -199,6 +201,12 @@ class Engine:
         _check(lib().mrtdf_sample_noalloc(self.h, ctypes.c_void_p(logits_dev_ptr), int(cfg), frame, level,
                                           ctypes.byref(opts), ctypes.c_void_p(uniforms_dev_ptr or None),
                                           ctypes.c_void_p(token_dev_ptr), ctypes.c_void_p(stream or None)))
+
+    def bench_l2_read(self, nbytes: int, reps: int) -> float:
+        """GB/s of 16-byte reads over an nbytes buffer held in L2."""
+        g = ctypes.c_double()
+        _check(lib().mrtdf_bench_l2_read(self.h, ctypes.c_size_t(nbytes), reps, ctypes.byref(g)))
+        return g.value
 
     def bench_encoder(self, rows: int, seq_len: int, reps: int):
         """(ms per encoder pass, algorithmic FLOPs per pass) for `rows`
@@ -310,14 +318,16 @@ class Stream:
                                        ctypes.byref(n)))
         return us.value, b.value, n.value
 
-    def bench_gemv(self, opts: GenOpts, reps: int):
-        """(ms per chunk replay, GEMV launches, algorithmic bytes) of the
-        GEMV phases of one chunk, timed with CUDA events on this stream."""
+    def bench_phases(self, opts: GenOpts, stack_mask: int, reps: int):
+        """(ms per chunk replay, launches, algorithmic bytes) of the
+        weight-streaming decode launches of one chunk for the stacks in
+        stack_mask (1 temporal, 2 depth + lm_head, 3 both), CUDA events on
+        this stream."""
         ms = ctypes.c_float()
         n = ctypes.c_longlong()
         b = ctypes.c_double()
-        _check(lib().mrtdf_bench_gemv(self.h, ctypes.byref(opts), reps, ctypes.byref(ms), ctypes.byref(n),
-                                      ctypes.byref(b)))
+        _check(lib().mrtdf_bench_phases(self.h, ctypes.byref(opts), stack_mask, reps, ctypes.byref(ms),
+                                        ctypes.byref(n), ctypes.byref(b)))
         return ms.value, n.value, b.value
 
     def cuda_stream(self) -> int:

@@ -266,10 +266,11 @@ def test_hybrid_bf16_chunk_properties(mrtdf, hybrid_weights):
 # bf16 self-attention inside the q/k/v cluster vs the separate kernel
 # ---------------------------------------------------------------------------
 @pytest.mark.parametrize("name", ["tiny", "hybrid"])
-def test_fused_self_attention_matches_separate_kernel(mrtdf, tiny_weights, name):
-    """bf16 self-attention inside the q/k/v launch (one thread-block cluster
-    per head, the default) has the separate kernel's arithmetic
-    (MRTDF_CLUSTER_ATTN=0): bit-identical logits and tokens."""
+def test_cluster_self_attention_matches_separate_kernel(mrtdf, tiny_weights, name):
+    """Streams of 3 - 8 bf16 rows run one launch per projection; their
+    self-attention runs inside the q/k/v launch (one thread-block cluster per
+    head) with the separate attention kernel's arithmetic
+    (MRTDF_CLUSTER_ATTN=0): bit-identical step outputs and tokens."""
     cfg = mrtdf.preset(name, 1)
     frames = cfg.max_frames if name == "tiny" else 3
     seq = cfg.max_encoder_length if name == "tiny" else 256
@@ -289,15 +290,17 @@ def test_fused_self_attention_matches_separate_kernel(mrtdf, tiny_weights, name)
                 del os.environ["MRTDF_CLUSTER_ATTN"]
             else:
                 os.environ["MRTDF_CLUSTER_ATTN"] = old
-        st = mrtdf.Stream(eng, 1, True)
-        ids = random_ids(cfg, 2, seq, seed=21)
-        lg = st.teacher_forced_logits(ids, _forced_tokens(cfg, frames, 5), frames)
-        gen = st.generate_tokens(ids, mrtdf.gen_opts(cfg, frames, seed=4))
-        outs.append((lg, gen))
+        st = mrtdf.Stream(eng, 2, True)  # 4 rows
+        ids = np.concatenate([random_ids(cfg, 2, seq, seed=21), random_ids(cfg, 2, seq, seed=22)])
+        st.encode(ids)
+        t = st.temporal_step(None, 0)
+        lg = st.depth_step(None, 0)
+        gen = st.generate_tokens(ids, mrtdf.gen_opts(cfg, frames, seed=4), seeds=[4, 5])
+        outs.append((t, lg, gen))
         st.close()
         eng.close()
-    np.testing.assert_array_equal(outs[0][0], outs[1][0])
-    np.testing.assert_array_equal(outs[0][1], outs[1][1])
+    for a, b in zip(outs[0], outs[1]):
+        np.testing.assert_array_equal(a, b)
 
 
 def test_measurement_hooks(mrtdf, tiny_weights):
@@ -311,9 +314,8 @@ def test_measurement_hooks(mrtdf, tiny_weights):
     st = mrtdf.Stream(eng, 1, True)
     o = mrtdf.gen_opts(cfg, cfg.max_frames, seed=3)
     us, b, n = st.bench_depth(o, cfg.max_frames, 2)
-    # (q/k/v, attention, o_proj, FFN-up, FFN-down) x layers + lm_head + sampler;
-    # 4 per layer when the attention runs inside the q/k/v launch
-    assert us > 0 and b > 0 and n in (cfg.num_depth_layers * 4 + 2, cfg.num_depth_layers * 5 + 2)
+    # one CFG pair in bf16: (self phase, FFN phase) x layers + lm_head + sampler
+    assert us > 0 and b > 0 and n == cfg.num_depth_layers * 2 + 2
     st.sync()
 
 
@@ -448,4 +450,4 @@ def test_chunk_graph_kernel_count(mrtdf, tiny_weights):
     st = mrtdf.Stream(eng, 1, True)
     ids = random_ids(cfg, 2, cfg.max_encoder_length, seed=80)
     st.generate_tokens(ids, mrtdf.gen_opts(cfg, cfg.max_frames, seed=1))
-    assert st.chunk_kernels() == bench.st_launch_count(cfg, cfg.max_frames)
+    assert st.chunk_kernels() == bench.st_launch_count(cfg, cfg.max_frames, fused=True)

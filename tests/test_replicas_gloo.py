@@ -69,6 +69,8 @@ def test_launch_count_matches_graph_structure():
 
     cfg = mrtdf.preset("hybrid")
     # encoder: embed + 12 x 7 + final norm + cross-K/V GEMM; PAD embedding;
-    # 50 x (20 x 7 temporal + 16 x (4 x 4 depth + lm_head + sampler)): the
-    # self-attention runs inside the q/k/v cluster launch
-    assert bench.st_launch_count(cfg) == (1 + 12 * 7 + 2) + 1 + 50 * (20 * 7 + 16 * 18)
+    # fused phases: 50 x (20 x 3 temporal + 16 x (4 x 2 depth + lm_head + sampler))
+    assert bench.st_launch_count(cfg) == (1 + 12 * 7 + 2) + 1 + 50 * (20 * 3 + 16 * 10)
+    # per projection (the self-attention inside the q/k/v cluster launch):
+    # 50 x (20 x 7 temporal + 16 x (4 x 4 depth + lm_head + sampler))
+    assert bench.st_launch_count(cfg, fused=False) == (1 + 12 * 7 + 2) + 1 + 50 * (20 * 7 + 16 * 18)
