@@ -1438,6 +1438,220 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
   }
 }
 
+// ---------------------------------------------------------------------------
+// Sampler for at most 1024 candidates (a level's vocab mask holds one
+// codebook): one CTA of 1024 threads per sequence, thread i owns candidate
+// lo + i. Same arithmetic and result as sample_kernel, organised for short
+// dependency chains:
+//   * the Gumbel noise of every candidate (Philox draw + two logs) does not
+//     depend on the logits, so it is computed while their loads are in flight;
+//   * the top-k threshold (the k-th largest order key, ties counted with
+//     their multiplicity as the radix select counts them) comes from two
+//     1024-bin histogram levels (key bits 31..22, then 21..12 inside the
+//     boundary bin; shared-memory atomics and block scans) and an exact
+//     rank count among the candidates left in the final bin.
+// ---------------------------------------------------------------------------
+constexpr int kSampleSmallThreads = 1024;
+
+// Inclusive prefix sum of v over the 1024 threads (thread order); wsum is
+// 32 words of shared scratch. Two barriers.
+__device__ __forceinline__ unsigned block_scan_1024(unsigned v, unsigned* wsum) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    unsigned w = wsum[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    wsum[lane] = w;
+  }
+  __syncthreads();
+  return x + (warp > 0 ? wsum[warp - 1] : 0u);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kSampleSmallThreads) sample_small_kernel(const SampleParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ unsigned hist[1024];
+  __shared__ unsigned wsum[32];
+  __shared__ uint32_t cand[1024];
+  __shared__ unsigned sel_bin, sel_above, ncand;
+  __shared__ uint32_t kth;
+  __shared__ float rv[32];
+  __shared__ int ri[32];
+  __shared__ int tok_s;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int seq = blockIdx.x;
+  const int n = p.hi - p.lo;
+  const int r0 = seq * p.rows_per_seq;
+  constexpr int EPC = Vec16<T>::N;
+  const int nchunk = p.d / EPC;
+
+  // the frame's running embedding sum does not depend on the token: its load
+  // goes out next to the logits loads
+  const bool fs_pre_ok = !p.is_first && tid < p.rows_per_seq * nchunk;
+  uint4 fs_pre = make_uint4(0, 0, 0, 0);
+  if (fs_pre_ok) {
+    const int r = tid / nchunk, ch = tid - r * nchunk;
+    fs_pre = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.fsum) + (size_t)(r0 + r) * p.d)[ch];
+  }
+
+  int token;
+  if (p.forced) {
+    token = p.forced[seq];
+  } else {
+    const bool has = tid < n;
+    const bool sampled = p.temperature != 0.0f;
+    float a = 0.f, b = 0.f, u = 0.5f;
+    if (has) {
+      const float* l0 = p.logits + (size_t)r0 * p.logits_stride + (p.lo - p.col_offset);
+      a = l0[tid];
+      if (p.rows_per_seq == 2) b = l0[p.logits_stride + tid];
+      if (sampled && p.uniforms) u = p.uniforms[(size_t)seq * p.uni_seq_stride + p.lo + tid];
+    }
+    // noise first: independent of the loads above
+    float gum = 0.f;
+    if (has && sampled) {
+      if (!p.uniforms) u = philox_uniform(p.seeds ? p.seeds[seq] : p.seed_value, p.step, (uint32_t)(p.lo + tid));
+      gum = gumbel_from_uniform(u);
+    }
+    float v = -INFINITY;
+    if (has) {
+      float g = p.rows_per_seq == 2 ? cfg_mix(a, b, p.w) : a;
+      if (sampled) g = __fdiv_rn(g, p.temperature);
+      v = g;
+    }
+    float thr = -INFINITY;
+    if (sampled && p.top_k > 0 && p.top_k < n) {
+      const uint32_t key = float_order_key(v);
+      // level 1: bins of key bits 31..22
+      hist[tid] = 0u;
+      if (tid == 0) ncand = 0u;
+      __syncthreads();
+      if (has) atomicAdd(&hist[key >> 22], 1u);
+      __syncthreads();
+      unsigned c = hist[1023 - tid];  // thread t <-> bin 1023 - t: descending keys
+      unsigned incl = block_scan_1024(c, wsum);
+      if (incl - c < (unsigned)p.top_k && incl >= (unsigned)p.top_k) {
+        sel_bin = 1023u - (unsigned)tid;
+        sel_above = incl - c;
+      }
+      __syncthreads();
+      const unsigned bin1 = sel_bin, above1 = sel_above;
+      // level 2: bins of key bits 21..12 inside bin1
+      hist[tid] = 0u;
+      __syncthreads();
+      const bool in1 = has && (key >> 22) == bin1;
+      if (in1) atomicAdd(&hist[(key >> 12) & 1023u], 1u);
+      __syncthreads();
+      c = hist[1023 - tid];
+      incl = block_scan_1024(c, wsum);
+      const unsigned k2 = (unsigned)p.top_k - above1;
+      if (incl - c < k2 && incl >= k2) {
+        sel_bin = 1023u - (unsigned)tid;
+        sel_above = above1 + incl - c;
+      }
+      __syncthreads();
+      const unsigned bin2 = sel_bin, above2 = sel_above;
+      // the final bin: exact ranks among its members
+      const bool in2 = in1 && ((key >> 12) & 1023u) == bin2;
+      if (in2) cand[atomicAdd(&ncand, 1u)] = key;
+      __syncthreads();
+      if (in2) {
+        const unsigned k3 = (unsigned)p.top_k - above2, m = ncand;
+        unsigned gt = 0, ge = 0;
+        for (unsigned j = 0; j < m; ++j) {
+          const uint32_t kj = cand[j];
+          gt += kj > key;
+          ge += kj >= key;
+        }
+        if (gt < k3 && k3 <= ge) kth = key;  // every writer holds the same key
+      }
+      __syncthreads();
+      thr = float_from_order_key(kth);
+    }
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    if (has) {
+      float val = v;
+      if (sampled) val = (val < thr || val == -INFINITY) ? -INFINITY : __fadd_rn(val, gum);
+      argmax_combine(best, bi, val, tid);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
+      const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+      argmax_combine(best, bi, v2, i2);
+    }
+    if (lane == 0) {
+      rv[warp] = best;
+      ri[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      best = rv[lane];
+      bi = ri[lane];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+        argmax_combine(best, bi, v2, i2);
+      }
+      if (lane == 0) tok_s = bi == 0x7fffffff ? -1 : p.lo + bi;  // -1: no candidate survived
+    }
+    __syncthreads();
+    token = tok_s;
+  }
+  int out_token = token;
+  if (token < 0 || token >= p.V) {
+    if (tid == 0 && p.err) atomicOr(p.err, kErrBadToken);
+    out_token = p.bad_token;
+    token = 0;  // the embedding rows stay defined
+  }
+  if (tid == 0 && p.tokens) p.tokens[(size_t)seq * p.tok_stride + p.tok_index] = out_token;
+
+  // embedding feedback: work item (row r, 16-byte chunk ch)
+  const uint4* e = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.emb) + (size_t)token * p.d);
+  for (int w = tid; w < p.rows_per_seq * nchunk; w += kSampleSmallThreads) {
+    const int r = w / nchunk, ch = w - r * nchunk;
+    const uint4 ev = e[ch];
+    float ef[EPC];
+    Vec16<T>::unpack(ev, ef);
+    const size_t off = (size_t)(r0 + r) * p.d + (size_t)ch * EPC;
+    *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.din) + off) = ev;
+    T* fs = reinterpret_cast<T*>(p.fsum) + off;
+    T* tin = reinterpret_cast<T*>(p.tin) + off;
+    float prev[EPC];
+    if (!p.is_first) {
+      if (w == tid && fs_pre_ok) {
+        Vec16<T>::unpack(fs_pre, prev);
+      } else {
+#pragma unroll
+        for (int q = 0; q < EPC; ++q) prev[q] = to_f(fs[q]);
+      }
+    }
+    T outv[EPC];
+#pragma unroll
+    for (int q = 0; q < EPC; ++q) {
+      const float sum = p.is_first ? ef[q] : rnd<T>(__fadd_rn(prev[q], ef[q]));
+      outv[q] = from_f<T>(sum);
+      if (p.is_last) tin[q] = from_f<T>(__fdiv_rn(sum, (float)p.depth));
+    }
+#pragma unroll
+    for (int q = 0; q < EPC; ++q) fs[q] = outv[q];
+  }
+}
+
 size_t sample_smem_bytes(int n_candidates) { return (size_t)n_candidates * 4; }
 
 cudaError_t sample_set_smem_limits() {
@@ -1448,7 +1662,12 @@ cudaError_t sample_set_smem_limits() {
 }
 
 cudaError_t launch_sample(int dtype, const SampleParams& p, int num_seq, cudaStream_t s, bool pdl) {
-  const size_t smem = sample_smem_bytes(p.hi - p.lo);
+  const int n = p.hi - p.lo;
+  if (n >= 1 && n <= kSampleSmallThreads)
+    return dtype == 1 ? launch_k(sample_small_kernel<__nv_bfloat16>, dim3(num_seq), dim3(kSampleSmallThreads), 0, s,
+                                 pdl, p)
+                      : launch_k(sample_small_kernel<float>, dim3(num_seq), dim3(kSampleSmallThreads), 0, s, pdl, p);
+  const size_t smem = sample_smem_bytes(n);
   if (smem > (size_t)kSampleMaxSmem) return cudaErrorInvalidValue;
   return dtype == 1 ? launch_k(sample_kernel<__nv_bfloat16>, dim3(num_seq), dim3(kSampleThreads), smem, s, pdl, p)
                     : launch_k(sample_kernel<float>, dim3(num_seq), dim3(kSampleThreads), smem, s, pdl, p);

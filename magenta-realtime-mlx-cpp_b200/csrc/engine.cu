@@ -238,8 +238,8 @@ static void upload_weights(mrtdf_engine* E, const WeightSource& src) {
   const size_t db = (size_t)c.rvq_depth * c.num_heads * c.rvq_depth * 4;
   const size_t pb = (size_t)c.max_encoder_length * d * 4;
   if (E->fused) {
-    const int64_t blk = (int64_t)c.num_heads * kFusedCluster * (d / kFusedCluster) * 72;  // o_proj block elements
-    const int64_t oblk = (int64_t)E->ffn_plan.nclusters * kFusedCluster * (d / kFusedCluster) * (E->ffn_plan.Uc + 8);
+    const int64_t blk = (int64_t)c.num_heads * d * 72;                                 // o_proj block elements
+    const int64_t oblk = (int64_t)E->ffn_plan.nclusters * d * (E->ffn_plan.Uc + 8);  // wo block elements
     for (int i = 0; i < c.num_temporal_layers; ++i) { add(blk); add(blk); add(oblk); }
     for (int i = 0; i < c.num_depth_layers; ++i) { add(blk); add(oblk); }
   }
@@ -354,32 +354,30 @@ static void upload_weights(mrtdf_engine* E, const WeightSource& src) {
   E->lm_head = single("lm_head.weight", V * d);
 
   if (E->fused) {
-    // o_proj (d, inner) -> [h][r][n][c]: row n of slice r = output dim
-    // r * d/8 + n, columns c < 64 = head h's attention outputs, 8 zeros after
-    const int64_t dpc = d / kFusedCluster, H = c.num_heads;
+    // o_proj (d, inner) -> [h][n][c]: row n = output dim, columns c < 64 =
+    // head h's attention outputs, 8 zeros after (a CTA's block of output
+    // dims is then one contiguous range, whatever the cluster size)
+    const int64_t H = c.num_heads;
     auto o_block = [&](const std::string& key) {
       const float* w = fetch(key, d * in);
-      tmp.assign((size_t)(H * kFusedCluster * dpc * 72), 0.f);
+      tmp.assign((size_t)(H * d * 72), 0.f);
       for (int64_t h = 0; h < H; ++h)
-        for (int64_t r = 0; r < kFusedCluster; ++r)
-          for (int64_t n = 0; n < dpc; ++n)
-            for (int64_t cc = 0; cc < 64; ++cc)
-              tmp[(size_t)((((h * kFusedCluster + r) * dpc + n) * 72) + cc)] = w[(r * dpc + n) * in + h * 64 + cc];
+        for (int64_t n = 0; n < d; ++n)
+          for (int64_t cc = 0; cc < 64; ++cc) tmp[(size_t)(((h * d + n) * 72) + cc)] = w[n * in + h * 64 + cc];
       void* dst = E->weights.take(tmp.size() * es);
       put(dst, tmp.data(), (int64_t)tmp.size());
       return dst;
     };
-    // wo (d, ff) -> [j][r][n][u]: row n of slice r = output dim r * d/8 + n,
-    // columns u < Uc = d_ff units j * Uc + u (zero past ff), 8 zeros after
+    // wo (d, ff) -> [j][n][u]: row n = output dim, columns u < Uc = d_ff
+    // units j * Uc + u of cluster j (zero past ff), 8 zeros after
     const int64_t NC = E->ffn_plan.nclusters, Uc = E->ffn_plan.Uc, Ur = Uc + 8;
     auto ffn_block = [&](const std::string& key) {
       const float* w = fetch(key, d * ff);
-      tmp.assign((size_t)(NC * kFusedCluster * dpc * Ur), 0.f);
+      tmp.assign((size_t)(NC * d * Ur), 0.f);
       for (int64_t j = 0; j < NC; ++j)
-        for (int64_t r = 0; r < kFusedCluster; ++r)
-          for (int64_t n = 0; n < dpc; ++n)
-            for (int64_t u = 0; u < Uc && j * Uc + u < ff; ++u)
-              tmp[(size_t)((((j * kFusedCluster + r) * dpc + n) * Ur) + u)] = w[(r * dpc + n) * ff + j * Uc + u];
+        for (int64_t n = 0; n < d; ++n)
+          for (int64_t u = 0; u < Uc && j * Uc + u < ff; ++u)
+            tmp[(size_t)(((j * d + n) * Ur) + u)] = w[n * ff + j * Uc + u];
       void* dst = E->weights.take(tmp.size() * es);
       put(dst, tmp.data(), (int64_t)tmp.size());
       return dst;
