@@ -76,9 +76,11 @@ struct EncLayerDev {
 };
 struct DecLayerDev {
   void *wqkv, *wo, *n_self, *wcq, *wco, *n_cross, *wi, *wout, *n_ffn;
-  // blocked copies for the fused phases (bf16): o_proj / cross o_proj as
-  // [H][8][d/8][64 + 8 pad], wo as [nclusters][8][d/8][Uc + 8 pad]
+  // copies for the fused phases (bf16): o_proj / cross o_proj as
+  // [H][d][64 + 8 pad], wo as [nclusters][d][Uc + 8 pad]; q/k/v, cross q
+  // and wi rows with a 16-byte pad after each row (one TMA copy per CTA)
   void *wo_blk = nullptr, *wco_blk = nullptr, *wout_blk = nullptr;
+  void *wqkv_pad = nullptr, *wcq_pad = nullptr, *wi_pad = nullptr;
 };
 
 // A hidden state between decode phases: `x` itself, or (fused phases)
@@ -240,8 +242,11 @@ static void upload_weights(mrtdf_engine* E, const WeightSource& src) {
   if (E->fused) {
     const int64_t blk = (int64_t)c.num_heads * d * 72;                                 // o_proj block elements
     const int64_t oblk = (int64_t)E->ffn_plan.nclusters * d * (E->ffn_plan.Uc + 8);  // wo block elements
-    for (int i = 0; i < c.num_temporal_layers; ++i) { add(blk); add(blk); add(oblk); }
-    for (int i = 0; i < c.num_depth_layers; ++i) { add(blk); add(oblk); }
+    const int64_t rp = d + 8;  // padded row elements
+    for (int i = 0; i < c.num_temporal_layers; ++i) {
+      add(blk); add(blk); add(oblk); add(3 * in * rp); add(in * rp); add(2 * ff * rp);
+    }
+    for (int i = 0; i < c.num_depth_layers; ++i) { add(blk); add(oblk); add(3 * in * rp); add(2 * ff * rp); }
   }
   total += tb + db + pb + 3 * 256;
   E->weights.reserve(total);
@@ -382,6 +387,26 @@ static void upload_weights(mrtdf_engine* E, const WeightSource& src) {
       put(dst, tmp.data(), (int64_t)tmp.size());
       return dst;
     };
+    // a device copy of `rows` rows of `src` (compute dtype, d columns) with a
+    // 16-byte zero pad after each row
+    auto padded = [&](const void* src, int64_t rows) {
+      const size_t rb = (size_t)d * es, rs = rb + 16;
+      void* dst = E->weights.take((size_t)rows * rs);
+      CUDA_OK(cudaMemset(dst, 0, (size_t)rows * rs));
+      CUDA_OK(cudaMemcpy2D(dst, rs, src, rb, rb, (size_t)rows, cudaMemcpyDeviceToDevice));
+      return dst;
+    };
+    for (int i = 0; i < c.num_temporal_layers; ++i) {
+      DecLayerDev& L = E->tl[i];
+      L.wqkv_pad = padded(L.wqkv, 3 * in);
+      L.wcq_pad = padded(L.wcq, in);
+      L.wi_pad = padded(L.wi, 2 * ff);
+    }
+    for (int i = 0; i < c.num_depth_layers; ++i) {
+      DecLayerDev& L = E->dl[i];
+      L.wqkv_pad = padded(L.wqkv, 3 * in);
+      L.wi_pad = padded(L.wi, 2 * ff);
+    }
     for (int i = 0; i < c.num_temporal_layers; ++i) {
       const std::string p = "temporal_layers." + std::to_string(i) + ".";
       E->tl[i].wo_blk = o_block(p + "self_attn.o_proj.weight");
@@ -594,7 +619,7 @@ Hidden enqueue_fused_layer(mrtdf_stream* st, const DecLayerDev& L, Hidden in, vo
   const bool on = phase_on(st);
   FusedSelfParams sp{};
   Hidden h = fused_io(st, in, sp.in);
-  sp.wqkv = L.wqkv; sp.norm_w = L.n_self; sp.wo_blk = L.wo_blk; sp.kc = kc; sp.vc = vc; sp.bias = bias;
+  sp.wqkv = L.wqkv_pad; sp.norm_w = L.n_self; sp.wo_blk = L.wo_blk; sp.kc = kc; sp.vc = vc; sp.bias = bias;
   sp.bias_stride = bias_stride; sp.H = c.num_heads; sp.cap = cap; sp.pos = pos; sp.l2_keep = l2_keep;
   if (on) {
     check_cuda(launch_fused_self(sp, st->s, E->pdl), "fused self phase");
@@ -604,7 +629,7 @@ Hidden enqueue_fused_layer(mrtdf_stream* st, const DecLayerDev& L, Hidden in, vo
   if (ck) {
     FusedCrossParams cp{};
     h = fused_io(st, h, cp.in);
-    cp.wcq = L.wcq; cp.norm_w = L.n_cross; cp.wco_blk = L.wco_blk; cp.ck = ck; cp.cv = cv; cp.H = c.num_heads;
+    cp.wcq = L.wcq_pad; cp.norm_w = L.n_cross; cp.wco_blk = L.wco_blk; cp.ck = ck; cp.cv = cv; cp.H = c.num_heads;
     cp.Smax = c.max_encoder_length; cp.S = st->S; cp.l2_keep = l2_keep;
     if (on) {
       check_cuda(launch_fused_cross(cp, st->s, E->pdl), "fused cross phase");
@@ -614,7 +639,7 @@ Hidden enqueue_fused_layer(mrtdf_stream* st, const DecLayerDev& L, Hidden in, vo
   }
   FusedFfnParams fp{};
   h = fused_io(st, h, fp.in);
-  fp.wi = L.wi; fp.norm_w = L.n_ffn; fp.wout_blk = L.wout_blk; fp.ff = c.d_ff; fp.Uc = E->ffn_plan.Uc;
+  fp.wi = L.wi_pad; fp.norm_w = L.n_ffn; fp.wout_blk = L.wout_blk; fp.ff = c.d_ff; fp.Uc = E->ffn_plan.Uc;
   fp.nclusters = E->ffn_plan.nclusters; fp.l2_keep = l2_keep;
   if (on) {
     check_cuda(launch_fused_ffn(fp, st->s, E->pdl), "fused ffn phase");

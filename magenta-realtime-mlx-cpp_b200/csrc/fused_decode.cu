@@ -400,16 +400,14 @@ __global__ void __launch_bounds__(kThreads, 1) fused_self_kernel(const FusedSelf
     fence_mbar_init();
   }
   __syncthreads();
-  const int row_bytes = d * 2;
   if (warp == 0) {
     const uint64_t pol = l2_policy(p.l2_keep != 0);
-    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(RQ * row_bytes + dpc * kBlkRow));
+    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(RQ * L.rs + dpc * kBlkRow));
     __syncwarp();
     const uint8_t* src =
-        reinterpret_cast<const uint8_t*>(p.wqkv) + ((size_t)h * kQkvRowsPerHead + (size_t)r * RQ) * row_bytes;
-    for (int rr = lane; rr < RQ; rr += 32)
-      bulk_g2s_hint(wsm + (size_t)rr * L.rs, src + (size_t)rr * row_bytes, (uint32_t)row_bytes, bar, pol);
-    if (lane == 0)
+        reinterpret_cast<const uint8_t*>(p.wqkv) + ((size_t)h * kQkvRowsPerHead + (size_t)r * RQ) * L.rs;
+    if (lane == 0) bulk_g2s_hint(wsm, src, (uint32_t)(RQ * L.rs), bar, pol);
+    if (lane == 1)
       bulk_g2s_hint(wob, reinterpret_cast<const uint8_t*>(p.wo_blk) + ((size_t)h * kFusedCluster + r) * dpc * kBlkRow,
                     (uint32_t)(dpc * kBlkRow), bar, pol);
   }
@@ -567,14 +565,13 @@ __global__ void __launch_bounds__(kThreads, 2) fused_cross_kernel(const FusedCro
     fence_mbar_init();
   }
   __syncthreads();
-  const int row_bytes = d * 2;
   if (warp == 0) {
     const uint64_t pol = l2_policy(p.l2_keep != 0);
-    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(8 * row_bytes + dpc * kBlkRow));
+    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(8 * L.rs + dpc * kBlkRow));
     __syncwarp();
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(p.wcq) + ((size_t)h * 64 + (size_t)r * 8) * row_bytes;
-    if (lane < 8) bulk_g2s_hint(wq + (size_t)lane * L.rs, src + (size_t)lane * row_bytes, (uint32_t)row_bytes, bar, pol);
-    if (lane == 0)
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(p.wcq) + ((size_t)h * 64 + (size_t)r * 8) * L.rs;
+    if (lane == 0) bulk_g2s_hint(wq, src, (uint32_t)(8 * L.rs), bar, pol);
+    if (lane == 1)
       bulk_g2s_hint(wob, reinterpret_cast<const uint8_t*>(p.wco_blk) + ((size_t)h * kFusedCluster + r) * dpc * kBlkRow,
                     (uint32_t)(dpc * kBlkRow), bar, pol);
   }
@@ -722,16 +719,14 @@ __global__ void __launch_bounds__(kThreads, 1) fused_ffn_kernel(const FusedFfnPa
     fence_mbar_init();
   }
   __syncthreads();
-  const int row_bytes = d * 2;
   const int blk_bytes = dpc * L.rsw;
   if (warp == 0) {
     const uint64_t pol = l2_policy(p.l2_keep != 0);
-    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(R * row_bytes + blk_bytes));
+    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(R * L.rs + blk_bytes));
     __syncwarp();
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(p.wi) + (size_t)2 * u0 * row_bytes;
-    for (int rr = lane; rr < R; rr += 32)
-      bulk_g2s_hint(wsm + (size_t)rr * L.rs, src + (size_t)rr * row_bytes, (uint32_t)row_bytes, bar, pol);
-    if (lane == 0)
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(p.wi) + (size_t)2 * u0 * L.rs;
+    if (lane == 0 && R > 0) bulk_g2s_hint(wsm, src, (uint32_t)(R * L.rs), bar, pol);
+    if (lane == 1)
       bulk_g2s_hint(wob, reinterpret_cast<const uint8_t*>(p.wout_blk) + ((size_t)j * kFusedCluster + r) * blk_bytes,
                     (uint32_t)blk_bytes, bar, pol);
   }

@@ -20,6 +20,11 @@
 // rounding there: x = R(residual + R(sum / 2^32)) (the o_proj / wo output
 // rounded to bf16, then the rounded residual add, modules.cpp:401-408).
 //
+// The weight rows a CTA multiplies are one contiguous range of a padded
+// copy (row stride d * 2 + 16 bytes, the shared-memory stride that keeps the
+// ldmatrix reads conflict free), fetched with a single TMA bulk copy: issuing
+// one bulk copy per row cost about 35 ns each.
+//
 // Three accumulators rotate: a phase reads one (acc), adds into the next
 // (acc_out), and zeroes the third (acc_clear), which the phase before it
 // read; kernels of a stream are serialised by their dependency waits, so a
@@ -48,7 +53,7 @@ struct FusedIn {
 
 struct FusedSelfParams {
   FusedIn in;
-  const void* wqkv;    // head-major q/k/v rows (H * 192, d)
+  const void* wqkv;    // head-major q/k/v rows (H * 192, d), rows padded to d * 2 + 16 bytes
   const void* norm_w;  // pre_self_attn_norm (d)
   const void* wo_blk;  // o_proj blocked: [H][8][d / 8][64] = rows r*d/8 .. of W_o's columns of head h
   void* kc;            // self K/V caches (B, H, cap, 64)
@@ -61,7 +66,7 @@ struct FusedSelfParams {
 
 struct FusedCrossParams {
   FusedIn in;
-  const void* wcq;     // cross q_proj (H * 64, d)
+  const void* wcq;     // cross q_proj (H * 64, d), rows padded to d * 2 + 16 bytes
   const void* norm_w;  // pre_cross_attn_norm (d)
   const void* wco_blk; // cross o_proj blocked like wo_blk
   const void* ck;      // cross K/V caches (B, H, Smax, 64)
@@ -72,7 +77,7 @@ struct FusedCrossParams {
 
 struct FusedFfnParams {
   FusedIn in;
-  const void* wi;       // wi_0 / wi_1 rows interleaved (2 * ff, d)
+  const void* wi;       // wi_0 / wi_1 rows interleaved (2 * ff, d), rows padded to d * 2 + 16 bytes
   const void* norm_w;   // pre_ffn_norm (d)
   const void* wout_blk; // wo blocked: [nclusters][8][d / 8][Uc], unit columns of cluster j (zero past ff)
   int ff, Uc, nclusters;
