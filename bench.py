@@ -398,15 +398,28 @@ def e2e_leg(mrtdf, torch, cfg, st, ext, ids, K: int, rank: int, dist, device) ->
             "ms_per_chunk": ms_e2e, "rtf": CHUNK_SECONDS * 1e3 / ms_e2e}
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch from
+# an ncu capture with --cache-control none of a 3-frame chunk
+# (bench.py --timed-only --frames 3), frame 1: temporal layer 5 (self, cross,
+# FFN) and depth level 3 (self, FFN, self) plus two lm_head slices. Per-launch
+# means over a stack's launch mix (temporal: 1 self + 1 cross + 1 FFN per
+# layer; depth: 4 self + 4 FFN + 1 lm_head per level).
+TRAFFIC_TEMPORAL = (8716544 + 13091584 + 17778176) / 3
+TRAFFIC_DEPTH = (4 * (8604928 + 1605120 + 8554240 + 1151488) / 2 + 4 * 14497792 + (1961728 + 1586176) / 2) / 9
+
+
 def roofline_leg(mrtdf, eng, cfg, st, peaks: dict) -> dict:
-    """The decode phases split by where their weights live. Temporal stack
-    (fused self / cross / FFN phases, weights and cross K/V streamed from
-    HBM): algorithmic bytes per launch / average launch time against the
-    measured HBM peak. Depth stack + lm_head (weights kept in L2 with
-    evict-last hints): the same against the L2 read peak, measured here with
-    the engine's own read kernel over a 64 MiB L2-resident buffer. Each stack
-    is timed by replaying exactly its launches of one chunk as one CUDA graph
-    between CUDA events (mrtdf_bench_phases)."""
+    """The decode phases split into the temporal stack (fused self / cross /
+    FFN phases; weights and cross K/V streamed from HBM) and the depth stack
+    + lm_head. Algorithmic bytes per launch / average launch time against the
+    measured HBM peak for both: the depth weights carry evict-last hints, but
+    the capture shows them read from DRAM again at every level (101 MB of
+    depth-layer weights plus the lm_head slices do not stay resident in L2
+    when all SMs read them), so HBM bounds both stacks. The L2 read peak,
+    measured here with the engine's own read kernel over a 64 MiB buffer, is
+    reported beside the depth figure for context. Each stack is timed by
+    replaying exactly its launches of one chunk as one CUDA graph between
+    CUDA events (mrtdf_bench_phases)."""
     o = mrtdf.gen_opts(cfg, 50, seed=1)
     t_ms, t_n, t_b = st.bench_phases(o, 1, 3)
     d_ms, d_n, d_b = st.bench_phases(o, 2, 3)
@@ -415,13 +428,18 @@ def roofline_leg(mrtdf, eng, cfg, st, peaks: dict) -> dict:
     t_ach = t_b / t_n / (t_ms / 1e3 / t_n) / 1e9
     d_ach = d_b / d_n / (d_ms / 1e3 / d_n) / 1e9
     return {"bound": "hbm", "achieved": t_ach, "peak": hbm, "unit": "GB/s", "frac": t_ach / hbm,
-            "traffic": None, "traffic_unit": "bytes per launch",
+            "traffic": TRAFFIC_TEMPORAL, "traffic_unit": "DRAM bytes per launch",
+            "traffic_source": "ncu --cache-control none capture of a 3-frame chunk (temporal layer 5 of frame 1)",
             "kernel": "temporal-stack decode phases (fused_self_kernel / fused_cross_kernel / fused_ffn_kernel)",
             "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
             "launches_per_chunk": t_n, "bytes_per_launch": t_b / t_n, "us_per_launch": t_ms * 1e3 / t_n,
             "ms_per_chunk": t_ms,
-            "depth": {"bound": "l2", "achieved": d_ach, "peak": l2_peak, "unit": "GB/s", "frac": d_ach / l2_peak,
-                      "peak_source": "measured: engine L2 read kernel, 64 MiB buffer, 16-byte loads on every SM",
+            "depth": {"bound": "hbm", "achieved": d_ach, "peak": hbm, "unit": "GB/s", "frac": d_ach / hbm,
+                      "traffic": TRAFFIC_DEPTH, "traffic_unit": "DRAM bytes per launch",
+                      "traffic_source": "ncu --cache-control none capture of a 3-frame chunk (depth level 3 of "
+                                        "frame 1: L2 sector hit rate 59-65 %)",
+                      "l2_peak": l2_peak, "frac_of_l2_peak": d_ach / l2_peak,
+                      "l2_peak_source": "measured: engine L2 read kernel, 64 MiB buffer, 16-byte loads on every SM",
                       "kernel": "depth-stack decode phases + lm_head level slice", "launches_per_chunk": d_n,
                       "bytes_per_launch": d_b / d_n, "us_per_launch": d_ms * 1e3 / d_n, "ms_per_chunk": d_ms}}
 
