@@ -380,6 +380,27 @@ int mrtdf_llm_to_rvq(const int32_t* llm, int n, int rvq_depth, int codebook_size
 int mrtdf_rvq_to_llm(const int32_t* rvq, int n, int rvq_depth, int codebook_size,
                      int codec_offset, int32_t* out);
 
+/* Paths of the C++ inference bundle under one cache root (InferenceBundlePaths,
+ * weights.h:70-78). Each is a NUL-terminated path of at most MRTDF_PATH_MAX - 1 bytes. */
+#define MRTDF_PATH_MAX 4096
+typedef struct mrtdf_bundle_paths {
+  char spectrostream_encoder[MRTDF_PATH_MAX];
+  char spectrostream_decoder[MRTDF_PATH_MAX];
+  char spectrostream_codebooks[MRTDF_PATH_MAX];
+  char musiccoca_encoder[MRTDF_PATH_MAX];
+  char musiccoca_codebooks[MRTDF_PATH_MAX];
+  char musiccoca_vocab[MRTDF_PATH_MAX];
+  char depthformer[MRTDF_PATH_MAX]; /* <root>/depthformer/depthformer_<tag>.safetensors */
+} mrtdf_bundle_paths;
+
+/* resolve_inference_bundle (weights.cpp:72-120): the bundle's file paths
+ * under `cache_root` for the Depthformer checkpoint `tag` ("base", "large").
+ * A root that is not a directory, or any of the seven files missing, is
+ * MRTDF_ERR_IO (std::runtime_error in the reference) with the reference's
+ * message (the missing files listed one per line). A path longer than
+ * MRTDF_PATH_MAX - 1 bytes is MRTDF_ERR_RANGE. No GPU is needed. */
+int mrtdf_resolve_inference_bundle(const char* cache_root, const char* tag, mrtdf_bundle_paths* out);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

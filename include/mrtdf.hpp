@@ -37,9 +37,12 @@
 #define MRTDF_HPP_
 
 #include <cstdint>
+#include <filesystem>
+#include <memory>
 #include <optional>
 #include <stdexcept>
 #include <string>
+#include <string_view>
 #include <utility>
 #include <vector>
 
@@ -295,6 +298,30 @@ inline IntArray llm_to_rvq(const IntArray& llm, const Config& c) {
 inline void context_roll(IntArray& context, const IntArray& new_codes) {
   check(mrtdf_context_roll(context.ptr(), static_cast<int>(context.dim(0)), static_cast<int>(context.dim(1)),
                            new_codes.ptr(), static_cast<int>(new_codes.dim(0))));
+}
+
+// InferenceBundlePaths (weights.h:70-78).
+struct InferenceBundlePaths {
+  std::filesystem::path spectrostream_encoder, spectrostream_decoder, spectrostream_codebooks;
+  std::filesystem::path musiccoca_encoder, musiccoca_codebooks, musiccoca_vocab;
+  std::filesystem::path depthformer;
+};
+
+// resolve_inference_bundle(cache_root, tag) (weights.cpp:72-120): throws
+// mrtdf::Error (a std::runtime_error) when the root is not a directory or a
+// file of the bundle is missing, with the reference's message.
+inline InferenceBundlePaths resolve_inference_bundle(const std::filesystem::path& cache_root, std::string_view tag) {
+  std::unique_ptr<mrtdf_bundle_paths> c(new mrtdf_bundle_paths());
+  check(mrtdf_resolve_inference_bundle(cache_root.string().c_str(), std::string(tag).c_str(), c.get()));
+  InferenceBundlePaths p;
+  p.spectrostream_encoder = c->spectrostream_encoder;
+  p.spectrostream_decoder = c->spectrostream_decoder;
+  p.spectrostream_codebooks = c->spectrostream_codebooks;
+  p.musiccoca_encoder = c->musiccoca_encoder;
+  p.musiccoca_codebooks = c->musiccoca_codebooks;
+  p.musiccoca_vocab = c->musiccoca_vocab;
+  p.depthformer = c->depthformer;
+  return p;
 }
 
 }  // namespace mrtdf

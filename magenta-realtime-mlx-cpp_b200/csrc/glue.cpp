@@ -5,7 +5,9 @@
 //   build_encoder_inputs_host  src/magenta_realtime_mlx/system.cpp:62-95
 //   context roll               system.cpp:320-333
 //   rvq_to_llm / llm_to_rvq    src/magenta_realtime_mlx/rvq.cpp:105-134
+//   resolve_inference_bundle   src/magenta_realtime_mlx/weights.cpp:72-120
 #include <cstring>
+#include <filesystem>
 #include <string>
 
 #include "host_util.h"
@@ -66,6 +68,43 @@ int mrtdf_llm_to_rvq(const int32_t* llm, int n, int rvq_depth, int codebook_size
           throw Error{MRTDF_ERR_INVALID, "llm_to_rvq: token levels do not match expected RVQ structure"};
         out[i * rvq_depth + d] = r;
       }
+  });
+}
+
+int mrtdf_resolve_inference_bundle(const char* cache_root, const char* tag, mrtdf_bundle_paths* out) {
+  return guarded([&] {
+    if (!cache_root || !tag || !out) throw Error{MRTDF_ERR_INVALID, "NULL argument"};
+    namespace fs = std::filesystem;
+    const fs::path root(cache_root);
+    std::error_code ec;
+    if (!fs::is_directory(root, ec))
+      throw Error{MRTDF_ERR_IO, "resolve_inference_bundle: not a directory: " + root.string()};
+    struct Entry {
+      const char* label;
+      fs::path path;
+      char* dst;
+    };
+    const Entry entries[] = {
+        {"SpectroStream encoder", root / "spectrostream_encoder.safetensors", out->spectrostream_encoder},
+        {"SpectroStream decoder", root / "spectrostream_decoder.safetensors", out->spectrostream_decoder},
+        {"SpectroStream codebooks", root / "spectrostream_codebooks.safetensors", out->spectrostream_codebooks},
+        {"MusicCoCa encoder", root / "musiccoca_encoder.safetensors", out->musiccoca_encoder},
+        {"MusicCoCa codebooks", root / "musiccoca_codebooks.safetensors", out->musiccoca_codebooks},
+        {"MusicCoCa SentencePiece vocab", root / "musiccoca_vocab.model", out->musiccoca_vocab},
+        {"Depthformer checkpoint", root / "depthformer" / ("depthformer_" + std::string(tag) + ".safetensors"),
+         out->depthformer},
+    };
+    std::string missing;
+    for (const Entry& e : entries)
+      if (!fs::is_regular_file(e.path, ec)) missing += "  - " + std::string(e.label) + ": " + e.path.string() + "\n";
+    if (!missing.empty())
+      throw Error{MRTDF_ERR_IO, "Incomplete Magenta RT C++ inference bundle (looked under " + root.string() + "):\n" +
+                                    missing + "Run `make ensure-weights-cache` to download + bundle."};
+    for (const Entry& e : entries) {
+      const std::string s = e.path.string();
+      if (s.size() >= MRTDF_PATH_MAX) throw Error{MRTDF_ERR_RANGE, "bundle path too long: " + s};
+      std::memcpy(e.dst, s.c_str(), s.size() + 1);
+    }
   });
 }
 

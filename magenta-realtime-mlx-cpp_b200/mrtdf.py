@@ -42,7 +42,7 @@ EXPORTS = [
     "mrtdf_bench_encoder", "mrtdf_bench_depth", "mrtdf_stream_chunk_kernels", "mrtdf_probe_encoder_layer",
     "mrtdf_probe_set_cache", "mrtdf_probe_decoder_layer", "mrtdf_probe_lm_head", "mrtdf_generate_stream_dev",
     "mrtdf_build_encoder_inputs",
-    "mrtdf_context_roll", "mrtdf_llm_to_rvq", "mrtdf_rvq_to_llm",
+    "mrtdf_context_roll", "mrtdf_llm_to_rvq", "mrtdf_rvq_to_llm", "mrtdf_resolve_inference_bundle",
 ]
 
 
@@ -50,6 +50,16 @@ class MrtdfError(RuntimeError):
     def __init__(self, code: int, msg: str):
         super().__init__(f"[mrtdf status {code}] {msg}")
         self.code = code
+
+
+PATH_MAX = 4096
+BUNDLE_FIELDS = ["spectrostream_encoder", "spectrostream_decoder", "spectrostream_codebooks", "musiccoca_encoder",
+                 "musiccoca_codebooks", "musiccoca_vocab", "depthformer"]
+
+
+class BundlePaths(ctypes.Structure):
+    """mrtdf_bundle_paths (include/mrtdf.h): InferenceBundlePaths, weights.h:70-78."""
+    _fields_ = [(n, ctypes.c_char * PATH_MAX) for n in BUNDLE_FIELDS]
 
 
 class Config(ctypes.Structure):
@@ -96,6 +106,7 @@ def lib() -> ctypes.CDLL:
         L.mrtdf_version.restype = ctypes.c_char_p
         L.mrtdf_stream_cuda.restype = ctypes.c_void_p
         L.mrtdf_stream_cuda.argtypes = [ctypes.c_void_p]
+        L.mrtdf_resolve_inference_bundle.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(BundlePaths)]
         L.mrtdf_write_random_safetensors.argtypes = [ctypes.POINTER(Config), ctypes.c_uint64, ctypes.c_float,
                                                      ctypes.c_int, ctypes.c_char_p]
         L.mrtdf_load_random.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_float, ctypes.c_int]
@@ -395,6 +406,15 @@ def llm_to_rvq(tokens: np.ndarray, codebook_size: int, codec_offset: int) -> np.
     out = np.empty_like(t)
     _check(lib().mrtdf_llm_to_rvq(_ip(t), t.shape[0], t.shape[1], codebook_size, codec_offset, _ip(out)))
     return out
+
+
+def resolve_inference_bundle(cache_root: str, tag: str) -> dict:
+    """resolve_inference_bundle (weights.cpp:72-120): {field: path} of the
+    seven bundle files; MrtdfError (MRTDF_ERR_IO) when the root is not a
+    directory or a file is missing."""
+    out = BundlePaths()
+    _check(lib().mrtdf_resolve_inference_bundle(str(cache_root).encode(), tag.encode(), ctypes.byref(out)))
+    return {n: getattr(out, n).decode() for n in BUNDLE_FIELDS}
 
 
 def rvq_to_llm(tokens: np.ndarray, codebook_size: int, codec_offset: int) -> np.ndarray:

@@ -196,3 +196,57 @@ def test_codec_writer_argument_errors(mrtdf, tmp_path):
     again = str(tmp_path / "d2.safetensors").encode()
     assert lib.mrtss_write_random_safetensors(0, 4, again, str(tmp_path / "c2.safetensors").encode()) == 0
     assert open(ok_dec, "rb").read() == open(again, "rb").read()
+
+
+# ---------------------------------------------------------------------------
+# resolve_inference_bundle (weights.cpp:72-120)
+# ---------------------------------------------------------------------------
+BUNDLE_FILES = {
+    "spectrostream_encoder": "spectrostream_encoder.safetensors",
+    "spectrostream_decoder": "spectrostream_decoder.safetensors",
+    "spectrostream_codebooks": "spectrostream_codebooks.safetensors",
+    "musiccoca_encoder": "musiccoca_encoder.safetensors",
+    "musiccoca_codebooks": "musiccoca_codebooks.safetensors",
+    "musiccoca_vocab": "musiccoca_vocab.model",
+}
+
+
+def _make_bundle(root, tag, skip=()):
+    (root / "depthformer").mkdir(parents=True, exist_ok=True)
+    for field, name in BUNDLE_FILES.items():
+        if field not in skip:
+            (root / name).write_bytes(b"x")
+    if "depthformer" not in skip:
+        (root / "depthformer" / f"depthformer_{tag}.safetensors").write_bytes(b"x")
+
+
+@pytest.mark.parametrize("tag", ["base", "large"])
+def test_resolve_inference_bundle_paths(mrtdf, tmp_path, tag):
+    _make_bundle(tmp_path, tag)
+    p = mrtdf.resolve_inference_bundle(str(tmp_path), tag)
+    for field, name in BUNDLE_FILES.items():
+        assert p[field] == str(tmp_path / name)
+    assert p["depthformer"] == str(tmp_path / "depthformer" / f"depthformer_{tag}.safetensors")
+
+
+def test_resolve_inference_bundle_errors(mrtdf, tmp_path):
+    ERR_IO = 3
+    # not a directory (a file, and a missing path)
+    f = tmp_path / "file"
+    f.write_bytes(b"x")
+    for root in (f, tmp_path / "missing"):
+        with pytest.raises(mrtdf.MrtdfError) as e:
+            mrtdf.resolve_inference_bundle(str(root), "base")
+        assert e.value.code == ERR_IO and "not a directory" in str(e.value)
+    # every missing file is listed (the other checkpoint's tag is missing too)
+    root = tmp_path / "cache"
+    _make_bundle(root, "base", skip=("musiccoca_vocab", "spectrostream_codebooks"))
+    with pytest.raises(mrtdf.MrtdfError) as e:
+        mrtdf.resolve_inference_bundle(str(root), "base")
+    msg = str(e.value)
+    assert e.value.code == ERR_IO and "Incomplete Magenta RT C++ inference bundle" in msg
+    assert "MusicCoCa SentencePiece vocab" in msg and "SpectroStream codebooks" in msg
+    assert "SpectroStream encoder" not in msg
+    with pytest.raises(mrtdf.MrtdfError) as e:
+        mrtdf.resolve_inference_bundle(str(root), "large")
+    assert "depthformer_large.safetensors" in str(e.value)

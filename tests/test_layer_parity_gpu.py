@@ -1,6 +1,6 @@
 """Layer-by-layer parity of the production kernels at the reference's model
-shapes ("hybrid", the benchmark architecture, and the published "base"
-checkpoint shape) against the CPU oracle, on identical inputs.
+shapes ("hybrid", the benchmark architecture, and the published "base" and
+"large" checkpoint shapes) against the CPU oracle, on identical inputs.
 
 Each check feeds ONE production launch sequence (through the engine's probe
 entry points: the same kernels, launch shapes and epilogues as a chunk) the
@@ -73,7 +73,7 @@ def check_logits(got, want16, want32, what: str) -> str:
     return f"max {err:.3e} (bf16 oracle vs fp32: {floor:.3e})"
 
 
-@pytest.fixture(scope="module", params=["hybrid", "base"])
+@pytest.fixture(scope="module", params=["hybrid", "base", "large"])
 def model(request, mrtdf, oracle):
     cfg = mrtdf.preset(request.param, mrtdf.DTYPE_BF16)
     eng = mrtdf.Engine(cfg).load_random(0)
