@@ -33,8 +33,16 @@ def test_library_exports_every_declared_symbol(mrtdf):
     missing = [s for s in codec if not hasattr(lib, s)]
     assert not missing, missing
     assert sorted(mrtss.EXPORTS) == sorted(codec)
+    # the style path (include/mrtmc.h) too
+    import mrtmc
+
+    style = _declared_symbols("mrtmc.h", "mrtmc_")
+    assert len(style) >= 8
+    missing = [s for s in style if not hasattr(lib, s)]
+    assert not missing, missing
+    assert sorted(mrtmc.EXPORTS) == sorted(style)
     # the C ABI headers, plus the header-only C++ wrapper over mrtdf.h
-    assert sorted(os.listdir(os.path.join(ROOT, "include"))) == ["mrtdf.h", "mrtdf.hpp", "mrtss.h"]
+    assert sorted(os.listdir(os.path.join(ROOT, "include"))) == ["mrtdf.h", "mrtdf.hpp", "mrtmc.h", "mrtss.h"]
 
 
 def test_version(mrtdf):

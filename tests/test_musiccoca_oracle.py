@@ -15,45 +15,6 @@ F = torch.nn.functional
 D, H, DH, FF, LAYERS, POOL_DH, VOCAB, LEVELS = 768, 12, 64, 3072, 12, 256, 1000, 12
 
 
-@pytest.fixture(scope="module")
-def style_bundle(tmp_path_factory):
-    from safetensors.numpy import save_file
-
-    rng = np.random.default_rng(90)
-    w = {}
-
-    def lin(p, out, inp):
-        w[p + ".weight"] = (rng.standard_normal((out, inp)) / np.sqrt(inp)).astype(np.float32)
-        w[p + ".bias"] = (rng.standard_normal(out) * 0.02).astype(np.float32)
-
-    def ln(p):
-        w[p + ".weight"] = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
-        w[p + ".bias"] = (0.1 * rng.standard_normal(D)).astype(np.float32)
-
-    w["token_embedding.weight"] = (rng.standard_normal((VOCAB, D)) / np.sqrt(D)).astype(np.float32)
-    for i in range(LAYERS):
-        p = f"text_layers.{i}"
-        ln(p + ".attn_ln")
-        ln(p + ".ffn_ln")
-        for n in ("q", "k", "v"):
-            lin(f"{p}.attn.{n}_proj", H * DH, D)
-        lin(p + ".attn.o_proj", D, H * DH)
-        lin(p + ".ffn_w1", FF, D)
-        lin(p + ".ffn_w2", D, FF)
-    ln("text_exit_ln")
-    ln("text_pooler.ln")
-    w["text_pooler.query"] = rng.standard_normal((1, 1, D)).astype(np.float32)
-    for n in ("q", "k", "v"):
-        lin(f"text_pooler.attn.{n}_proj", H * POOL_DH, D)
-    lin("text_pooler.attn.o_proj", D, H * POOL_DH)
-    w["text_pooler.attn._per_dim_scale"] = (0.5 * rng.standard_normal(POOL_DH)).astype(np.float32)
-    d = tmp_path_factory.mktemp("style")
-    enc, cb = str(d / "musiccoca_encoder.safetensors"), str(d / "musiccoca_codebooks.safetensors")
-    save_file(w, enc)
-    save_file({"codebooks": (rng.standard_normal((LEVELS, 1024, D)) / np.sqrt(D)).astype(np.float32)}, cb)
-    return enc, cb, w
-
-
 def _prompt(rng, n):
     # StyleModel::tokenize_text_ids (style_model.cpp): BOS = 1, then the
     # pieces, zeros after; padding 1.0 on every position after them
