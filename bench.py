@@ -356,6 +356,13 @@ def run_ours(args):
 
                 traceback.print_exc()
                 line["codec_decode"] = {"error": f"{type(exc).__name__}: {exc}"}
+            try:
+                line["style_prompt"] = style_prompt_leg(cpu=world == 1 and not args.no_cpu_baseline, device=local)
+            except Exception as exc:  # noqa: BLE001
+                import traceback
+
+                traceback.print_exc()
+                line["style_prompt"] = {"error": f"{type(exc).__name__}: {exc}"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.timed_only:
         tps, ms_cpu, cores = cpu_chunk()
         line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port",
@@ -556,6 +563,59 @@ def codec_decode(torch, peaks: dict, device, local: int, cpu: bool, S: int = 51,
         orc.close()
         out["cpu_baseline"] = {"ms": ms_cpu, "cores": oracle_py.num_threads(), "kind": "port",
                                "sample": f"one full chunk ({S} frames) through the float32 oracle"}
+    return out
+
+
+def style_prompt_leg(cpu: bool, device: int, reps: int = 10) -> dict:
+    """The style path once per prompt change (system.cpp:158-161): a 20-piece
+    prompt padded to 128 tokens -> MusicCoCa text tower -> 6 style RVQ levels
+    -> LLM ids (StyleModel::style_tokens_lm after tokenisation), through the
+    host API (ids in, style ids out). Random-init tower with the reference's
+    64,000-token vocabulary (numpy seed 13). float32 CUDA-core GEMMs: the
+    roofline is against the nominal B200 float32 FMA rate (148 SMs x 128
+    lanes x 2 x 1.965 GHz = 74.4 TFLOP/s). CPU baseline: the float32 oracle
+    (all host threads) on the same prompt."""
+    import mrtmc
+
+    rng = np.random.default_rng(14)
+    ids = np.zeros((1, 128), np.int32)
+    pad = np.ones((1, 128), np.float32)
+    ids[0, 0] = 1
+    ids[0, 1:21] = rng.integers(2, 64000, 20)
+    pad[0, :21] = 0
+    with tempfile.TemporaryDirectory() as td:
+        enc, cb = os.path.join(td, "musiccoca_encoder.safetensors"), os.path.join(td, "musiccoca_codebooks.safetensors")
+        mrtmc.write_random_safetensors(enc, cb, seed=13)
+        model = mrtmc.StyleModel(max_batch=1, device=device).load_safetensors(enc, cb)
+        for _ in range(3):
+            toks = model.style_tokens_lm(ids, pad)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            toks = model.style_tokens_lm(ids, pad)
+        ms = (time.perf_counter() - t0) * 1e3 / reps
+        L, D, FF, P = 128, 768, 3072, 3072
+        flops = 2.0 * L * (12 * (3 * D * D + D * D + 2 * D * FF) + 2 * P * D) + 12 * 12 * 4.0 * L * L * 64 \
+            + 2.0 * P * D + 12 * 4.0 * L * 256
+        out = {"prompt_tokens": 21, "padded_len": L, "ms": ms, "kernels": model.embed_kernels(1, L),
+               "gflop": flops / 1e9,
+               "roofline": {"bound": "fp32 FMA", "achieved": flops / (ms / 1e3) / 1e12, "peak": 74.4,
+                            "unit": "TFLOP/s", "frac": flops / (ms / 1e3) / 1e12 / 74.4,
+                            "peak_source": "nominal (no measured fp32 peak)"},
+               "style_ids": toks[0].tolist()}
+        model.close()
+        if cpu:
+            sys.path.insert(0, os.path.join(ROOT, "oracle"))
+            import oracle_py
+
+            oracle_py.set_num_threads(host_cores())
+            orc = oracle_py.StyleOracle(enc, cb)
+            t0 = time.perf_counter()
+            emb = orc.embed_text(ids, pad)
+            orc.quantize(emb, 6)
+            ms_cpu = (time.perf_counter() - t0) * 1e3
+            orc.close()
+            out["cpu_baseline"] = {"ms": ms_cpu, "cores": oracle_py.num_threads(), "kind": "port",
+                                   "sample": "the same prompt through the float32 oracle"}
     return out
 
 

@@ -54,6 +54,50 @@ def _check(rc: int) -> None:
     mrtdf._check(rc)
 
 
+def write_random_safetensors(encoder_path: str, codebooks_path: str, seed: int = 0, vocab: int = 64000,
+                             levels: int = RVQ_DEPTH, codebook_size: int = 1024) -> None:
+    """A random-init text-tower bundle with the reference's key layout
+    (musiccoca.cpp constructors: token_embedding, text_layers.{0..11},
+    text_exit_ln, text_pooler) and a (levels, codebook_size, 768) codebook
+    bundle: weights N(0, 1 / fan_in), biases N(0, 0.02^2), LayerNorm scales
+    1 + N(0, 0.1^2) and shifts N(0, 0.1^2), numpy seed `seed`. No reference
+    counterpart (the real bundles are downloaded; none is available here)."""
+    from safetensors.numpy import save_file
+
+    D, H, DH, FF, POOL_DH = EMBED_DIM, 12, 64, 3072, 256
+    rng = np.random.default_rng(seed)
+    w = {}
+
+    def lin(p, out, inp):
+        w[p + ".weight"] = (rng.standard_normal((out, inp), dtype=np.float32) / np.float32(np.sqrt(inp)))
+        w[p + ".bias"] = rng.standard_normal(out, dtype=np.float32) * np.float32(0.02)
+
+    def ln(p):
+        w[p + ".weight"] = 1 + np.float32(0.1) * rng.standard_normal(D, dtype=np.float32)
+        w[p + ".bias"] = np.float32(0.1) * rng.standard_normal(D, dtype=np.float32)
+
+    w["token_embedding.weight"] = rng.standard_normal((vocab, D), dtype=np.float32) / np.float32(np.sqrt(D))
+    for i in range(12):
+        p = f"text_layers.{i}"
+        ln(p + ".attn_ln")
+        ln(p + ".ffn_ln")
+        for n in ("q", "k", "v"):
+            lin(f"{p}.attn.{n}_proj", H * DH, D)
+        lin(p + ".attn.o_proj", D, H * DH)
+        lin(p + ".ffn_w1", FF, D)
+        lin(p + ".ffn_w2", D, FF)
+    ln("text_exit_ln")
+    ln("text_pooler.ln")
+    w["text_pooler.query"] = rng.standard_normal((1, 1, D), dtype=np.float32)
+    for n in ("q", "k", "v"):
+        lin(f"text_pooler.attn.{n}_proj", H * POOL_DH, D)
+    lin("text_pooler.attn.o_proj", D, H * POOL_DH)
+    w["text_pooler.attn._per_dim_scale"] = np.float32(0.5) * rng.standard_normal(POOL_DH, dtype=np.float32)
+    save_file(w, encoder_path)
+    cb = rng.standard_normal((levels, codebook_size, D), dtype=np.float32) / np.float32(np.sqrt(D))
+    save_file({"codebooks": cb}, codebooks_path)
+
+
 class StyleModel:
     """MusicCoCa text tower + style RVQ on one GPU, for up to ``max_batch``
     prompts of up to 128 tokens per call."""

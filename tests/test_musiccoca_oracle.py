@@ -102,3 +102,25 @@ def test_style_tokens(oracle, mrtdf, style_bundle):
     assert np.all((llm >= 17410 + np.arange(6) * 1024) & (llm < 17410 + (np.arange(6) + 1) * 1024))
     with pytest.raises(RuntimeError):
         o.quantize(emb, LEVELS + 1)
+
+
+def test_random_bundle_writer_loads_in_the_oracle(oracle, mrtdf, tmp_path, style_bundle):
+    """mrtmc.write_random_safetensors writes every key the text tower reads
+    with the reference's shapes (same key set as the test bundle)."""
+    import mrtmc
+    from safetensors.numpy import load_file
+
+    enc, cb = str(tmp_path / "e.safetensors"), str(tmp_path / "c.safetensors")
+    mrtmc.write_random_safetensors(enc, cb, seed=1, vocab=500, levels=3)
+    got = load_file(enc)
+    _, _, want = style_bundle
+    assert sorted(got) == sorted(want)
+    assert all(got[k].shape == want[k].shape for k in want if k != "token_embedding.weight")
+    assert got["token_embedding.weight"].shape == (500, D)
+    o = oracle.StyleOracle(enc, cb)
+    ids, pad = _prompt(np.random.default_rng(2), 7)
+    ids[ids >= 500] = 3
+    emb = o.embed_text(ids, pad)
+    assert np.isfinite(emb).all()
+    assert o.quantize(emb, 3).shape == (1, 3)
+    o.close()
