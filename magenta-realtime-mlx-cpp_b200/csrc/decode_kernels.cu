@@ -1480,8 +1480,6 @@ __device__ __forceinline__ unsigned block_scan_1024(unsigned v, unsigned* wsum) 
 
 template <typename T>
 __global__ void __launch_bounds__(kSampleSmallThreads) sample_small_kernel(const SampleParams p) {
-  pdl_wait();
-  pdl_launch_dependents();
   __shared__ unsigned hist[1024];
   __shared__ unsigned wsum[32];
   __shared__ uint32_t cand[1024];
@@ -1497,33 +1495,37 @@ __global__ void __launch_bounds__(kSampleSmallThreads) sample_small_kernel(const
   constexpr int EPC = Vec16<T>::N;
   const int nchunk = p.d / EPC;
 
-  // the frame's running embedding sum does not depend on the token: its load
-  // goes out next to the logits loads
+  // Before the dependency wait (none of it is written by the kernel ahead,
+  // the lm_head launch): the Gumbel noise of every candidate (seeds and
+  // injected draws are inputs of the chunk) and the frame's running
+  // embedding sum (written by the previous level's sampler, which completed
+  // before the kernel ahead passed its own wait).
   const bool fs_pre_ok = !p.is_first && tid < p.rows_per_seq * nchunk;
   uint4 fs_pre = make_uint4(0, 0, 0, 0);
   if (fs_pre_ok) {
     const int r = tid / nchunk, ch = tid - r * nchunk;
     fs_pre = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.fsum) + (size_t)(r0 + r) * p.d)[ch];
   }
+  const bool has = tid < n;
+  const bool sampled = p.temperature != 0.0f;
+  float gum = 0.f;
+  if (!p.forced && has && sampled) {
+    const float u = p.uniforms ? p.uniforms[(size_t)seq * p.uni_seq_stride + p.lo + tid]
+                               : philox_uniform(p.seeds ? p.seeds[seq] : p.seed_value, p.step, (uint32_t)(p.lo + tid));
+    gum = gumbel_from_uniform(u);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
 
   int token;
   if (p.forced) {
     token = p.forced[seq];
   } else {
-    const bool has = tid < n;
-    const bool sampled = p.temperature != 0.0f;
-    float a = 0.f, b = 0.f, u = 0.5f;
+    float a = 0.f, b = 0.f;
     if (has) {
       const float* l0 = p.logits + (size_t)r0 * p.logits_stride + (p.lo - p.col_offset);
       a = l0[tid];
       if (p.rows_per_seq == 2) b = l0[p.logits_stride + tid];
-      if (sampled && p.uniforms) u = p.uniforms[(size_t)seq * p.uni_seq_stride + p.lo + tid];
-    }
-    // noise first: independent of the loads above
-    float gum = 0.f;
-    if (has && sampled) {
-      if (!p.uniforms) u = philox_uniform(p.seeds ? p.seeds[seq] : p.seed_value, p.step, (uint32_t)(p.lo + tid));
-      gum = gumbel_from_uniform(u);
     }
     float v = -INFINITY;
     if (has) {

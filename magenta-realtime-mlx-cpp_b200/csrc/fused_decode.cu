@@ -277,12 +277,15 @@ __host__ __device__ inline SelfLayout self_layout(int d, int nkv) {
   SelfLayout L;
   L.rs = d * 2 + 16;
   int o = 0;
+  // the o_proj block is copied into the q/k/v rows' space once the q/k/v
+  // product is done (during the attention): a depth-stack self phase then
+  // fits beside an FFN phase on one SM, so the FFN's weights load while the
+  // self phase runs and the other way round
   L.wsm = o;
-  o = align128(o + (kQkvRowsPerHead / kFusedCluster) * L.rs);
+  L.wob = o;
+  o = align128(o + max((kQkvRowsPerHead / kFusedCluster) * L.rs, (d / kFusedCluster) * kBlkRow));
   L.xsm = o;
   o = align128(o + 2 * L.rs);
-  L.wob = o;
-  o = align128(o + (d / kFusedCluster) * kBlkRow);
   L.kv = o;
   o = align128(o + 2 * 2 * nkv * kBlkRow);
   L.recv = o;
@@ -396,20 +399,17 @@ __global__ void __launch_bounds__(kThreads, 1) fused_self_kernel(const FusedSelf
   uint4 nw[2];
   load_norm_chunks(p.norm_w, nch, B, nw);
   if (tid == 0) {
-    mbar_init(bar, 1);
+    mbar_init(bar, 1);      // q/k/v rows
+    mbar_init(bar + 1, 1);  // o_proj block
     fence_mbar_init();
   }
   __syncthreads();
-  if (warp == 0) {
-    const uint64_t pol = l2_policy(p.l2_keep != 0);
-    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(RQ * L.rs + dpc * kBlkRow));
-    __syncwarp();
+  const uint64_t pol = l2_policy(p.l2_keep != 0);
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar, (uint32_t)(RQ * L.rs));
     const uint8_t* src =
         reinterpret_cast<const uint8_t*>(p.wqkv) + ((size_t)h * kQkvRowsPerHead + (size_t)r * RQ) * L.rs;
-    if (lane == 0) bulk_g2s_hint(wsm, src, (uint32_t)(RQ * L.rs), bar, pol);
-    if (lane == 1)
-      bulk_g2s_hint(wob, reinterpret_cast<const uint8_t*>(p.wo_blk) + ((size_t)h * kFusedCluster + r) * dpc * kBlkRow,
-                    (uint32_t)(dpc * kBlkRow), bar, pol);
+    bulk_g2s_hint(wsm, src, (uint32_t)(RQ * L.rs), bar, pol);
   }
   // relative-position bias of this query for head h (a table written at load)
   float bias0 = 0.f, bias1 = 0.f;
@@ -440,6 +440,14 @@ __global__ void __launch_bounds__(kThreads, 1) fused_self_kernel(const FusedSelf
   mbar_wait_bounded(bar, 0, p.in.err);
   mma_rows<3>(smem_u32(wsm), RQ, smem_u32(xsm), L.rs, B, d, red);
   __syncthreads();
+  // the q/k/v rows are consumed: the o_proj block goes into their space (the
+  // proxy fence orders the reads above before the copy's writes)
+  if (tid == 0) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_arrive_expect_tx(bar + 1, (uint32_t)(dpc * kBlkRow));
+    bulk_g2s_hint(wob, reinterpret_cast<const uint8_t*>(p.wo_blk) + ((size_t)h * kFusedCluster + r) * dpc * kBlkRow,
+                  (uint32_t)(dpc * kBlkRow), bar + 1, pol);
+  }
   // q/k/v epilogue: k / v appended to the caches at `pos`; every value of
   // both rows pushed to all eight CTAs (recv[b][head row])
   cluster_wait();
@@ -528,6 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_self_kernel(const FusedSelf
   }
   __syncthreads();
   // o_proj block: output dims r * dpc .. + dpc of both rows
+  mbar_wait_bounded(bar + 1, 0, p.in.err);
   proj_red(smem_u32(wob), kBlkRow, dpc / 8, smem_u32(osm), kBlkRow, B, 64, p.in.acc_out, d, r * dpc, p.in.err);
 }
 
