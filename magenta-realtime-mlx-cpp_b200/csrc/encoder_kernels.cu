@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(128) enc_attn_bf16_kernel(const EncAttnParams 
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       nm[r] = fmaxf(m_r[r], mx[r]);
-      scale[r] = (m_r[r] == -INFINITY) ? 0.f : expf(m_r[r] - nm[r]);
+      scale[r] = (m_r[r] == -INFINITY) ? 0.f : __expf(m_r[r] - nm[r]);
       m_r[r] = nm[r];
     }
     // P is split as P_hi + P_lo with both halves bf16 (P_lo = bf16(P -
@@ -246,8 +246,8 @@ __global__ void __launch_bounds__(128) enc_attn_bf16_kernel(const EncAttnParams 
     uint32_t pf[4][4], pl[4][4];
 #pragma unroll
     for (int ni = 0; ni < 8; ++ni) {
-      const float p0 = expf(s[ni][0] - nm[0]), p1 = expf(s[ni][1] - nm[0]);
-      const float p2 = expf(s[ni][2] - nm[1]), p3 = expf(s[ni][3] - nm[1]);
+      const float p0 = __expf(s[ni][0] - nm[0]), p1 = __expf(s[ni][1] - nm[0]);
+      const float p2 = __expf(s[ni][2] - nm[1]), p3 = __expf(s[ni][3] - nm[1]);
       ls[0] += p0 + p1;
       ls[1] += p2 + p3;
       const int kk = ni >> 1;
