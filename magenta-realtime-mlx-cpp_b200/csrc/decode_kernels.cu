@@ -1196,7 +1196,7 @@ cudaError_t launch_attn_self(int dtype, const AttnParams& p, cudaStream_t s, boo
 }
 
 cudaError_t launch_attn_cross(int dtype, const AttnParams& p, cudaStream_t s, bool pdl) {
-  if (p.nsplit != kCrossSplit) return cudaErrorInvalidValue;
+  if (p.nsplit != 1 && p.nsplit != 2 && p.nsplit != 4 && p.nsplit != kCrossSplit) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.B * p.H, p.nsplit);
   cfg.blockDim = dim3(128);
@@ -1204,7 +1204,7 @@ cudaError_t launch_attn_cross(int dtype, const AttnParams& p, cudaStream_t s, bo
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = kCrossSplit;
+  attr[0].val.clusterDim.y = p.nsplit;
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;

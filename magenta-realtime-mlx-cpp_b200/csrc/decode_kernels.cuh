@@ -76,7 +76,7 @@ struct AttnParams {
   int* err;
   int B, H, cap, T;  // T = number of valid keys
   int inner;
-  int nsplit;  // cross attention: key slices = CTAs of one cluster (kCrossSplit)
+  int nsplit;  // cross attention: key slices = CTAs of one cluster (1, 2, 4 or kCrossSplit)
 };
 cudaError_t launch_attn_self(int dtype, const AttnParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_attn_cross(int dtype, const AttnParams& p, cudaStream_t s, bool pdl);

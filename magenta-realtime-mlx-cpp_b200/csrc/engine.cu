@@ -487,6 +487,16 @@ void wide_gemv(mrtdf_stream* st, int mode, bool norm, const GemvParams& p) {
 }
 
 // In the measurement hook, whether the current stack's phases are enqueued.
+// Key slices of the unfused cross attention: 8 for a few rows (latency), fewer
+// once the (row, head) pairs alone fill the GPU several times over (64 CFG
+// pairs: 2 slices, 503 -> 461 ms per chunk against 8; 1 or 4 slices are slower).
+int cross_split(const mrtdf_stream* st) {
+  const int pairs = st->B * st->eng->c.num_heads;
+  if (pairs >= 512) return 2;
+  if (pairs >= 256) return 4;
+  return kCrossSplit;
+}
+
 bool phase_on(const mrtdf_stream* st) { return !st->gemv_only || (st->phase_mask & (st->in_depth ? 2 : 1)); }
 
 void gemv(mrtdf_stream* st, int mode, bool norm, GemvParams p) {
@@ -553,7 +563,7 @@ void enqueue_decoder_layer(mrtdf_stream* st, const DecLayerDev& L, const void* x
     AttnParams ca{};
     ca.q = st->qb; ca.K = ck; ca.V = cv; ca.bias = nullptr; ca.out = st->ao;
     ca.err = st->err; ca.B = st->B; ca.H = c.num_heads; ca.cap = c.max_encoder_length;
-    ca.T = st->S; ca.inner = in; ca.nsplit = kCrossSplit;
+    ca.T = st->S; ca.inner = in; ca.nsplit = cross_split(st);
     if (!st->gemv_only) check_cuda(launch_attn_cross(c.dtype, ca, st->s, E->pdl), "attn_cross launch");
     // 6. cross o_proj + residual
     p = GemvParams{};
