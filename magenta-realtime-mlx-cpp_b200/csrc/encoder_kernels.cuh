@@ -49,8 +49,12 @@ struct EncAttnParams {
   const void* qkv;  // (B*S, 3*inner): q | k | v
   void* out;        // (B*S, inner)
   int B, S, H, inner;
+  int* err;         // device error word (bounded waits of the tensor-core kernel)
 };
 cudaError_t launch_enc_attention(int dtype, const EncAttnParams& p, cudaStream_t s, bool pdl);
+// bf16 attention on tcgen05 (enc_attn_tc.cu)
+cudaError_t launch_enc_attention_tc(const EncAttnParams& p, cudaStream_t s, bool pdl);
+cudaError_t enc_attn_tc_set_smem_limits();
 
 // x[b*S+s, :] = R(emb[ids[b*S+s], :] + pe[s, :]) with pe already rounded to the dtype.
 // An id outside [0, V) sets kErrBadToken in *err and reads row 0 instead.

@@ -751,7 +751,7 @@ void enqueue_encoder_layer(mrtdf_stream* st, const EncLayerDev& L, int S) {
   GemmParams g{};
   g.A = st->en; g.W = L.wqkv; g.out = st->eqkv; g.M = M; g.N = 3 * in; g.K = d; g.lda = d; g.ldo = 3 * in;
   check_cuda(encoder_gemm(st, kEpiStore, g), "gemm qkv");
-  EncAttnParams a{st->eqkv, st->eo, st->B, S, c.num_heads, in};
+  EncAttnParams a{st->eqkv, st->eo, st->B, S, c.num_heads, in, st->err};
   check_cuda(launch_enc_attention(dt, a, st->s, pdl), "enc attention");
   g = GemmParams{};
   g.A = st->eo; g.W = L.wo; g.out = st->ex; g.M = M; g.N = d; g.K = in; g.lda = in; g.ldo = d;
@@ -995,6 +995,7 @@ int mrtdf_create(const mrtdf_config* cfg, int device, mrtdf_engine** out) {
     CUDA_OK(gemv_set_smem_limits());
     CUDA_OK(gemm_tc_set_smem_limits());
     CUDA_OK(fused_set_smem_limits());
+    CUDA_OK(enc_attn_tc_set_smem_limits());
     E->fused = cfg->dtype == MRTDF_DTYPE_BF16 && env_flag("MRTDF_FUSED", true) &&
                fused_supported(cfg->d_model, cfg->num_heads, cfg->d_kv, cfg->d_ff);
     if (E->fused && fused_ffn_plan(cfg->d_model, cfg->d_ff, E->num_sms, &E->ffn_plan) != cudaSuccess) {
