@@ -411,8 +411,8 @@ def e2e_leg(mrtdf, torch, cfg, st, ext, ids, K: int, rank: int, dist, device) ->
 # FFN) and depth level 3 (self, FFN, self) plus two lm_head slices. Per-launch
 # means over a stack's launch mix (temporal: 1 self + 1 cross + 1 FFN per
 # layer; depth: 4 self + 4 FFN + 1 lm_head per level).
-TRAFFIC_TEMPORAL = (8716544 + 13091584 + 17778176) / 3
-TRAFFIC_DEPTH = (4 * (8604928 + 1605120 + 8554240 + 1151488) / 2 + 4 * 14497792 + (1961728 + 1586176) / 2) / 9
+TRAFFIC_TEMPORAL = (8715008 + 13177088 + 17774336) / 3
+TRAFFIC_DEPTH = (4 * (8666624 + 1420800 + 8615424 + 823552) / 2 + 4 * 14456576 + (2048256 + 1632768) / 2) / 9
 
 
 def roofline_leg(mrtdf, eng, cfg, st, peaks: dict) -> dict:
