@@ -186,6 +186,27 @@ def test_codec_create_fails_cleanly_without_sm100(mrtdf):
     assert ei.value.code == 2  # MRTDF_ERR_CUDA
 
 
+def test_style_model_fails_cleanly_without_sm100(mrtdf):
+    """The style path (include/mrtmc.h) refuses without a B200 (no CPU
+    fallback), and rejects bad arguments before touching a device."""
+    import torch
+
+    import mrtmc
+
+    lib = mrtmc.lib()
+    out = ctypes.c_void_p()
+    assert lib.mrtmc_create(0, 0, ctypes.byref(out)) == 1  # max_batch must be in [1, 64]
+    assert lib.mrtmc_create(0, 65, ctypes.byref(out)) == 1
+    assert lib.mrtmc_create(0, 1, None) == 1
+    assert lib.mrtmc_embed_text(None, None, None, 1, 1, None) == 1  # NULL model
+    assert lib.mrtmc_embed_kernels(None, 1, 1) == -1
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    with pytest.raises(mrtdf.MrtdfError) as ei:
+        mrtmc.StyleModel(max_batch=1)
+    assert ei.value.code == 2  # MRTDF_ERR_CUDA
+
+
 def test_codec_writer_argument_errors(mrtdf, tmp_path):
     import mrtss
 
