@@ -5,12 +5,14 @@
 // scale 1.0, no mask, bidirectional) inside EncoderLayer (modules.cpp:349-358):
 // softmax in fp32 over the keys of one (row, head), then P V.
 //
-// CTA = 128 queries of one (row, head), 192 threads:
-//   warps 0-3   softmax: thread t owns query row t (TMEM lane t);
-//   warp 4      TMA producer (lane 0): Q once, then K (and V) tiles of 64 keys
+// CTA = 128 queries of one (row, head), 320 threads:
+//   warps 0-7   softmax: two threads per query row (row = TMEM lane t % 128),
+//               each taking 32 of a tile's 64 key columns; the row's maximum
+//               and sum are combined through shared memory after each pass;
+//   warp 8      TMA producer (lane 0): Q once, then K (and V) tiles of 64 keys
 //               through a 2-stage ring, 128-byte swizzle, straight from the
 //               (B*S, 3*inner) q|k|v rows;
-//   warp 5      MMA issuer (lane 0): S = Q K^T (tcgen05.mma M 128, N 64) into
+//   warp 9      MMA issuer (lane 0): S = Q K^T (tcgen05.mma M 128, N 64) into
 //               one of two 64-column TMEM buffers, O += P V (M 128, N 64, V as
 //               an MN-major operand) into 64 more columns.
 // Two passes over the keys: the row maxima first, then P = exp(s - max) with
@@ -42,7 +44,8 @@ typedef __nv_bfloat16 bf16;
 constexpr int kQ = 128;    // queries per CTA
 constexpr int kKt = 64;    // keys per tile
 constexpr int kDh = 64;    // head dimension
-constexpr int kThreadsA = 192;
+constexpr int kSoft = 256;                // softmax threads: two per query row
+constexpr int kThreadsA = kSoft + 64;    // + the TMA and MMA warps
 constexpr int kQBytes = kQ * kDh * 2;     // 16 KB
 constexpr int kKVBytes = kKt * kDh * 2;   // 8 KB per K or V tile
 constexpr int kPBytes = kQ * kKt * 2;     // 16 KB per P half
@@ -137,8 +140,8 @@ __global__ void __launch_bounds__(kThreadsA, (kNPB == 1 ? 2 : 1))
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(br.s_full + i, 1);
-      mbar_init(br.s_empty + i, 128);
-      mbar_init(br.p_full + i, 128);
+      mbar_init(br.s_empty + i, kSoft);
+      mbar_init(br.p_full + i, kSoft);
       mbar_init(br.p_empty + i, 1);
     }
     mbar_init(br.o_done, 1);
@@ -161,7 +164,7 @@ __global__ void __launch_bounds__(kThreadsA, (kNPB == 1 ? 2 : 1))
     return false;
   };
 
-  if (warp == 4) {
+  if (warp == kSoft / 32) {
     // ---- TMA producer ----
     if (lane == 0) {
       const int xq = h * kDh, xk = p.inner + h * kDh, xv = 2 * p.inner + h * kDh;
@@ -184,7 +187,7 @@ __global__ void __launch_bounds__(kThreadsA, (kNPB == 1 ? 2 : 1))
         mbar_wait_bounded(br.kv_full + u % kNS, (uint32_t)((u / kNS) & 1), p.err);
       mbar_wait_bounded(br.q_full, 0, p.err);
     }
-  } else if (warp == 5) {
+  } else if (warp == kSoft / 32 + 1) {
     // ---- MMA issuer ----
     if (lane == 0) {
       const uint32_t aq = smem_u32(smem + kOffQ);
@@ -232,8 +235,12 @@ __global__ void __launch_bounds__(kThreadsA, (kNPB == 1 ? 2 : 1))
       mbar_wait_bounded(br.drain, 0, p.err);
     }
   } else {
-    // ---- softmax: thread tid = query row tid = TMEM lane tid ----
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    // ---- softmax: two threads per query row: row = TMEM lane = tid % 128,
+    // half = tid / 128 takes columns 32 half .. + 32 of every S tile ----
+    __shared__ float xm[2][kQ], xl[2][kQ];
+    const int row = tid & (kQ - 1), half = tid >> 7;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const int c0 = half * 32;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int u = 0; ok && u < nkt; ++u) {
@@ -241,17 +248,21 @@ __global__ void __launch_bounds__(kThreadsA, (kNPB == 1 ? 2 : 1))
       if (!(ok = wait(br.s_full + sb, (uint32_t)((u >> 1) & 1)))) break;
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < kKt; c += 16) {
+      for (int c = 0; c < 32; c += 16) {
         uint32_t r[16];
-        tmem_ld16(tmem + lane_base + (uint32_t)(sb * 64 + c), r);
+        tmem_ld16(tmem + lane_base + (uint32_t)(sb * 64 + c0 + c), r);
         tmem_wait_ld();
 #pragma unroll
         for (int q = 0; q < 16; ++q)
-          if (u * kKt + c + q < S) m = fmaxf(m, __uint_as_float(r[q]));
+          if (u * kKt + c0 + c + q < S) m = fmaxf(m, __uint_as_float(r[q]));
       }
       tc_fence_before();
       mbar_arrive(br.s_empty + sb);
     }
+    // the row maximum from both halves (every softmax thread passes here once)
+    xm[half][row] = m;
+    asm volatile("bar.sync 1, %0;" ::"n"(kSoft) : "memory");
+    m = fmaxf(xm[0][row], xm[1][row]);
     for (int j = 0; ok && j < nkt; ++j) {
       const int u = nkt + j, sb = u & 1, pb = j % kNPB;
       if (!(ok = wait(br.s_full + sb, (uint32_t)((u >> 1) & 1)))) break;
@@ -260,14 +271,14 @@ __global__ void __launch_bounds__(kThreadsA, (kNPB == 1 ? 2 : 1))
       uint8_t* ph = smem + kOffPh + pb * kPBytes;
       uint8_t* pl = smem + kOffPl + pb * kPBytes;
 #pragma unroll
-      for (int c = 0; c < kKt; c += 16) {
+      for (int c = 0; c < 32; c += 16) {
         uint32_t r[16];
-        tmem_ld16(tmem + lane_base + (uint32_t)(sb * 64 + c), r);
+        tmem_ld16(tmem + lane_base + (uint32_t)(sb * 64 + c0 + c), r);
         tmem_wait_ld();
         uint32_t hi[8], lo[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const int k0 = j * kKt + c + 2 * e;
+          const int k0 = j * kKt + c0 + c + 2 * e;
           const float a0 = k0 < S ? __expf(__uint_as_float(r[2 * e]) - m) : 0.f;
           const float a1 = k0 + 1 < S ? __expf(__uint_as_float(r[2 * e + 1]) - m) : 0.f;
           l += a0;
@@ -275,11 +286,11 @@ __global__ void __launch_bounds__(kThreadsA, (kNPB == 1 ? 2 : 1))
           hi[e] = pack_bf16(a0, a1);
           lo[e] = pack_bf16(a0 - __uint_as_float(hi[e] << 16), a1 - __uint_as_float(hi[e] & 0xffff0000u));
         }
-        const int ch = c >> 3;  // 16-byte chunk of the 128-byte row
-        *reinterpret_cast<uint4*>(ph + sw128(tid, ch)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(ph + sw128(tid, ch + 1)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-        *reinterpret_cast<uint4*>(pl + sw128(tid, ch)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        *reinterpret_cast<uint4*>(pl + sw128(tid, ch + 1)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+        const int ch = (c0 + c) >> 3;  // 16-byte chunk of the 128-byte row
+        *reinterpret_cast<uint4*>(ph + sw128(row, ch)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(ph + sw128(row, ch + 1)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+        *reinterpret_cast<uint4*>(pl + sw128(row, ch)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(pl + sw128(row, ch + 1)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
       }
       tc_fence_before();
       mbar_arrive(br.s_empty + sb);
@@ -287,25 +298,29 @@ __global__ void __launch_bounds__(kThreadsA, (kNPB == 1 ? 2 : 1))
       mbar_arrive(br.p_full + pb);
     }
     if (ok) ok = wait(br.o_done, 0);
+    // the row sum from both halves (every softmax thread passes here once)
+    xl[half][row] = l;
+    asm volatile("bar.sync 1, %0;" ::"n"(kSoft) : "memory");
+    l = xl[0][row] + xl[1][row];
     // the TMEM loads below are .sync.aligned: decide warp-uniformly
     ok = __all_sync(0xffffffffu, ok) != 0;
     if (ok) {
       tc_fence_after();
-      const int qr = q0 + tid;
+      const int qr = q0 + row;
       const float inv_l = 1.0f / l;
       bf16* out = reinterpret_cast<bf16*>(p.out) + ((size_t)row0 + qr) * p.inner + h * kDh;
 #pragma unroll
-      for (int c = 0; c < kDh; c += 16) {
+      for (int c = 0; c < 32; c += 16) {
         uint32_t rr[16];
-        tmem_ld16(tmem + lane_base + (uint32_t)(128 + c), rr);
+        tmem_ld16(tmem + lane_base + (uint32_t)(128 + c0 + c), rr);
         tmem_wait_ld();
         uint32_t w[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q)
           w[q] = pack_bf16(__uint_as_float(rr[2 * q]) * inv_l, __uint_as_float(rr[2 * q + 1]) * inv_l);
         if (qr < S) {
-          reinterpret_cast<uint4*>(out + c)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          reinterpret_cast<uint4*>(out + c)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          reinterpret_cast<uint4*>(out + c0 + c)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          reinterpret_cast<uint4*>(out + c0 + c)[1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
       }
     }
