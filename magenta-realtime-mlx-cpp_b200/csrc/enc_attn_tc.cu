@@ -44,8 +44,6 @@ typedef __nv_bfloat16 bf16;
 constexpr int kQ = 128;    // queries per CTA
 constexpr int kKt = 64;    // keys per tile
 constexpr int kDh = 64;    // head dimension
-constexpr int kSoft = 256;                // softmax threads: two per query row
-constexpr int kThreadsA = kSoft + 64;    // + the TMA and MMA warps
 constexpr int kQBytes = kQ * kDh * 2;     // 16 KB
 constexpr int kKVBytes = kKt * kDh * 2;   // 8 KB per K or V tile
 constexpr int kPBytes = kQ * kKt * 2;     // 16 KB per P half
@@ -105,9 +103,15 @@ struct Bars {
   uint64_t* drain;
 };
 
-template <int kNS, int kNPB>
-__global__ void __launch_bounds__(kThreadsA, (kNPB == 1 ? 2 : 1))
+// kSplit softmax threads per query row, each taking 64 / kSplit key columns
+template <int kSplit>
+constexpr int threads_of() { return 128 * kSplit + 64; }  // + the TMA and MMA warps
+
+template <int kNS, int kNPB, int kSplit>
+__global__ void __launch_bounds__(threads_of<kSplit>(), (kNPB == 1 ? 2 : 1))
     enc_attn_tc_kernel(const __grid_constant__ CUtensorMap tm, const EncAttnParams p) {
+  constexpr int kSoft = 128 * kSplit;
+  constexpr int kCols = kKt / kSplit;  // key columns per softmax thread
   typedef AttnCfg<kNS, kNPB> C;
   constexpr int kOffQ = C::kOffQ, kOffK = C::kOffK, kOffV = C::kOffV, kOffPh = C::kOffPh, kOffPl = C::kOffPl,
                 kOffBar = C::kOffBar;
@@ -237,10 +241,10 @@ __global__ void __launch_bounds__(kThreadsA, (kNPB == 1 ? 2 : 1))
   } else {
     // ---- softmax: two threads per query row: row = TMEM lane = tid % 128,
     // half = tid / 128 takes columns 32 half .. + 32 of every S tile ----
-    __shared__ float xm[2][kQ], xl[2][kQ];
+    __shared__ float xm[kSplit][kQ], xl[kSplit][kQ];
     const int row = tid & (kQ - 1), half = tid >> 7;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    const int c0 = half * 32;
+    const int c0 = half * kCols;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int u = 0; ok && u < nkt; ++u) {
@@ -248,7 +252,7 @@ __global__ void __launch_bounds__(kThreadsA, (kNPB == 1 ? 2 : 1))
       if (!(ok = wait(br.s_full + sb, (uint32_t)((u >> 1) & 1)))) break;
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < 32; c += 16) {
+      for (int c = 0; c < kCols; c += 16) {
         uint32_t r[16];
         tmem_ld16(tmem + lane_base + (uint32_t)(sb * 64 + c0 + c), r);
         tmem_wait_ld();
@@ -262,7 +266,9 @@ __global__ void __launch_bounds__(kThreadsA, (kNPB == 1 ? 2 : 1))
     // the row maximum from both halves (every softmax thread passes here once)
     xm[half][row] = m;
     asm volatile("bar.sync 1, %0;" ::"n"(kSoft) : "memory");
-    m = fmaxf(xm[0][row], xm[1][row]);
+    m = xm[0][row];
+#pragma unroll
+    for (int i = 1; i < kSplit; ++i) m = fmaxf(m, xm[i][row]);
     for (int j = 0; ok && j < nkt; ++j) {
       const int u = nkt + j, sb = u & 1, pb = j % kNPB;
       if (!(ok = wait(br.s_full + sb, (uint32_t)((u >> 1) & 1)))) break;
@@ -271,7 +277,7 @@ __global__ void __launch_bounds__(kThreadsA, (kNPB == 1 ? 2 : 1))
       uint8_t* ph = smem + kOffPh + pb * kPBytes;
       uint8_t* pl = smem + kOffPl + pb * kPBytes;
 #pragma unroll
-      for (int c = 0; c < 32; c += 16) {
+      for (int c = 0; c < kCols; c += 16) {
         uint32_t r[16];
         tmem_ld16(tmem + lane_base + (uint32_t)(sb * 64 + c0 + c), r);
         tmem_wait_ld();
@@ -301,7 +307,9 @@ __global__ void __launch_bounds__(kThreadsA, (kNPB == 1 ? 2 : 1))
     // the row sum from both halves (every softmax thread passes here once)
     xl[half][row] = l;
     asm volatile("bar.sync 1, %0;" ::"n"(kSoft) : "memory");
-    l = xl[0][row] + xl[1][row];
+    l = xl[0][row];
+#pragma unroll
+    for (int i = 1; i < kSplit; ++i) l += xl[i][row];
     // the TMEM loads below are .sync.aligned: decide warp-uniformly
     ok = __all_sync(0xffffffffu, ok) != 0;
     if (ok) {
@@ -310,7 +318,7 @@ __global__ void __launch_bounds__(kThreadsA, (kNPB == 1 ? 2 : 1))
       const float inv_l = 1.0f / l;
       bf16* out = reinterpret_cast<bf16*>(p.out) + ((size_t)row0 + qr) * p.inner + h * kDh;
 #pragma unroll
-      for (int c = 0; c < 32; c += 16) {
+      for (int c = 0; c < kCols; c += 16) {
         uint32_t rr[16];
         tmem_ld16(tmem + lane_base + (uint32_t)(128 + c0 + c), rr);
         tmem_wait_ld();
@@ -349,11 +357,14 @@ bool make_qkv_map(CUtensorMap* m, const void* base, int rows, int cols) {
 
 }  // namespace
 
+// per-shape variants: one wave (few CTAs) / many waves
+constexpr int kSplitFew = 2, kSplitMany = 2;  // 4 per row measured slower (1.51 vs 1.48 ms, one CFG pair)
+
 cudaError_t enc_attn_tc_set_smem_limits() {
-  cudaError_t e = cudaFuncSetAttribute(enc_attn_tc_kernel<2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(enc_attn_tc_kernel<2, 2, kSplitFew>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        AttnCfg<2, 2>::kSmem);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(enc_attn_tc_kernel<3, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(enc_attn_tc_kernel<3, 1, kSplitMany>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              AttnCfg<3, 1>::kSmem);
   return e;
 }
@@ -373,7 +384,7 @@ cudaError_t launch_enc_attention_tc(const EncAttnParams& p, cudaStream_t s, bool
   const bool few = (long long)grid.x * grid.y <= 2LL * sms;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(kThreadsA);
+  cfg.blockDim = dim3(few ? threads_of<kSplitFew>() : threads_of<kSplitMany>());
   cfg.dynamicSmemBytes = few ? AttnCfg<2, 2>::kSmem : AttnCfg<3, 1>::kSmem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -381,8 +392,8 @@ cudaError_t launch_enc_attention_tc(const EncAttnParams& p, cudaStream_t s, bool
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return few ? cudaLaunchKernelEx(&cfg, enc_attn_tc_kernel<2, 2>, tm, p)
-             : cudaLaunchKernelEx(&cfg, enc_attn_tc_kernel<3, 1>, tm, p);
+  return few ? cudaLaunchKernelEx(&cfg, enc_attn_tc_kernel<2, 2, kSplitFew>, tm, p)
+             : cudaLaunchKernelEx(&cfg, enc_attn_tc_kernel<3, 1, kSplitMany>, tm, p);
 }
 
 }  // namespace mrtdf
