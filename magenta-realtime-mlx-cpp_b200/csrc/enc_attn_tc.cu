@@ -7,21 +7,26 @@
 //
 // CTA = 128 queries of one (row, head), 320 threads:
 //   warps 0-7   softmax: two threads per query row (row = TMEM lane t % 128),
-//               each taking 32 of a tile's 64 key columns; the row's maximum
-//               and sum are combined through shared memory after each pass;
-//   warp 8      TMA producer (lane 0): Q once, then K (and V) tiles of 64 keys
-//               through a 2-stage ring, 128-byte swizzle, straight from the
-//               (B*S, 3*inner) q|k|v rows;
+//               each owning 32 of a tile's 64 key columns (the key half);
+//   warp 8      TMA producer (lane 0): Q once, then K and V tiles of 64 keys
+//               through a 2- or 3-stage ring, 128-byte swizzle, straight from
+//               the (B*S, 3*inner) q|k|v rows;
 //   warp 9      MMA issuer (lane 0): S = Q K^T (tcgen05.mma M 128, N 64) into
-//               one of two 64-column TMEM buffers, O += P V (M 128, N 64, V as
-//               an MN-major operand) into 64 more columns.
-// Two passes over the keys: the row maxima first, then P = exp(s - max) with
-// the final maximum (the reference's softmax: no rescaling), l += P, and P
-// split as P_hi + P_lo (both bf16, P_lo = bf16(P - P_hi)) into two K-major
-// 128 x 64 tiles (double-buffered) so that O += P_hi V + P_lo V keeps ~16
-// mantissa bits of P. S(j + 1) is issued before P(j) V, so the softmax of a
-// tile overlaps the products of its neighbours. Keys past S are masked to
-// P = 0 (their K / V rows are other rows' data or the TMA's zero fill).
+//               one of two 64-column TMEM buffers, then O_h += P_h V_h for the
+//               two key halves h (M 128, N 64, V as an MN-major operand) into
+//               two more 64-column accumulators.
+// One pass over the keys. Each softmax thread keeps its own running maximum
+// m over its key half and computes P = exp(s - m), l += P; m is raised only
+// when a tile's maximum exceeds it by more than kLazy (then O_h and l are
+// scaled by exp(m_old - m_new) once the previous P V has retired), so P stays
+// below e^kLazy and rescaling is rare. The end combines the halves exactly:
+// O = (a_0 O_0 + a_1 O_1) / (a_0 l_0 + a_1 l_1), a_h = exp(m_h - max(m_0, m_1)),
+// i.e. softmax(s) V with fp32 sums. P is split as P_hi + P_lo (both bf16,
+// P_lo = bf16(P - P_hi)) into two K-major 128 x 64 tiles (double-buffered) so
+// that O += P_hi V + P_lo V keeps ~16 mantissa bits of P. S(j + 1) is issued
+// before P(j) V, so the softmax of a tile overlaps the products of its
+// neighbours. Keys past S are masked to P = 0 (their K / V rows are other
+// rows' data or the TMA's zero fill).
 // mbarriers hand every buffer between the roles; every wait is bounded, a
 // failed wait stops all roles and reports in the error word, and the MMA
 // issuer drains its products before TMEM (256 columns) is released.
@@ -60,7 +65,10 @@ struct AttnCfg {
   static constexpr int kOffBar = kOffPl + NPB * kPBytes;
   static constexpr int kSmem = kOffBar + 256 + 1024;  // barriers, + 1024-byte alignment slack
 };
-constexpr uint32_t kTmemColsA = 256;                   // S: 0..63 and 64..127, O: 128..191
+constexpr uint32_t kTmemColsA = 256;  // S: 0..63 and 64..127; O_0: 128..191, O_1: 192..255
+// A running maximum is raised only when a tile exceeds it by more than this
+// (natural-log units): P = exp(s - m) stays below e^8 ~ 2981.
+constexpr float kLazy = 8.0f;
 // kind::f16, D f32, A / B bf16, M 128, N 64; K-major A and B ...
 constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(64 >> 3) << 17) |
                              ((uint32_t)(128 >> 4) << 24);
@@ -176,13 +184,12 @@ __global__ void __launch_bounds__(threads_of<kSplit>(), (kNPB == 1 ? 2 : 1))
       tma_load_2d(smem + kOffQ, &tm, xq, row0 + q0, br.q_full);  // 64-row boxes: two loads
       tma_load_2d(smem + kOffQ + kQBytes / 2, &tm, xq, row0 + q0 + 64, br.q_full);
       int issued = 0;
-      for (int u = 0; u < 2 * nkt; ++u) {
-        const int st = u % kNS, j = u % nkt;
-        const bool pass2 = u >= nkt;
+      for (int u = 0; u < nkt; ++u) {
+        const int st = u % kNS;
         if (u >= kNS && !wait(br.kv_empty + st, (uint32_t)(((u / kNS) - 1) & 1))) break;
-        mbar_arrive_expect_tx(br.kv_full + st, pass2 ? 2 * kKVBytes : kKVBytes);
-        tma_load_2d(smem + kOffK + st * kKVBytes, &tm, xk, row0 + j * kKt, br.kv_full + st);
-        if (pass2) tma_load_2d(smem + kOffV + st * kKVBytes, &tm, xv, row0 + j * kKt, br.kv_full + st);
+        mbar_arrive_expect_tx(br.kv_full + st, 2 * kKVBytes);
+        tma_load_2d(smem + kOffK + st * kKVBytes, &tm, xk, row0 + u * kKt, br.kv_full + st);
+        tma_load_2d(smem + kOffV + st * kKVBytes, &tm, xv, row0 + u * kKt, br.kv_full + st);
         issued = u + 1;
       }
       // no copy may still be landing when the CTA exits: wait (bounded) for
@@ -209,27 +216,25 @@ __global__ void __launch_bounds__(threads_of<kSplit>(), (kNPB == 1 ? 2 : 1))
         mma_commit(br.s_full + sb);
         return true;
       };
-      for (int u = 0; ok && u < nkt; ++u) {
-        ok = issue_s(u);
-        if (ok) mma_commit(br.kv_empty + u % kNS);
-      }
-      if (ok) ok = issue_s(nkt);
+      if (ok) ok = issue_s(0);
       for (int j = 0; ok && j < nkt; ++j) {
-        const int u = nkt + j, st = u % kNS, pb = j % kNPB;
-        if (j + 1 < nkt && !(ok = issue_s(u + 1))) break;
+        const int st = j % kNS, pb = j % kNPB;
+        if (j + 1 < nkt && !(ok = issue_s(j + 1))) break;
         if (!(ok = wait(br.p_full + pb, (uint32_t)((j / kNPB) & 1)))) break;
         tc_fence_after();
         const uint32_t aph = smem_u32(smem + kOffPh + pb * kPBytes), apl = smem_u32(smem + kOffPl + pb * kPBytes);
         const uint32_t av = smem_u32(smem + kOffV + st * kKVBytes);
         // K-major P: the k-th 16-key slice starts 32 bytes further; MN-major
-        // V: 16 keys = 16 rows of 128 bytes further (two 8-row swizzle atoms)
+        // V: 16 keys = 16 rows of 128 bytes further (two 8-row swizzle atoms).
+        // Slices 0, 1 (keys 0-31) go to O_0, slices 2, 3 to O_1.
 #pragma unroll
         for (int kk = 0; kk < kKt / 16; ++kk)
-          umma(tmem + 128, smem_desc_sw128(aph + kk * 32), smem_desc_sw128(av + kk * 2048), kIdescPV,
-               (j | kk) != 0);
+          umma(tmem + 128 + (uint32_t)(kk >> 1) * 64, smem_desc_sw128(aph + kk * 32), smem_desc_sw128(av + kk * 2048),
+               kIdescPV, (j != 0 || (kk & 1)) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < kKt / 16; ++kk)
-          umma(tmem + 128, smem_desc_sw128(apl + kk * 32), smem_desc_sw128(av + kk * 2048), kIdescPV, 1u);
+          umma(tmem + 128 + (uint32_t)(kk >> 1) * 64, smem_desc_sw128(apl + kk * 32), smem_desc_sw128(av + kk * 2048),
+               kIdescPV, 1u);
         mma_commit(br.p_empty + pb);
         mma_commit(br.kv_empty + st);
       }
@@ -240,53 +245,76 @@ __global__ void __launch_bounds__(threads_of<kSplit>(), (kNPB == 1 ? 2 : 1))
     }
   } else {
     // ---- softmax: two threads per query row: row = TMEM lane = tid % 128,
-    // half = tid / 128 takes columns 32 half .. + 32 of every S tile ----
+    // half = tid / 128 owns key columns 32 half .. + 32 of every S tile and
+    // the accumulator O_half ----
+    static_assert(kSplit == 2, "one O accumulator per key half");
     __shared__ float xm[kSplit][kQ], xl[kSplit][kQ];
     const int row = tid & (kQ - 1), half = tid >> 7;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const int c0 = half * kCols;
+    const uint32_t ocol = 128u + (uint32_t)half * 64u;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int u = 0; ok && u < nkt; ++u) {
-      const int sb = u & 1;
-      if (!(ok = wait(br.s_full + sb, (uint32_t)((u >> 1) & 1)))) break;
+    for (int j = 0; ok && j < nkt; ++j) {
+      const int sb = j & 1, pb = j % kNPB;
+      ok = wait(br.s_full + sb, (uint32_t)((j >> 1) & 1));
+      // the TMEM accesses below are .sync.aligned: decide warp-uniformly
+      if (!(ok = __all_sync(0xffffffffu, ok) != 0)) break;
       tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < kCols; c += 16) {
-        uint32_t r[16];
-        tmem_ld16(tmem + lane_base + (uint32_t)(sb * 64 + c0 + c), r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int q = 0; q < 16; ++q)
-          if (u * kKt + c0 + c + q < S) m = fmaxf(m, __uint_as_float(r[q]));
-      }
+      uint32_t r[kCols];
+      tmem_ld16(tmem + lane_base + (uint32_t)(sb * 64 + c0), r);
+      tmem_ld16(tmem + lane_base + (uint32_t)(sb * 64 + c0 + 16), r + 16);
+      tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(br.s_empty + sb);
-    }
-    // the row maximum from both halves (every softmax thread passes here once)
-    xm[half][row] = m;
-    asm volatile("bar.sync 1, %0;" ::"n"(kSoft) : "memory");
-    m = xm[0][row];
+      const int kb = j * kKt + c0;  // key of r[0]
+      float mt = -INFINITY;
 #pragma unroll
-    for (int i = 1; i < kSplit; ++i) m = fmaxf(m, xm[i][row]);
-    for (int j = 0; ok && j < nkt; ++j) {
-      const int u = nkt + j, sb = u & 1, pb = j % kNPB;
-      if (!(ok = wait(br.s_full + sb, (uint32_t)((u >> 1) & 1)))) break;
-      if (j >= kNPB && !(ok = wait(br.p_empty + pb, (uint32_t)(((j / kNPB) - 1) & 1)))) break;
-      tc_fence_after();
+      for (int q = 0; q < kCols; ++q)
+        if (kb + q < S) mt = fmaxf(mt, __uint_as_float(r[q]));
+      float alpha = 1.f;
+      bool resc = false;
+      if (mt > m + kLazy) {  // also the first tile with a key (m = -inf)
+        if (m != -INFINITY) {
+          alpha = __expf(m - mt);
+          resc = true;
+        }
+        m = mt;
+        l *= alpha;
+      }
+      if (__any_sync(0xffffffffu, resc)) {
+        // O_half holds products made with the old maximum: once P(j - 1) V
+        // has retired (j >= 1: the old maximum came from an earlier tile),
+        // scale it in TMEM; the next P V is issued after this thread's
+        // p_full arrival below
+        ok = wait(br.p_empty + (j - 1) % kNPB, (uint32_t)(((j - 1) / kNPB) & 1));
+        if (!(ok = __all_sync(0xffffffffu, ok) != 0)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 64; c += 16) {
+          uint32_t o[16];
+          tmem_ld16(tmem + lane_base + ocol + (uint32_t)c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < 16; ++q) o[q] = __float_as_uint(__uint_as_float(o[q]) * alpha);
+          tmem_st16(tmem + lane_base + ocol + (uint32_t)c, o);
+        }
+        tmem_wait_st();
+      }
+      if (j >= kNPB) {
+        ok = wait(br.p_empty + pb, (uint32_t)(((j / kNPB) - 1) & 1));
+        if (!(ok = __all_sync(0xffffffffu, ok) != 0)) break;
+      }
       uint8_t* ph = smem + kOffPh + pb * kPBytes;
       uint8_t* pl = smem + kOffPl + pb * kPBytes;
 #pragma unroll
       for (int c = 0; c < kCols; c += 16) {
-        uint32_t r[16];
-        tmem_ld16(tmem + lane_base + (uint32_t)(sb * 64 + c0 + c), r);
-        tmem_wait_ld();
         uint32_t hi[8], lo[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const int k0 = j * kKt + c0 + c + 2 * e;
-          const float a0 = k0 < S ? __expf(__uint_as_float(r[2 * e]) - m) : 0.f;
-          const float a1 = k0 + 1 < S ? __expf(__uint_as_float(r[2 * e + 1]) - m) : 0.f;
+          const int k0 = kb + c + 2 * e;
+          const float a0 = k0 < S ? __expf(__uint_as_float(r[c + 2 * e]) - m) : 0.f;
+          const float a1 = k0 + 1 < S ? __expf(__uint_as_float(r[c + 2 * e + 1]) - m) : 0.f;
           l += a0;
           l += a1;
           hi[e] = pack_bf16(a0, a1);
@@ -299,33 +327,37 @@ __global__ void __launch_bounds__(threads_of<kSplit>(), (kNPB == 1 ? 2 : 1))
         *reinterpret_cast<uint4*>(pl + sw128(row, ch + 1)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
       }
       tc_fence_before();
-      mbar_arrive(br.s_empty + sb);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(br.p_full + pb);
     }
     if (ok) ok = wait(br.o_done, 0);
-    // the row sum from both halves (every softmax thread passes here once)
+    // combine the halves (every softmax thread passes here once)
+    xm[half][row] = m;
     xl[half][row] = l;
     asm volatile("bar.sync 1, %0;" ::"n"(kSoft) : "memory");
-    l = xl[0][row];
-#pragma unroll
-    for (int i = 1; i < kSplit; ++i) l += xl[i][row];
-    // the TMEM loads below are .sync.aligned: decide warp-uniformly
+    const float m0 = xm[0][row], m1 = xm[1][row];
+    const float mx = fmaxf(m0, m1);  // finite: key 0 is in half 0
+    const float w0 = m0 == -INFINITY ? 0.f : __expf(m0 - mx);
+    const float w1 = m1 == -INFINITY ? 0.f : __expf(m1 - mx);
+    const float inv_l = 1.0f / (w0 * xl[0][row] + w1 * xl[1][row]);
     ok = __all_sync(0xffffffffu, ok) != 0;
     if (ok) {
       tc_fence_after();
       const int qr = q0 + row;
-      const float inv_l = 1.0f / l;
       bf16* out = reinterpret_cast<bf16*>(p.out) + ((size_t)row0 + qr) * p.inner + h * kDh;
 #pragma unroll
       for (int c = 0; c < kCols; c += 16) {
-        uint32_t rr[16];
-        tmem_ld16(tmem + lane_base + (uint32_t)(128 + c0 + c), rr);
+        uint32_t x0[16], x1[16];
+        tmem_ld16(tmem + lane_base + (uint32_t)(128 + c0 + c), x0);
+        tmem_ld16(tmem + lane_base + (uint32_t)(192 + c0 + c), x1);
         tmem_wait_ld();
         uint32_t w[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
-          w[q] = pack_bf16(__uint_as_float(rr[2 * q]) * inv_l, __uint_as_float(rr[2 * q + 1]) * inv_l);
+        for (int q = 0; q < 8; ++q) {
+          const float v0 = (w0 * __uint_as_float(x0[2 * q]) + w1 * __uint_as_float(x1[2 * q])) * inv_l;
+          const float v1 = (w0 * __uint_as_float(x0[2 * q + 1]) + w1 * __uint_as_float(x1[2 * q + 1])) * inv_l;
+          w[q] = pack_bf16(v0, v1);
+        }
         if (qr < S) {
           reinterpret_cast<uint4*>(out + c0 + c)[0] = make_uint4(w[0], w[1], w[2], w[3]);
           reinterpret_cast<uint4*>(out + c0 + c)[1] = make_uint4(w[4], w[5], w[6], w[7]);
