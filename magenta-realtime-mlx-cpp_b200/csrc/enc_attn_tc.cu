@@ -389,8 +389,10 @@ bool make_qkv_map(CUtensorMap* m, const void* base, int rows, int cols) {
 
 }  // namespace
 
-// per-shape variants: one wave (few CTAs) / many waves
-constexpr int kSplitFew = 2, kSplitMany = 2;  // 4 per row measured slower (1.51 vs 1.48 ms, one CFG pair)
+// per-shape variants: one wave (few CTAs) / many waves. Two softmax threads
+// per row, one per key half and O accumulator (four per row measured slower
+// in a two-pass version, 1.51 vs 1.48 ms at one CFG pair).
+constexpr int kSplitFew = 2, kSplitMany = 2;
 
 cudaError_t enc_attn_tc_set_smem_limits() {
   cudaError_t e = cudaFuncSetAttribute(enc_attn_tc_kernel<2, 2, kSplitFew>, cudaFuncAttributeMaxDynamicSharedMemorySize,
