@@ -215,3 +215,47 @@ def test_hybrid_bf16_teacher_forced_50_frames(mrtdf, oracle):
     assert e32.mean() <= 1.25 * floor.mean()
     assert e16.mean() <= 2.0 * floor.mean()
     assert e32.max() <= 1.25 * floor.max() + BF16_TOL
+
+
+def test_encoder_attention_wide_logits(mrtdf, oracle):
+    """Encoder layer 0 with weights N(0, 0.04^2): attention logits of std
+    ~12.5, so that the one-pass softmax raises its running maximum mid-row
+    (a key tile beats it by more than e^8 and O and the sum are rescaled in
+    TMEM) in ~72 % of the (row, head, query, key half) sequences, against
+    ~7 % at the N(0, 0.02^2) weights of the tests above (counted on the host
+    from the weights under the kernel's tile schedule).
+
+    Hidden values reach |x| ~ 14 here and the attention is peaky, so the
+    bf16 emulation itself leaves the fp32 result by more than 2e-2 in more
+    than half of the elements (max 0.27); the test requires the engine to be
+    no noisier than that: mean / max distance to fp32 within the floor's,
+    and its distance to the bf16 oracle (mean, max, share beyond 2e-2) below
+    the floor's. A wrong rescale (O kept at the old maximum's scale, a race
+    with the previous P V) is off by factors up to e^8 and misses all of
+    these."""
+    std = 0.04
+    cfg = mrtdf.preset("hybrid", mrtdf.DTYPE_BF16)
+    eng = mrtdf.Engine(cfg).load_random(0, stddev=std)
+    orc16 = oracle.Oracle.from_random(cfg.as_ints(), 0, stddev=std)
+    orc32 = oracle.Oracle.from_random(mrtdf.preset("hybrid", mrtdf.DTYPE_FP32).as_ints(), 0, stddev=std)
+    ids = random_ids(cfg, 2, cfg.max_encoder_length, seed=20)
+    st = mrtdf.Stream(eng, 1, True)
+    x = orc16.embed_pe(ids)
+    got = st.probe_encoder_layer(0, x).astype(np.float64)
+    want16 = orc16.encoder_layer(0, x).astype(np.float64)
+    want32 = orc32.encoder_layer(0, x).astype(np.float64)
+    e16, e32, floor = np.abs(got - want16), np.abs(got - want32), np.abs(want16 - want32)
+    stats = {"max16": e16.max(), "mean16": e16.mean(), "frac16": (e16 > BF16_TOL).mean(), "max32": e32.max(),
+             "mean32": e32.mean(), "floor_max": floor.max(), "floor_mean": floor.mean(),
+             "floor_frac": (floor > BF16_TOL).mean(), "max_abs_value": np.abs(want16).max()}
+    stats = {k: round(float(v), 6) for k, v in stats.items()}
+    print(f"hybrid encoder layer 0, weights N(0, {std}^2): {stats}")
+    assert stats["mean32"] <= 1.25 * stats["floor_mean"], stats
+    assert stats["max32"] <= 1.25 * stats["floor_max"] + BF16_TOL, stats
+    assert stats["mean16"] <= stats["floor_mean"], stats
+    assert stats["max16"] <= stats["floor_max"], stats
+    assert stats["frac16"] <= stats["floor_frac"], stats
+    st.close()
+    orc32.close()
+    orc16.close()
+    eng.close()
